@@ -1,0 +1,54 @@
+/* nabla_g1.h — C ABI of the B200 (sm_100a) batched Unitree G1 physics step (libnabla_g1.so).
+ *
+ * The drop-in boundary for the reference's "one control step of B independent G1 worlds" path. Every entry point is
+ * plain C: device pointers, sizes and a CUDA stream; no torch or XLA types. All arrays are row-major, contiguous,
+ * float32 (info: int32), on the device that is current when the function is called; the caller owns every buffer.
+ * Launches are asynchronous on `stream` (no host synchronisation), so the calls can be captured in a CUDA graph
+ * after nb_g1_upload has run once on the device. Each returns a cudaError_t value as int (0 = success).
+ *
+ * Shapes (mjlab G1): nq 36, nv 35, nu 29; B worlds. qpos (B,36): root position, root quaternion (w x y z), 29 hinge
+ * angles; qvel (B,35): root linear velocity (world), root angular velocity (local frame), 29 hinge rates; warm (B,35):
+ * the Newton warm start (the previous step's warm'); ctrl (B,29): PD setpoints; friction (B,): the 14 sole-floor
+ * pairs' sliding friction; com (B,3): the torso's COM offset in its frame (m).
+ */
+#ifndef NABLA_G1_H
+#define NABLA_G1_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef __CUDA_RUNTIME_API_H__
+typedef struct CUstream_st* cudaStream_t;
+#endif
+
+/* Sizes compiled into the library, in this order: nq, nv, nu, nbody, maxcon (64), nefc (192), tape words per world
+ * and substep, ABI version. Replaces the reference's `<pfx>_sizes(long long*)` (src/nablaengine/jax_ffi.py:255),
+ * which the bindings check against their own constants before the first call. */
+void nb_g1_sizes(long long out[8]);
+
+/* Scratch bytes nb_g1_forward needs for nw worlds (16-byte aligned, caller-allocated, e.g. a torch uint8 tensor or
+ * XLA's scratch allocator). Replaces `long long <pfx>_work_bytes(int nw)` (src/nablaengine/jax_ffi.py:265). */
+long long nb_g1_work_bytes(int nw);
+
+/* Per-device preparation: must run once on each device before its first step and before any stream capture (it
+ * may synchronise the stream once). consts may be NULL: the mjlab G1 constants are compiled into the library.
+ * Replaces `int <pfx>_upload(const float* consts, cudaStream_t)` (src/nablaengine/jax_ffi.py:214-227). */
+int nb_g1_upload(const float* consts, cudaStream_t stream);
+
+/* One control step of nw worlds: nsub substeps (1..32) of 5 ms, Newton capped at `iterations` (>= 0) per substep.
+ * Outputs qpos' (B,36), qvel' (B,35), warm' (B,35) (the last substep's constraint solution), info (B,4) int32 =
+ * [Newton iterations of the last substep, contacts the last substep's collision found (may exceed 64), constraint
+ * rows of the last substep (<= 192), bits 1 unsupported geom pair / 4 contacts beyond 64 dropped / 16 rows beyond
+ * 192 dropped, ORed over the substeps]. ocon (B,64,8) may be NULL: the last substep's contacts as (pair, dist,
+ * pos[3], normal[3]), pair -1 past the count. tape must be NULL (no tape is recorded by this entry). work:
+ * nb_g1_work_bytes(nw) bytes or NULL when that is 0. nw == 0 is a no-op.
+ * Replaces `int <pfx>_forward(cudaStream_t, int nw, ...)` (src/nablaengine/jax_ffi.py:266-279). */
+int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                  const float* ctrl, const float* friction, const float* com, int iterations, int nsub, float* qpos_out,
+                  float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NABLA_G1_H */

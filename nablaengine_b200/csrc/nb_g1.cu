@@ -1,0 +1,101 @@
+// libnabla_g1: the B200 (sm_100a) batched G1 control step behind the C ABI of include/nabla_g1.h.
+//
+// k_forward: one warp per world, WPB worlds per block, each world's whole control step (nsub substeps) in one
+// launch with its state resident in shared memory (nb_g1_step.cuh), so a step is a single kernel per call.
+#include "../../include/nabla_g1.h"
+#include "nb_g1_step.cuh"
+
+namespace nbg1 {
+
+constexpr int WPB = 2;  // worlds (warps) per block
+constexpr int TAPE_WORDS = 0;
+constexpr long long ABI_VERSION = 1;
+
+__global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __restrict__ qpos,
+                                                      const float* __restrict__ qvel, const float* __restrict__ warm,
+                                                      const float* __restrict__ ctrl, const float* __restrict__ fric,
+                                                      const float* __restrict__ com, int iterations, int nsub,
+                                                      float* __restrict__ oq, float* __restrict__ ov,
+                                                      float* __restrict__ ow, int* __restrict__ info,
+                                                      float* __restrict__ ocon) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x * WPB + warp;
+  if (w >= nw) return;  // whole warps leave; the block has no block-wide barrier
+  World& s = reinterpret_cast<World*>(smem)[warp];
+  const size_t w64 = (size_t)w;
+  for (int i = lane; i < NQ; i += 32) s.qpos[i] = qpos[w64 * NQ + i];
+  for (int i = lane; i < NV; i += 32) { s.qvel[i] = qvel[w64 * NV + i]; s.qacc[i] = warm[w64 * NV + i]; }
+  for (int i = lane; i < NU; i += 32) s.ctrl[i] = ctrl[w64 * NU + i];
+  if (lane < 3) s.com[lane] = com[w64 * 3 + lane];
+  if (lane == 0) { s.fric = fric[w]; s.unsup = 0; s.nit = 0; }
+  __syncwarp();
+  for (int k = 0; k < nsub; k++) substep(s, iterations, lane);
+  for (int i = lane; i < NQ; i += 32) oq[w64 * NQ + i] = s.qpos[i];
+  for (int i = lane; i < NV; i += 32) { ov[w64 * NV + i] = s.qvel[i]; ow[w64 * NV + i] = s.qacc[i]; }
+  if (lane == 0) {
+    info[w64 * 4] = s.nit;
+    info[w64 * 4 + 1] = s.ncon_raw;
+    info[w64 * 4 + 2] = s.nefc;
+    info[w64 * 4 + 3] = s.unsup;
+  }
+  if (ocon)
+    for (int c = lane; c < MAXCON; c += 32) {
+      float* o = ocon + (w64 * MAXCON + c) * 8;
+      const bool v = c < s.ncon;
+      o[0] = v ? (float)s.con_pair[c] : -1.f;
+      o[1] = v ? s.con_dist[c] : 0.f;
+      for (int k = 0; k < 3; k++) { o[2 + k] = v ? s.con_pos[c][k] : 0.f; o[5 + k] = v ? s.con_fr[c][k] : 0.f; }
+    }
+}
+
+constexpr size_t SMEM = sizeof(World) * WPB;
+static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
+
+}  // namespace nbg1
+
+using namespace nbg1;
+
+extern "C" {
+
+void nb_g1_sizes(long long out[8]) {
+  const long long v[8] = {NQ, NV, NU, NB, MAXCON, NEFC, TAPE_WORDS, ABI_VERSION};
+  for (int i = 0; i < 8; i++) out[i] = v[i];
+}
+
+long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : 0; }
+
+int nb_g1_upload(const float* consts, cudaStream_t stream) {
+  (void)consts;
+  (void)stream;
+  // the model is compiled in; the per-device work is the kernel's shared-memory opt-in (above 48 KB)
+  return (int)cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+}
+
+int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                  const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                  float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work) {
+  (void)work;
+  if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return (int)cudaErrorInvalidValue;
+  if (tape) return (int)cudaErrorNotSupported;
+  if (nw == 0) return 0;
+  if (!qpos || !qvel || !warm || !ctrl || !friction || !com || !qpos_out || !qvel_out || !warm_out || !info)
+    return (int)cudaErrorInvalidValue;
+  const int blocks = (nw + WPB - 1) / WPB;
+  k_forward<<<blocks, WPB * 32, SMEM, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
+                                                qvel_out, warm_out, info, ocon);
+  return (int)cudaGetLastError();
+}
+
+#ifdef NB_PROFILE
+// profile builds only: read and clear the phase counters (not part of the product ABI)
+int nb_g1_profile_read(unsigned long long* out, int n) {
+  unsigned long long h[NPROF] = {};
+  cudaError_t e = cudaMemcpyFromSymbol(h, g_prof, sizeof(h));
+  if (e != cudaSuccess) return (int)e;
+  for (int i = 0; i < n && i < NPROF; i++) out[i] = h[i];
+  unsigned long long z[NPROF] = {};
+  return (int)cudaMemcpyToSymbol(g_prof, z, sizeof(z));
+}
+#endif
+}  // extern "C"

@@ -1,0 +1,1192 @@
+// Device code of one G1 substep, one warp per world, the world's state in shared memory (struct World).
+//
+// Algorithm (reference OamIcs/NablaEngine, src/nablaengine/g1_engine/): forward kinematics, Newton-Euler bias forces
+// and the joint-space mass matrix (source.py:181-334), PD actuation clamped to the joint force range (step.py:
+// 1762-1778), collision of the 502 explicit pairs with MuJoCo Warp's sphere / capsule / plane primitives (step.py:
+// 436-556, 1043-1145), hinge-limit and pyramidal contact rows with refsafe impedance (step.py:1881-1957, 1147-1188),
+// the primal Newton solver with an exact line search (step.py:1969-2137) and implicitfast integration (step.py:
+// 2153-2182). The layout and the parallel decomposition are this library's own:
+//  * lanes own bodies (tree sweeps one depth level at a time), dofs (mass-matrix rows, actuation, J' f), pairs
+//    (broad phase), candidate pairs (narrow phase), contacts and constraint rows;
+//  * every dof's motion vector about the root origin O is kept (dw = angular, dv = velocity of the point O), and a
+//    contact keeps its frame rows and their moments (pos - O) x row: a contact row's Jacobian entry is then
+//    frame . dv + moment . dw, so no per-contact Jacobian is stored; J v for all contacts comes from the bodies'
+//    spatial velocities at O (one pass over each body's ancestor dofs), and J' f from the contacts' wrenches at O;
+//  * contacts are numbered deterministically: pair order, then the pair's contact slot (a ballot prefix sum over the
+//    candidates), so results are bitwise reproducible run to run.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define NB_REAL float
+#define NB_MODEL_CONST static __device__ const
+#include "g1_model_data.h"
+
+namespace nbg1 {
+
+constexpr int NQ = G1_NQ, NV = G1_NV, NU = G1_NU, NB = G1_NBODY, NG = G1_NGEOM, NP = G1_NPAIR;
+constexpr int MAXCON = 64, NEFC = 192, KDOF = 16, MAXD = G1_MAXDEPTH;
+constexpr int NTRI = NV * (NV + 1) / 2;
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int ROWS_PER_LANE = (NEFC + 31) / 32;
+__host__ __device__ constexpr int TRI(int i, int j) { return i * (i + 1) / 2 + j; }  // packed lower triangle, j <= i
+
+enum : int { UNSUPPORTED_PAIR = 1, CONTACT_OVERFLOW = 4, ROW_OVERFLOW = 16 };
+enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
+
+// Phase profile (build with -DNB_PROFILE; the product build has none of it): lane 0 of every world adds the clock64
+// cycles since the previous mark to g_prof[phase]; counters from phase 16 on count events.
+#ifdef NB_PROFILE
+constexpr int NPROF = 24;
+__device__ unsigned long long g_prof[NPROF];
+#define PROF_START(s) do { __syncwarp(); if (lane == 0) (s).prof_t = clock64(); } while (0)
+#define PROF(s, k) do { __syncwarp(); if (lane == 0) { long long t_ = clock64(); \
+    atomicAdd(&g_prof[k], (unsigned long long)(t_ - (s).prof_t)); (s).prof_t = t_; } __syncwarp(); } while (0)
+#define PROF_COUNT(k, n) do { if (lane == 0) atomicAdd(&g_prof[k], (unsigned long long)(n)); } while (0)
+#else
+#define PROF_START(s) do { } while (0)
+#define PROF(s, k) do { } while (0)
+#define PROF_COUNT(k, n) do { } while (0)
+#endif
+
+struct __align__(16) World {
+  unsigned long long con_m1[MAXCON], con_m2[MAXCON];  // dofs that move only body 1 / only body 2 of the contact
+  float qpos[NQ], qvel[NV], qacc[NV], ctrl[NU], com[3], fric;
+  float Q[NB][4], X[NB][3];            // body poses
+  float dw[NV][3], dv[NV][3];          // dof motion about O: angular axis, velocity of the point O
+  float BV[NB][6];                     // body spatial motion at O (angular, linear) for a generalised vector
+  float M[NTRI], L[NTRI];              // mass matrix (with armature), factor scratch
+  float qsm[NV], qacc0[NV], Ma[NV], grad[NV], p[NV], Mp[NV], tmp[NV], dinv[NV + 1];
+  union {
+    struct { float om[NB][3], vo[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
+    struct { float gx[NG][3], gq[NG][4]; unsigned short cand[NP + 2]; } col;                 // collision phase
+    struct { float K[21], P[KDOF][6]; unsigned char dof[KDOF]; } hs;                        // Hessian assembly
+  } u;
+  unsigned long long grp_mask[MAXCON];  // contacts of group g (same body pair) as bits
+  float con_C[MAXCON][5];               // Hessian coefficients of a contact's rows: nn, n1, 11, n2, 22
+  short lim_row[NV];                    // the dof's limit row, or -1
+  unsigned char con_grp[MAXCON], grp_lead[MAXCON];
+  int ngroup, pad2_;
+  int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
+  int con_pair[MAXCON];
+  unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
+  float con_dist[MAXCON], con_mu[MAXCON];
+  float con_fr[MAXCON][9];             // frame rows: normal, tangent 1, tangent 2
+  float con_cv[MAXCON][9];             // (pos - O) x frame row
+  float con_pos[MAXCON][3];
+  union { float jd[MAXCON][3]; float wr[MAXCON][6]; } cs;  // J_d v per frame row / the contact wrench at O
+  float efc_D[NEFC], efc_aref[NEFC], efc_jar[NEFC], efc_jv[NEFC];
+  short efc_a[NEFC];                   // dof (limit row) or contact
+  signed char efc_b[NEFC];             // limit sign, or the contact row t (n + mu t1, n - mu t1, n + mu t2, ...)
+  unsigned char efc_kind[NEFC];
+#ifdef NB_PROFILE
+  long long prof_t;
+#endif
+};
+
+// ---- small vector helpers --------------------------------------------------------------------------------------
+__device__ __forceinline__ void qmul(const float* a, const float* b, float* o) {
+  float w = a[0] * b[0] - a[1] * b[1] - a[2] * b[2] - a[3] * b[3];
+  float x = a[0] * b[1] + a[1] * b[0] + a[2] * b[3] - a[3] * b[2];
+  float y = a[0] * b[2] - a[1] * b[3] + a[2] * b[0] + a[3] * b[1];
+  float z = a[0] * b[3] + a[1] * b[2] - a[2] * b[1] + a[3] * b[0];
+  o[0] = w; o[1] = x; o[2] = y; o[3] = z;
+}
+__device__ __forceinline__ void cross(const float* a, const float* b, float* o) {
+  float x = a[1] * b[2] - a[2] * b[1], y = a[2] * b[0] - a[0] * b[2], z = a[0] * b[1] - a[1] * b[0];
+  o[0] = x; o[1] = y; o[2] = z;
+}
+__device__ __forceinline__ float dot3(const float* a, const float* b) { return a[0] * b[0] + a[1] * b[1] + a[2] * b[2]; }
+__device__ __forceinline__ void qrot(const float* q, const float* v, float* o) {  // o = q v q^-1
+  float t[3], u[3];
+  const float qv[3] = {q[1], q[2], q[3]};
+  cross(qv, v, t);
+  for (int k = 0; k < 3; k++) t[k] *= 2.f;
+  cross(qv, t, u);
+  for (int k = 0; k < 3; k++) o[k] = v[k] + q[0] * t[k] + u[k];
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+  return v;
+}
+__device__ __forceinline__ float ld(const float* p) { return __ldg(p); }
+__device__ __forceinline__ int ldi(const int* p) { return __ldg(p); }
+
+// M(i, j) of a symmetric matrix stored as its packed lower triangle
+__device__ __forceinline__ float sym(const float* A, int i, int j) { return j <= i ? A[TRI(i, j)] : A[TRI(j, i)]; }
+
+// ---- smooth dynamics ---------------------------------------------------------------------------------------------
+// Forward kinematics with velocities and the velocity-product accelerations (qacc = 0; gravity enters as the
+// base acceleration -g), one depth level at a time (lane = body).
+__device__ void kinematics(World& s, int lane) {
+  const int b = lane;
+  const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
+  if (lane == 0) {
+    s.Q[0][0] = 1.f; s.Q[0][1] = s.Q[0][2] = s.Q[0][3] = 0.f;
+    for (int k = 0; k < 3; k++) { s.X[0][k] = 0.f; }
+  }
+  for (int L = 1; L <= MAXD; L++) {
+    if (depth == L) {
+      if (b == 1) {
+        float q[4] = {s.qpos[3], s.qpos[4], s.qpos[5], s.qpos[6]};
+        float n = sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
+        for (int k = 0; k < 4; k++) s.Q[1][k] = q[k] / n;
+        float wl[3] = {s.qvel[3], s.qvel[4], s.qvel[5]}, om[3];
+        qrot(s.Q[1], wl, om);
+        for (int k = 0; k < 3; k++) {
+          s.X[1][k] = s.qpos[k];
+          s.u.sm.om[1][k] = om[k];
+          s.u.sm.vo[1][k] = s.qvel[k];
+          s.u.sm.al[1][k] = 0.f;
+          s.u.sm.ao[1][k] = 0.f;
+        }
+        s.u.sm.ao[1][2] = -G1_GRAVITY_Z;
+      } else {
+        const int p = ldi(g1_body_parent + b);
+        float Qp[4], Xp[3], omp[3], vop[3], alp[3], aop[3];
+        for (int k = 0; k < 4; k++) Qp[k] = s.Q[p][k];
+        for (int k = 0; k < 3; k++) {
+          Xp[k] = s.X[p][k]; omp[k] = s.u.sm.om[p][k]; vop[k] = s.u.sm.vo[p][k];
+          alp[k] = s.u.sm.al[p][k]; aop[k] = s.u.sm.ao[p][k];
+        }
+        const float bq[4] = {ld(g1_body_quat + 4 * b), ld(g1_body_quat + 4 * b + 1), ld(g1_body_quat + 4 * b + 2),
+                             ld(g1_body_quat + 4 * b + 3)};
+        const float bp[3] = {ld(g1_body_pos + 3 * b), ld(g1_body_pos + 3 * b + 1), ld(g1_body_pos + 3 * b + 2)};
+        const float ax[3] = {ld(g1_body_axis + 3 * b), ld(g1_body_axis + 3 * b + 1), ld(g1_body_axis + 3 * b + 2)};
+        const int d = ldi(g1_body_dofadr + b);
+        const float ang = s.qpos[d + 1], qd = s.qvel[d];
+        float q0[4], sn, cs, t[3], X[3], Q[4];
+        qmul(Qp, bq, q0);
+        qrot(Qp, bp, t);
+        for (int k = 0; k < 3; k++) X[k] = Xp[k] + t[k];
+        sincosf(0.5f * ang, &sn, &cs);
+        const float ha[4] = {cs, sn * ax[0], sn * ax[1], sn * ax[2]};
+        qmul(q0, ha, Q);
+        float aw[3], r[3], wd[3], u1[3], u2[3], u3[3];
+        qrot(Q, ax, aw);
+        for (int k = 0; k < 3; k++) { r[k] = X[k] - Xp[k]; wd[k] = aw[k] * qd; }
+        cross(omp, r, u1);
+        cross(omp, wd, u2);
+        cross(alp, r, u3);
+        float wr_[3];
+        cross(omp, u1, wr_);
+        for (int k = 0; k < 4; k++) s.Q[b][k] = Q[k];
+        for (int k = 0; k < 3; k++) {
+          s.X[b][k] = X[k];
+          s.u.sm.om[b][k] = omp[k] + wd[k];
+          s.u.sm.vo[b][k] = vop[k] + u1[k];
+          s.u.sm.al[b][k] = alp[k] + u2[k];
+          s.u.sm.ao[b][k] = aop[k] + u3[k] + wr_[k];
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// the dofs' motion vectors about O = the root origin (lane = dof)
+__device__ void dof_motion(World& s, int lane) {
+  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  for (int i = lane; i < NV; i += 32) {
+    float w[3] = {0.f, 0.f, 0.f}, v[3] = {0.f, 0.f, 0.f};
+    if (i < 3) {
+      v[i] = 1.f;
+    } else if (i < 6) {
+      float e[3] = {0.f, 0.f, 0.f};
+      e[i - 3] = 1.f;
+      qrot(s.Q[1], e, w);
+    } else {
+      const int b = ldi(g1_dof_body + i);
+      const float ax[3] = {ld(g1_body_axis + 3 * b), ld(g1_body_axis + 3 * b + 1), ld(g1_body_axis + 3 * b + 2)};
+      qrot(s.Q[b], ax, w);
+      const float r[3] = {O[0] - s.X[b][0], O[1] - s.X[b][1], O[2] - s.X[b][2]};
+      cross(w, r, v);
+    }
+    for (int k = 0; k < 3; k++) { s.dw[i][k] = w[k]; s.dv[i][k] = v[k]; }
+  }
+  __syncwarp();
+}
+
+// per body: the Newton-Euler wrench at O and the spatial inertia about O (lane = body), then both summed over
+// subtrees (leaves first)
+__device__ void body_terms(World& s, int lane) {
+  const int b = lane;
+  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  if (b >= 1 && b < NB) {
+    float ip[3] = {ld(g1_body_ipos + 3 * b), ld(g1_body_ipos + 3 * b + 1), ld(g1_body_ipos + 3 * b + 2)};
+    if (b == G1_TORSO)
+      for (int k = 0; k < 3; k++) ip[k] += s.com[k];
+    float c[3], Q[4], om[3], al[3], ao[3];
+    for (int k = 0; k < 4; k++) Q[k] = s.Q[b][k];
+    for (int k = 0; k < 3; k++) { om[k] = s.u.sm.om[b][k]; al[k] = s.u.sm.al[b][k]; ao[k] = s.u.sm.ao[b][k]; }
+    qrot(Q, ip, c);
+    const float iq[4] = {ld(g1_body_iquat + 4 * b), ld(g1_body_iquat + 4 * b + 1), ld(g1_body_iquat + 4 * b + 2),
+                         ld(g1_body_iquat + 4 * b + 3)};
+    float qi[4], R[3][3];
+    qmul(Q, iq, qi);
+    for (int k = 0; k < 3; k++) {
+      float e[3] = {0.f, 0.f, 0.f}, col[3];
+      e[k] = 1.f;
+      qrot(qi, e, col);
+      for (int r = 0; r < 3; r++) R[r][k] = col[r];
+    }
+    const float In[3] = {ld(g1_body_inertia + 3 * b), ld(g1_body_inertia + 3 * b + 1), ld(g1_body_inertia + 3 * b + 2)};
+    float I[3][3];
+    for (int r = 0; r < 3; r++)
+      for (int q = r; q < 3; q++) {
+        float v = R[r][0] * In[0] * R[q][0] + R[r][1] * In[1] * R[q][1] + R[r][2] * In[2] * R[q][2];
+        I[r][q] = v; I[q][r] = v;
+      }
+    const float m = ld(g1_body_mass + b);
+    // COM acceleration (qacc = 0) and the inertial wrench about the COM
+    float u1[3], u2[3], u3[3], ac[3], F[3], Iom[3], Ial[3], N[3];
+    cross(al, c, u1);
+    cross(om, c, u2);
+    cross(om, u2, u3);
+    for (int k = 0; k < 3; k++) { ac[k] = ao[k] + u1[k] + u3[k]; F[k] = m * ac[k]; }
+    for (int r = 0; r < 3; r++) {
+      Iom[r] = I[r][0] * om[0] + I[r][1] * om[1] + I[r][2] * om[2];
+      Ial[r] = I[r][0] * al[0] + I[r][1] * al[1] + I[r][2] * al[2];
+    }
+    cross(om, Iom, u1);
+    // moment arm from O to the COM
+    float cO[3], mo[3];
+    for (int k = 0; k < 3; k++) cO[k] = s.X[b][k] + c[k] - O[k];
+    cross(cO, F, mo);
+    for (int k = 0; k < 3; k++) { N[k] = Ial[k] + u1[k] + mo[k]; }
+    for (int k = 0; k < 3; k++) { s.u.sm.wr[b][k] = N[k]; s.u.sm.wr[b][3 + k] = F[k]; }
+    // spatial inertia about O: rotational inertia about O (xx yy zz xy xz yz), h = m cO, m
+    const float cc = dot3(cO, cO);
+    float* J = s.u.sm.I[b];
+    J[0] = I[0][0] + m * (cc - cO[0] * cO[0]);
+    J[1] = I[1][1] + m * (cc - cO[1] * cO[1]);
+    J[2] = I[2][2] + m * (cc - cO[2] * cO[2]);
+    J[3] = I[0][1] - m * cO[0] * cO[1];
+    J[4] = I[0][2] - m * cO[0] * cO[2];
+    J[5] = I[1][2] - m * cO[1] * cO[2];
+    J[6] = m * cO[0]; J[7] = m * cO[1]; J[8] = m * cO[2]; J[9] = m;
+  }
+  __syncwarp();
+  const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
+  const int nch = b < NB ? ldi(g1_body_nchild + b) : 0;
+  for (int L = MAXD - 1; L >= 1; L--) {
+    if (depth == L && nch > 0) {
+      float wr[6], I[10];
+      for (int k = 0; k < 6; k++) wr[k] = s.u.sm.wr[b][k];
+      for (int k = 0; k < 10; k++) I[k] = s.u.sm.I[b][k];
+      for (int c = 0; c < nch; c++) {
+        const int ch = ldi(g1_body_child + 3 * b + c);
+        for (int k = 0; k < 6; k++) wr[k] += s.u.sm.wr[ch][k];
+        for (int k = 0; k < 10; k++) I[k] += s.u.sm.I[ch][k];
+      }
+      for (int k = 0; k < 6; k++) s.u.sm.wr[b][k] = wr[k];
+      for (int k = 0; k < 10; k++) s.u.sm.I[b][k] = I[k];
+    }
+    __syncwarp();
+  }
+}
+
+// (n, f) = I (w, v) for a packed spatial inertia about O: n = I_O w + h x v, f = m v - h x w
+__device__ __forceinline__ void apply_inertia(const float* J, const float* w, const float* v, float* n, float* f) {
+  float hv[3], hw[3];
+  cross(J + 6, v, hv);
+  cross(J + 6, w, hw);
+  n[0] = J[0] * w[0] + J[3] * w[1] + J[4] * w[2] + hv[0];
+  n[1] = J[3] * w[0] + J[1] * w[1] + J[5] * w[2] + hv[1];
+  n[2] = J[4] * w[0] + J[5] * w[1] + J[2] * w[2] + hv[2];
+  for (int k = 0; k < 3; k++) f[k] = J[9] * v[k] - hw[k];
+}
+
+// mass matrix rows (lane = dof: entries with its ancestor dofs) and qfrc_smooth = clamped actuator force - bias
+__device__ void mass_and_force(World& s, int lane) {
+  for (int e = lane; e < NTRI; e += 32) s.M[e] = 0.f;
+  __syncwarp();
+  for (int i = lane; i < NV; i += 32) {
+    const int b = ldi(g1_dof_body + i);
+    const float w[3] = {s.dw[i][0], s.dw[i][1], s.dw[i][2]}, v[3] = {s.dv[i][0], s.dv[i][1], s.dv[i][2]};
+    float J[10], n[3], f[3];
+    for (int k = 0; k < 10; k++) J[k] = s.u.sm.I[b][k];
+    apply_inertia(J, w, v, n, f);
+    // ancestor dofs j < i (the dof's own body first for the free joint's dofs) and the diagonal
+    unsigned long long anc = g1_body_dofmask[b] & ((1ull << i) - 1ull);
+    while (anc) {
+      const int j = __ffsll((long long)anc) - 1;
+      anc &= anc - 1ull;
+      s.M[TRI(i, j)] = dot3(s.dw[j], n) + dot3(s.dv[j], f);
+    }
+    s.M[TRI(i, i)] = dot3(w, n) + dot3(v, f) + ld(g1_dof_armature + i);
+    // bias: the subtree wrench of the dof's body projected on its motion
+    const float bias = dot3(w, s.u.sm.wr[b]) + dot3(v, s.u.sm.wr[b] + 3);
+    float act = 0.f;
+    if (i >= 6) {
+      act = ld(g1_dof_kp + i) * (s.ctrl[i - 6] - s.qpos[i + 1]) - ld(g1_dof_kv + i) * s.qvel[i];
+      const float lim = ld(g1_dof_frclim + i);
+      act = fminf(fmaxf(act, -lim), lim);
+    }
+    s.qsm[i] = act - bias;
+  }
+  __syncwarp();
+}
+
+// ---- dense Cholesky and solves --------------------------------------------------------------------------------
+// chol_factor: A = L L' (then chol_solve: b <- A^-1 b). The factorisation runs in registers: lane l holds row l (a0) and, for
+// l < NV - 32, row l + 32 (a1), all NV entries of the symmetric row (the update of the entries above the diagonal
+// is the symmetric Schur complement, never read as L); step k scales column k by 1 / sqrt(pivot) (rsqrt refined by
+// one Newton step) and broadcasts L(j, k) from row j's lane with one shuffle per j. Every index is a compile-time
+// constant after unrolling, so nothing spills to local memory. L (packed lower, true diagonal) and 1 / diag(L) are
+// written to shared memory for the triangular solves and for later re-solves (chol_solve). A is read completely
+// before L is written, so L may alias A.
+__device__ __forceinline__ float rsqrt_nr(float x) {
+  float r = rsqrtf(x);
+  return r * (1.5f - 0.5f * x * r * r);
+}
+
+__device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, int lane) {
+  static_assert(NV > 32 && NV - 32 == 3, "rows 0..31 in lanes, a 3-row tail");
+  // lane l: row l of the leading 32 x 32 block (all 32 entries), the tail entries T[t] = A(32 + t, l) (column l of
+  // the 3 x 32 tail block), and the 3 x 3 trailing block C (the same on every lane)
+  float a[32], T[3], C[6];
+#pragma unroll
+  for (int j = 0; j < 32; j++) a[j] = j <= lane ? A[TRI(lane, j)] : A[TRI(j, lane)];
+#pragma unroll
+  for (int t = 0; t < 3; t++) T[t] = A[TRI(32 + t, lane)];
+  C[0] = A[TRI(32, 32)]; C[1] = A[TRI(33, 32)]; C[2] = A[TRI(33, 33)];
+  C[3] = A[TRI(34, 32)]; C[4] = A[TRI(34, 33)]; C[5] = A[TRI(34, 34)];
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 32; k++) {
+    const float dkk = fmaxf(__shfl_sync(FULL, a[k], k), 1e-30f);
+    const float inv = rsqrt_nr(dkk);
+    if (lane == 0) dinv[k] = inv;
+    if (lane > k) a[k] *= inv; else if (lane == k) a[k] = dkk * inv;
+    if (lane == k) { T[0] *= inv; T[1] *= inv; T[2] *= inv; }  // tail column k: L(32 + t, k)
+    const float t0 = __shfl_sync(FULL, T[0], k), t1 = __shfl_sync(FULL, T[1], k), t2 = __shfl_sync(FULL, T[2], k);
+#pragma unroll
+    for (int j = k + 1; j < 32; j++) a[j] -= a[k] * __shfl_sync(FULL, a[k], j);
+    if (lane > k) { T[0] -= t0 * a[k]; T[1] -= t1 * a[k]; T[2] -= t2 * a[k]; }
+    C[0] -= t0 * t0; C[1] -= t1 * t0; C[2] -= t1 * t1; C[3] -= t2 * t0; C[4] -= t2 * t1; C[5] -= t2 * t2;
+  }
+  // the 3 x 3 tail factor (every lane, redundantly)
+  const float i0 = rsqrt_nr(fmaxf(C[0], 1e-30f));
+  const float l00 = C[0] * i0, l10 = C[1] * i0, l20 = C[3] * i0;
+  const float c11 = C[2] - l10 * l10, i1 = rsqrt_nr(fmaxf(c11, 1e-30f)), l11 = c11 * i1;
+  const float l21 = (C[4] - l20 * l10) * i1;
+  const float c22 = C[5] - l20 * l20 - l21 * l21, i2 = rsqrt_nr(fmaxf(c22, 1e-30f)), l22 = c22 * i2;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    if (j <= lane) L[TRI(lane, j)] = a[j];
+#pragma unroll
+  for (int t = 0; t < 3; t++) L[TRI(32 + t, lane)] = T[t];
+  if (lane == 0) {
+    L[TRI(32, 32)] = l00; L[TRI(33, 32)] = l10; L[TRI(33, 33)] = l11;
+    L[TRI(34, 32)] = l20; L[TRI(34, 33)] = l21; L[TRI(34, 34)] = l22;
+    dinv[32] = i0; dinv[33] = i1; dinv[34] = i2;
+  }
+  __syncwarp();
+}
+
+// b <- (L L')^-1 b with the factor L and dinv = 1 / diag(L) in shared memory; lane l keeps entries l, l + 32 in
+// registers; the forward pass reads column k (L(lane, k): distinct banks for the 32 lanes), the backward pass row k
+__device__ void chol_solve(const float* L, const float* dinv, float* b, int lane) {
+  float y0 = b[lane], y1 = lane + 32 < NV ? b[lane + 32] : 0.f;
+  __syncwarp();
+#pragma unroll 5
+  for (int k = 0; k < NV; k++) {
+    const float yk = __shfl_sync(FULL, k < 32 ? y0 : y1, k & 31) * dinv[k];
+    if (lane == k) y0 = yk;
+    else if (lane > k) y0 -= L[TRI(lane, k)] * yk;
+    if (lane + 32 == k) y1 = yk;
+    else if (lane + 32 > k && lane + 32 < NV) y1 -= L[TRI(lane + 32, k)] * yk;
+  }
+#pragma unroll 5
+  for (int k = NV - 1; k >= 0; k--) {
+    const float xk = __shfl_sync(FULL, k < 32 ? y0 : y1, k & 31) * dinv[k];
+    if (lane == k) y0 = xk;
+    else if (lane < k) y0 -= L[TRI(k, lane)] * xk;
+    if (lane + 32 == k) y1 = xk;
+    else if (lane + 32 < k) y1 -= L[TRI(k, lane + 32)] * xk;
+  }
+  b[lane] = y0;
+  if (lane + 32 < NV) b[lane + 32] = y1;
+  __syncwarp();
+}
+
+// out = A v (A symmetric, packed)
+__device__ void matvec(const float* A, const float* v, float* out, int lane) {
+  for (int i = lane; i < NV; i += 32) {
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; j += 2) {
+      a0 += sym(A, i, j) * v[j];
+      if (j + 1 < NV) a1 += sym(A, i, j + 1) * v[j + 1];
+    }
+    out[i] = a0 + a1;
+  }
+  __syncwarp();
+}
+
+// ---- collision ---------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void zaxis(const float* q, float* a) {
+  const float ez[3] = {0.f, 0.f, 1.f};
+  qrot(q, ez, a);
+}
+__device__ __forceinline__ void make_frame(const float* n, float* fr) {  // MuJoCo's make_frame: rows n, b, n x b
+  float b[3] = {0.f, 0.f, 0.f};
+  if (n[1] > -0.5f && n[1] < 0.5f) b[1] = 1.f; else b[2] = 1.f;
+  const float d = dot3(n, b);
+  for (int k = 0; k < 3; k++) b[k] -= n[k] * d;
+  const float bn = sqrtf(dot3(b, b));
+  if (bn > 0.f)
+    for (int k = 0; k < 3; k++) b[k] /= bn;
+  float c[3];
+  cross(n, b, c);
+  for (int k = 0; k < 3; k++) { fr[k] = n[k]; fr[3 + k] = b[k]; fr[6 + k] = c[k]; }
+}
+__device__ __forceinline__ void sphere_sphere(const float* p1, float r1, const float* p2, float r2, float* dist,
+                                              float* pos, float* n) {
+  const float dir[3] = {p2[0] - p1[0], p2[1] - p1[1], p2[2] - p1[2]};
+  const float d = sqrtf(dot3(dir, dir));
+  if (d == 0.f) { n[0] = 1.f; n[1] = 0.f; n[2] = 0.f; }
+  else for (int k = 0; k < 3; k++) n[k] = dir[k] / d;
+  *dist = d - (r1 + r2);
+  const float hp = r1 + 0.5f * *dist;
+  for (int k = 0; k < 3; k++) pos[k] = p1[k] + n[k] * hp;
+}
+
+// The bounding test of pair pr at the current geom poses (no contact at zero margin when it fails)
+__device__ __forceinline__ bool bounding(const World& s, int pr) {
+  const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
+  const float dif[3] = {s.u.col.gx[g2][0] - s.u.col.gx[g1][0], s.u.col.gx[g2][1] - s.u.col.gx[g1][1],
+                        s.u.col.gx[g2][2] - s.u.col.gx[g1][2]};
+  if (ldi(g1_geom_type + g1) == 0) {
+    float n[3];
+    zaxis(s.u.col.gq[g1], n);
+    return dot3(dif, n) <= ld(g1_geom_rbound + g2);
+  }
+  const float rb = ld(g1_geom_rbound + g1) + ld(g1_geom_rbound + g2);
+  return dot3(dif, dif) <= rb * rb;
+}
+
+// Narrow phase of candidate pair pr: returns the number of contacts (0..2, dist < 0) and, when write is set,
+// stores them at contact slots base, base + 1 (those below MAXCON). MuJoCo Warp's primitives at margin 0.
+__device__ int collide(World& s, int pr, bool write, int base, int* unsup) {
+  const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
+  const int t1 = ldi(g1_geom_type + g1), t2 = ldi(g1_geom_type + g2);
+  float p1[3], p2[3];
+  for (int k = 0; k < 3; k++) { p1[k] = s.u.col.gx[g1][k]; p2[k] = s.u.col.gx[g2][k]; }
+  const float r1 = ld(g1_geom_size + 3 * g1), r2 = ld(g1_geom_size + 3 * g2);
+  int n = 0;
+  auto emit = [&](int slot, float dist, const float* pos, const float* fr) {
+    const int c = base + n;
+    n++;
+    if (!write || c >= MAXCON) return;
+    s.con_pair[c] = pr;
+    s.con_slot[c] = (unsigned char)slot;
+    s.con_dist[c] = dist;
+    for (int k = 0; k < 3; k++) s.con_pos[c][k] = pos[k];
+    for (int k = 0; k < 9; k++) s.con_fr[c][k] = fr[k];
+  };
+  if (t1 == 0) {  // plane (the floor) against a sphere or a capsule
+    float nrm[3];
+    zaxis(s.u.col.gq[g1], nrm);
+    const float poff = dot3(p1, nrm);
+    if (t2 == 2) {
+      const float dist = dot3(p2, nrm) - poff - r2;
+      if (dist < 0.f) {
+        float pos[3], fr[9];
+        const float hp = r2 + 0.5f * dist;
+        for (int k = 0; k < 3; k++) pos[k] = p2[k] - nrm[k] * hp;
+        make_frame(nrm, fr);
+        emit(0, dist, pos, fr);
+      }
+    } else if (t2 == 3) {
+      const float hl = ld(g1_geom_size + 3 * g2 + 1);
+      float ax[3], fr[9];
+      zaxis(s.u.col.gq[g2], ax);
+      float d[2], ce[2][3];
+      for (int e = 0; e < 2; e++) {
+        for (int k = 0; k < 3; k++) ce[e][k] = e == 0 ? p2[k] + hl * ax[k] : p2[k] - hl * ax[k];
+        d[e] = dot3(ce[e], nrm) - poff - r2;
+      }
+      if (d[0] < 0.f || d[1] < 0.f) {
+        // frame: the capsule axis projected on the plane when that projection is long enough
+        const float na = dot3(nrm, ax);
+        float b[3] = {ax[0] - nrm[0] * na, ax[1] - nrm[1] * na, ax[2] - nrm[2] * na};
+        const float bn = sqrtf(dot3(b, b));
+        if (bn < 0.5f) make_frame(nrm, fr);
+        else {
+          for (int k = 0; k < 3; k++) b[k] /= bn;
+          float c[3];
+          cross(nrm, b, c);
+          for (int k = 0; k < 3; k++) { fr[k] = nrm[k]; fr[3 + k] = b[k]; fr[6 + k] = c[k]; }
+        }
+        for (int e = 0; e < 2; e++)
+          if (d[e] < 0.f) {
+            float pos[3];
+            const float hp = r2 + 0.5f * d[e];
+            for (int k = 0; k < 3; k++) pos[k] = ce[e][k] - nrm[k] * hp;
+            emit(e, d[e], pos, fr);
+          }
+      }
+    } else {
+      *unsup |= UNSUPPORTED_PAIR;
+    }
+    return n;
+  }
+  if (t1 == 2 && t2 == 2) {  // sphere-sphere
+    float dist, pos[3], nn[3], fr[9];
+    sphere_sphere(p1, r1, p2, r2, &dist, pos, nn);
+    if (dist < 0.f) { make_frame(nn, fr); emit(0, dist, pos, fr); }
+    return n;
+  }
+  if (t1 == 2 && t2 == 3) {  // sphere-capsule: the regularised closest point of the segment
+    const float hl = ld(g1_geom_size + 3 * g2 + 1);
+    float ax[3], a[3], ab[3], ap[3], pt[3];
+    zaxis(s.u.col.gq[g2], ax);
+    for (int k = 0; k < 3; k++) { a[k] = p2[k] - ax[k] * hl; ab[k] = 2.f * hl * ax[k]; ap[k] = p1[k] - a[k]; }
+    const float gam = dot3(ab, ab) + 1e-6f;
+    const float t = fminf(fmaxf(dot3(ap, ab) / gam, 0.f), 1.f);
+    for (int k = 0; k < 3; k++) pt[k] = a[k] + t * ab[k];
+    float dist, pos[3], nn[3], fr[9];
+    sphere_sphere(p1, r1, pt, r2, &dist, pos, nn);
+    if (dist < 0.f) { make_frame(nn, fr); emit(0, dist, pos, fr); }
+    return n;
+  }
+  if (t1 == 3 && t2 == 3) {  // capsule-capsule: closest points of the segments (clamp cascade)
+    const float hl1 = ld(g1_geom_size + 3 * g1 + 1), hl2 = ld(g1_geom_size + 3 * g2 + 1);
+    float a1[3], a2[3], df[3];
+    zaxis(s.u.col.gq[g1], a1);
+    zaxis(s.u.col.gq[g2], a2);
+    for (int k = 0; k < 3; k++) { a1[k] *= hl1; a2[k] *= hl2; df[k] = p1[k] - p2[k]; }
+    const float ma = dot3(a1, a1), mb = -dot3(a1, a2), mc = dot3(a2, a2), u = -dot3(a1, df), v = dot3(a2, df);
+    const float det = ma * mc - mb * mb;
+    auto at = [&](float x1, float x2, float* dist, float* pos, float* nn) {
+      const float v1[3] = {p1[0] + a1[0] * x1, p1[1] + a1[1] * x1, p1[2] + a1[2] * x1};
+      const float v2[3] = {p2[0] + a2[0] * x2, p2[1] + a2[1] * x2, p2[2] + a2[2] * x2};
+      sphere_sphere(v1, r1, v2, r2, dist, pos, nn);
+    };
+    if (fabsf(det) >= 1e-15f) {
+      float x1 = (mc * u - mb * v) / det, x2 = (ma * v - mb * u) / det;
+      if (x1 > 1.f) { x1 = 1.f; x2 = (v - mb) / mc; }
+      else if (x1 < -1.f) { x1 = -1.f; x2 = (v + mb) / mc; }
+      if (x2 > 1.f || x2 < -1.f) {
+        const bool hi = x2 > 1.f;
+        x2 = hi ? 1.f : -1.f;
+        x1 = fminf(fmaxf(hi ? (u - mb) / ma : (u + mb) / ma, -1.f), 1.f);
+      }
+      float dist, pos[3], nn[3], fr[9];
+      at(x1, x2, &dist, pos, nn);
+      if (dist < 0.f) { make_frame(nn, fr); emit(0, dist, pos, fr); }
+    } else {  // parallel: the ends of one segment against the other, at most two touching candidates
+      int cnt = 0;
+      for (int e = 0; e < 4 && cnt < 2; e++) {
+        float x1, x2;
+        if (e < 2) {
+          x1 = e == 0 ? 1.f : -1.f;
+          x2 = fminf(fmaxf(e == 0 ? (v - mb) / mc : (v + mb) / mc, -1.f), 1.f);
+        } else {
+          x2 = e == 2 ? 1.f : -1.f;
+          x1 = fminf(fmaxf(e == 2 ? (u - mb) / ma : (u + mb) / ma, -1.f), 1.f);
+        }
+        float dist, pos[3], nn[3], fr[9];
+        at(x1, x2, &dist, pos, nn);
+        if (dist <= 0.f) {
+          cnt++;
+          if (dist < 0.f) { make_frame(nn, fr); emit(e, dist, pos, fr); }
+        }
+      }
+    }
+    return n;
+  }
+  *unsup |= UNSUPPORTED_PAIR;
+  return n;
+}
+
+// geom poses, broad phase (ballot-compacted candidates in pair order), narrow phase in two passes (count, prefix
+// sum over the warp, write): contacts in pair order, deterministic
+__device__ void collision(World& s, int lane) {
+  for (int g = lane; g < NG; g += 32) {
+    const int b = ldi(g1_geom_body + g);
+    const float gp[3] = {ld(g1_geom_pos + 3 * g), ld(g1_geom_pos + 3 * g + 1), ld(g1_geom_pos + 3 * g + 2)};
+    const float gq[4] = {ld(g1_geom_quat + 4 * g), ld(g1_geom_quat + 4 * g + 1), ld(g1_geom_quat + 4 * g + 2),
+                         ld(g1_geom_quat + 4 * g + 3)};
+    float t[3];
+    qrot(s.Q[b], gp, t);
+    for (int k = 0; k < 3; k++) s.u.col.gx[g][k] = s.X[b][k] + t[k];
+    qmul(s.Q[b], gq, s.u.col.gq[g]);
+  }
+  __syncwarp();
+  const unsigned below = (1u << lane) - 1u;
+  int ncand = 0;
+  for (int k = 0; k < (NP + 31) / 32; k++) {
+    const int pr = lane + 32 * k;
+    const bool keep = pr < NP && bounding(s, pr);
+    const unsigned bal = __ballot_sync(FULL, keep);
+    if (keep) s.u.col.cand[ncand + __popc(bal & below)] = (unsigned short)pr;
+    ncand += __popc(bal);
+  }
+  __syncwarp();
+  int total = 0, unsup = 0;
+  for (int c0 = 0; c0 < ncand; c0 += 32) {
+    const int ci = c0 + lane;
+    const int pr = ci < ncand ? s.u.col.cand[ci] : -1;
+    int cnt = pr >= 0 ? collide(s, pr, false, 0, &unsup) : 0;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (cnt > 0) collide(s, pr, true, total + incl - cnt, &unsup);
+    total += __shfl_sync(FULL, incl, 31);
+  }
+  unsup = (int)__reduce_or_sync(FULL, (unsigned)unsup);
+  if (lane == 0) {
+    s.ncon_raw = total;
+    s.ncon = min(total, MAXCON);
+    s.unsup |= unsup | (total > MAXCON ? CONTACT_OVERFLOW : 0);
+  }
+  __syncwarp();
+}
+
+// per contact: friction, the frame rows' moments about O and the support masks (lane = contact); then the groups:
+// the contacts between the same two bodies (in contact order, numbered by their first contact), which share the
+// support and the sign of every Jacobian column, so the Hessian and J' f treat a group as one spatial stiffness /
+// one wrench
+__device__ void contact_setup(World& s, int lane) {
+  const int ncon = s.ncon;
+  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  for (int c = lane; c < ncon; c += 32) {
+    const int pr = s.con_pair[c];
+    // condim 1 (frictionless) contacts: mu = 0 makes the pyramid formulas below reduce to the normal row
+    s.con_mu[c] = ldi(g1_pair_dim + pr) != 3 ? 0.f : (ldi(g1_pair_foot + pr) ? s.fric : ld(g1_pair_mu + pr));
+    const float r[3] = {s.con_pos[c][0] - O[0], s.con_pos[c][1] - O[1], s.con_pos[c][2] - O[2]};
+    for (int d = 0; d < 3; d++) cross(r, s.con_fr[c] + 3 * d, s.con_cv[c] + 3 * d);
+    const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+    const unsigned long long m1 = g1_body_dofmask[b1], m2 = g1_body_dofmask[b2];
+    s.con_m1[c] = m1 & ~m2;
+    s.con_m2[c] = m2 & ~m1;
+  }
+  // group leaders: the first contact of each (body1, body2); the key is kept in con_C[c][0] for a moment
+  int ngroup = 0;
+  for (int c0 = 0; c0 < ncon; c0 += 32) {
+    const int c = c0 + lane;
+    int key = -1 - lane, lead = c;
+    if (c < ncon) {
+      const int pr = s.con_pair[c];
+      key = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)) * 32 + ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+      for (int e = 0; e < c0; e++)  // an earlier chunk (only past 32 contacts)
+        if (__float_as_int(s.con_C[e][0]) == key) { lead = e; break; }
+    }
+    const unsigned same = __match_any_sync(FULL, key);
+    if (lead == c) lead = c0 + __ffs(same) - 1;
+    const bool leader = c < ncon && lead == c;
+    const unsigned bal = __ballot_sync(FULL, leader);
+    if (c < ncon) {
+      s.con_C[c][0] = __int_as_float(key);
+      s.grp_lead[c] = (unsigned char)lead;
+      if (leader) s.con_grp[c] = (unsigned char)(ngroup + __popc(bal & ((1u << lane) - 1u)));
+    }
+    ngroup += __popc(bal);
+    __syncwarp();
+  }
+  for (int c = lane; c < ncon; c += 32) s.con_grp[c] = s.con_grp[s.grp_lead[c]];
+  __syncwarp();
+  for (int g = lane; g < ngroup; g += 32) {
+    unsigned long long m = 0ull;
+    for (int c = 0; c < ncon; c++)
+      if (s.con_grp[c] == g) m |= 1ull << c;
+    s.grp_mask[g] = m;
+  }
+  if (lane == 0) s.ngroup = ngroup;
+  __syncwarp();
+}
+
+// ---- constraint rows -----------------------------------------------------------------------------------------------
+// body spatial motion at O for the generalised vector v (lane = body: a sum over its ancestor dofs)
+__device__ void body_motion(World& s, const float* v, int lane) {
+  if (lane < NB) {
+    float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    unsigned long long m = g1_body_dofmask[lane];
+    while (m) {
+      const int i = __ffsll((long long)m) - 1;
+      m &= m - 1ull;
+      const float vi = v[i];
+      for (int k = 0; k < 3; k++) { a[k] += vi * s.dw[i][k]; a[3 + k] += vi * s.dv[i][k]; }
+    }
+    for (int k = 0; k < 6; k++) s.BV[lane][k] = a[k];
+  }
+  __syncwarp();
+}
+
+// J_d v of every contact's frame rows (after body_motion(v))
+__device__ void contact_jv(World& s, int lane) {
+  const int ncon = s.ncon;
+  for (int c = lane; c < ncon; c += 32) {
+    const int pr = s.con_pair[c];
+    const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+    float dV[6];
+    for (int k = 0; k < 6; k++) dV[k] = s.BV[b2][k] - s.BV[b1][k];
+    for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(s.con_fr[c] + 3 * d, dV + 3) + dot3(s.con_cv[c] + 3 * d, dV);
+  }
+  __syncwarp();
+}
+
+// J v of every row into out (contact rows from cs.jd, limit rows from v)
+__device__ void rows_jv(World& s, const float* v, float* out, int lane) {
+  body_motion(s, v, lane);
+  contact_jv(s, lane);
+  const int nefc = s.nefc;
+  for (int r = lane; r < nefc; r += 32) {
+    const int kind = s.efc_kind[r], a = s.efc_a[r], b = s.efc_b[r];
+    float val;
+    if (kind == ROW_LIMIT) val = b * v[a];
+    else if (kind == ROW_PYRAMID) val = s.cs.jd[a][0] + ((b & 1) ? -1.f : 1.f) * s.con_mu[a] * s.cs.jd[a][1 + (b >> 1)];
+    else val = s.cs.jd[a][0];
+    out[r] = val;
+  }
+  __syncwarp();
+}
+
+// refsafe impedance at the row position pos: stiffness k, damping b, impedance imp (solimp power 2 folded)
+__device__ __forceinline__ void impedance(const float* solref, const float* solimp, float pos, float h, float* k,
+                                          float* b, float* imp) {
+  const float tc = fmaxf(solref[0], 2.f * h), dr = solref[1];
+  const float dmin = fminf(fmaxf(solimp[0], 1e-4f), 0.9999f), dmax = fminf(fmaxf(solimp[1], 1e-4f), 0.9999f);
+  const float width = fmaxf(1e-15f, solimp[2]), mid = fminf(fmaxf(solimp[3], 1e-4f), 0.9999f);
+  const float power = fmaxf(1.f, solimp[4]);
+  *k = 1.f / fmaxf(1e-15f, dmax * dmax * tc * tc * dr * dr);
+  *b = 2.f / fmaxf(1e-15f, dmax * tc);
+  const float x = fabsf(pos) / width;
+  if (x >= 1.f) *imp = dmax;
+  else if (x <= 0.f) *imp = dmin;
+  else {
+    float y;
+    if (power == 2.f) y = x <= mid ? x * x / mid : 1.f - (1.f - x) * (1.f - x) / (1.f - mid);
+    else y = x <= mid ? powf(x, power) / powf(mid, power - 1.f) : 1.f - powf(1.f - x, power) / powf(1.f - mid, power - 1.f);
+    *imp = fminf(fmaxf(dmin + y * (dmax - dmin), dmin), dmax);
+  }
+}
+
+// constraint rows: hinge limits (dof order), then per contact 4 pyramid rows (condim 3) or 1 normal row
+__device__ void make_rows(World& s, int lane) {
+  const float h = G1_TIMESTEP;
+  const unsigned below = (1u << lane) - 1u;
+  for (int i = lane; i < NV; i += 32) s.lim_row[i] = -1;
+  __syncwarp();
+  int nlim = 0;
+  for (int i0 = 0; i0 < NV; i0 += 32) {
+    const int i = i0 + lane;
+    float dlo = 1.f, dhi = 1.f;
+    if (i >= 6 && i < NV) {
+      const float q = s.qpos[i + 1];
+      dlo = q - ld(g1_dof_range + 2 * i);
+      dhi = ld(g1_dof_range + 2 * i + 1) - q;
+    }
+    const bool on = fminf(dlo, dhi) < 0.f;
+    const unsigned bal = __ballot_sync(FULL, on);
+    if (on) {
+      const int r = nlim + __popc(bal & below);
+      const float pos = fminf(dlo, dhi), sg = dlo < dhi ? 1.f : -1.f;
+      const float sr[2] = {ld(g1_jnt_solref), ld(g1_jnt_solref + 1)};
+      const float si[5] = {ld(g1_jnt_solimp), ld(g1_jnt_solimp + 1), ld(g1_jnt_solimp + 2), ld(g1_jnt_solimp + 3),
+                           ld(g1_jnt_solimp + 4)};
+      float k, b, imp;
+      impedance(sr, si, pos, h, &k, &b, &imp);
+      const float R = fmaxf(1e-15f, ld(g1_dof_invweight0 + i) * (1.f - imp) / imp);
+      s.efc_kind[r] = ROW_LIMIT; s.efc_a[r] = (short)i; s.efc_b[r] = (signed char)sg;
+      s.lim_row[i] = (short)r;
+      s.efc_D[r] = 1.f / R;
+      s.efc_aref[r] = -b * (sg * s.qvel[i]) - k * imp * pos;
+    }
+    nlim += __popc(bal);
+  }
+  // contact rows need J qvel
+  body_motion(s, s.qvel, lane);
+  contact_jv(s, lane);
+  const int ncon = s.ncon;
+  int r0 = nlim;
+  for (int c0 = 0; c0 < ncon; c0 += 32) {
+    const int c = c0 + lane;
+    const bool valid = c < ncon;
+    const int pr = valid ? s.con_pair[c] : 0;
+    const int dim = valid ? ldi(g1_pair_dim + pr) : 0;
+    const int want = valid ? (dim == 3 ? 4 : 1) : 0;
+    int incl = want;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int first = r0 + incl - want;
+    if (valid) {
+      const int nr = max(0, min(want, NEFC - first));
+      s.con_row0[c] = (unsigned char)min(first, 255);
+      s.con_nrow[c] = (unsigned char)nr;
+      const float mu = s.con_mu[c];
+      const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+      float iw = ld(g1_body_invweight0 + b1) + ld(g1_body_invweight0 + b2);
+      if (dim == 3) iw = (mu * mu * iw + iw) * 2.f * mu * mu / (float)G1_IMPRATIO;
+      const float sr[2] = {ld(g1_pair_solref), ld(g1_pair_solref + 1)};
+      const float si[5] = {ld(g1_pair_solimp), ld(g1_pair_solimp + 1), ld(g1_pair_solimp + 2),
+                           ld(g1_pair_solimp + 3), ld(g1_pair_solimp + 4)};
+      float k, b, imp;
+      const float dist = s.con_dist[c];
+      impedance(sr, si, dist, h, &k, &b, &imp);
+      const float D = 1.f / fmaxf(1e-15f, iw * (1.f - imp) / imp);
+      for (int t = 0; t < nr; t++) {
+        const int r = first + t;
+        const float vel = dim == 3 ? s.cs.jd[c][0] + ((t & 1) ? -1.f : 1.f) * mu * s.cs.jd[c][1 + (t >> 1)]
+                                   : s.cs.jd[c][0];
+        s.efc_kind[r] = dim == 3 ? ROW_PYRAMID : ROW_NORMAL;
+        s.efc_a[r] = (short)c;
+        s.efc_b[r] = (signed char)t;
+        s.efc_D[r] = D;
+        s.efc_aref[r] = -b * vel - k * imp * dist;
+      }
+    }
+    r0 += __shfl_sync(FULL, incl, 31);
+  }
+  if (lane == 0) {
+    s.nlim = nlim;
+    s.nefc = min(r0, NEFC);
+    if (r0 > NEFC) s.unsup |= ROW_OVERFLOW;
+  }
+  __syncwarp();
+}
+
+// ---- Newton solver -------------------------------------------------------------------------------------------------
+// Ma = M a and jar = J a - aref at the current qacc
+__device__ void refresh(World& s, int lane) {
+  matvec(s.M, s.qacc, s.Ma, lane);
+  rows_jv(s, s.qacc, s.efc_jar, lane);
+  for (int r = lane; r < s.nefc; r += 32) s.efc_jar[r] -= s.efc_aref[r];
+  __syncwarp();
+}
+
+__device__ float total_cost(World& s, int lane) {
+  float g = 0.f;
+  for (int i = lane; i < NV; i += 32) g += 0.5f * (s.Ma[i] - s.qsm[i]) * (s.qacc[i] - s.qacc0[i]);
+  for (int r = lane; r < s.nefc; r += 32) {
+    const float x = s.efc_jar[r];
+    if (x < 0.f) g += 0.5f * s.efc_D[r] * x * x;
+  }
+  return warp_sum(g);
+}
+
+// grad = M qacc - qfrc_smooth - J' f with f = -D jar on the active rows; returns |grad|. J' f: each contact's
+// wrench at O from its rows' forces, summed per group (members in contact order), then per dof the groups whose
+// support holds it (sign +1 on body 2's chain, -1 on body 1's) and the dof's limit row
+__device__ float newton_grad(World& s, int lane) {
+  const int ncon = s.ncon, ngroup = s.ngroup;
+  for (int c = lane; c < ncon; c += 32) {
+    const int r0 = s.con_row0[c], nr = s.con_nrow[c];
+    float f[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t = 0; t < nr; t++) {
+      const float x = s.efc_jar[r0 + t];
+      f[t] = x < 0.f ? -s.efc_D[r0 + t] * x : 0.f;
+    }
+    const float mu = s.con_mu[c];
+    const float F[3] = {f[0] + f[1] + f[2] + f[3], mu * (f[0] - f[1]), mu * (f[2] - f[3])};
+    float w[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int d = 0; d < 3; d++)
+      for (int k = 0; k < 3; k++) { w[k] += F[d] * s.con_cv[c][3 * d + k]; w[3 + k] += F[d] * s.con_fr[c][3 * d + k]; }
+    for (int k = 0; k < 6; k++) s.cs.wr[c][k] = w[k];
+  }
+  __syncwarp();
+  // group sums into the leader's slot: lane (g mod 5, entry) sums, then writes after a fence
+  for (int g0 = 0; g0 < ngroup; g0 += 5) {
+    const int g = g0 + lane / 6, e = lane % 6;
+    float acc = 0.f;
+    const bool on = lane < 30 && g < ngroup;
+    if (on) {
+      unsigned long long m = s.grp_mask[g];
+      while (m) {
+        const int c = __ffsll((long long)m) - 1;
+        m &= m - 1ull;
+        acc += s.cs.wr[c][e];
+      }
+    }
+    __syncwarp();
+    if (on) s.cs.wr[__ffsll((long long)s.grp_mask[g]) - 1][e] = acc;
+    __syncwarp();
+  }
+  float gn = 0.f;
+  for (int i = lane; i < NV; i += 32) {
+    float jtf = 0.f;
+    const int lr = s.lim_row[i];
+    if (lr >= 0) {
+      const float x = s.efc_jar[lr];
+      if (x < 0.f) jtf = s.efc_b[lr] * (-s.efc_D[lr] * x);
+    }
+    const float w[3] = {s.dw[i][0], s.dw[i][1], s.dw[i][2]}, v[3] = {s.dv[i][0], s.dv[i][1], s.dv[i][2]};
+    const unsigned long long bit = 1ull << i;
+    for (int g = 0; g < ngroup; g++) {
+      const int c = __ffsll((long long)s.grp_mask[g]) - 1;
+      const float sg = (s.con_m2[c] & bit) ? 1.f : ((s.con_m1[c] & bit) ? -1.f : 0.f);
+      if (sg != 0.f) jtf += sg * (dot3(w, s.cs.wr[c]) + dot3(v, s.cs.wr[c] + 3));
+    }
+    const float g = s.Ma[i] - s.qsm[i] - jtf;
+    s.grad[i] = g;
+    gn += g * g;
+  }
+  __syncwarp();
+  return sqrtf(warp_sum(gn));
+}
+
+// H = M + J' D J over the quadratic rows, into s.L (lower triangle). A contact's rows add J_f' C J_f with J_f its
+// frame rows and C the 3 x 3 sum of D u u' over its quadratic pyramid rows u = n +- mu t_k; J_f = G S with G the
+// 3 x 6 rows (moment, frame) and S the dofs' motion vectors, so a group of contacts adds S' K S with the 6 x 6
+// spatial stiffness K = sum G' C G, on the group's support with the columns' signs
+__device__ void hessian(World& s, int lane) {
+  const int ncon = s.ncon, ngroup = s.ngroup;
+  for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
+  for (int c = lane; c < ncon; c += 32) {
+    const int r0 = s.con_row0[c], nr = s.con_nrow[c];
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t = 0; t < nr; t++) d[t] = s.efc_jar[r0 + t] < 0.f ? s.efc_D[r0 + t] : 0.f;
+    const float mu = s.con_mu[c];
+    s.con_C[c][0] = d[0] + d[1] + d[2] + d[3];
+    s.con_C[c][1] = mu * (d[0] - d[1]);
+    s.con_C[c][2] = mu * mu * (d[0] + d[1]);
+    s.con_C[c][3] = mu * (d[2] - d[3]);
+    s.con_C[c][4] = mu * mu * (d[2] + d[3]);
+  }
+  __syncwarp();
+  for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
+    if (s.efc_jar[r] < 0.f) s.L[TRI(s.efc_a[r], s.efc_a[r])] += s.efc_D[r];
+  __syncwarp();
+  for (int g = 0; g < ngroup; g++) {
+    const unsigned long long gm = s.grp_mask[g];
+    // K (upper triangle of 6 x 6, entry e = (e1, e2)), lane e < 21, summed over the members in contact order
+    if (lane < 21) {
+      int e1 = 0, rest = lane;
+      while (rest >= 6 - e1) { rest -= 6 - e1; e1++; }
+      const int e2 = e1 + rest;
+      float acc = 0.f;
+      unsigned long long m = gm;
+      while (m) {
+        const int c = __ffsll((long long)m) - 1;
+        m &= m - 1ull;
+        const float* C = s.con_C[c];
+        if (C[0] == 0.f) continue;
+        float x[3], y[3];
+        for (int dd = 0; dd < 3; dd++) {
+          x[dd] = e1 < 3 ? s.con_cv[c][3 * dd + e1] : s.con_fr[c][3 * dd + e1 - 3];
+          y[dd] = e2 < 3 ? s.con_cv[c][3 * dd + e2] : s.con_fr[c][3 * dd + e2 - 3];
+        }
+        acc += C[0] * x[0] * y[0] + C[1] * (x[0] * y[1] + x[1] * y[0]) + C[2] * x[1] * y[1]
+               + C[3] * (x[0] * y[2] + x[2] * y[0]) + C[4] * x[2] * y[2];
+      }
+      s.u.hs.K[lane] = acc;
+    }
+    __syncwarp();
+    const int lead = __ffsll((long long)gm) - 1;
+    const unsigned long long m1 = s.con_m1[lead], m2 = s.con_m2[lead], sup = m1 | m2;
+    bool any = false;
+    for (int e = 0; e < 21; e++) any |= s.u.hs.K[e] != 0.f;
+    __syncwarp();
+    if (!any) continue;  // (uniform) no quadratic row in the group
+    const int nsup = __popcll(sup);
+    // P_k = K s_i for the support dofs i (rank k), signed
+    for (int h = 0; h < 2; h++) {
+      const int i = lane + 32 * h;
+      if (i < NV && ((sup >> i) & 1ull)) {
+        const int k = __popcll(sup & ((1ull << i) - 1ull));
+        const float sg = ((m2 >> i) & 1ull) ? 1.f : -1.f;
+        const float* K = s.u.hs.K;
+        const float v[6] = {sg * s.dw[i][0], sg * s.dw[i][1], sg * s.dw[i][2], sg * s.dv[i][0], sg * s.dv[i][1],
+                            sg * s.dv[i][2]};
+        // K rows from the packed upper triangle
+        float P[6];
+#pragma unroll
+        for (int r = 0; r < 6; r++) {
+          float acc = 0.f;
+#pragma unroll
+          for (int q = 0; q < 6; q++) {
+            const int lo = r < q ? r : q, hi = r < q ? q : r;
+            acc += K[lo * 6 - lo * (lo - 1) / 2 + (hi - lo)] * v[q];
+          }
+          P[r] = acc;
+        }
+        for (int r = 0; r < 6; r++) s.u.hs.P[k][r] = P[r];
+        s.u.hs.dof[k] = (unsigned char)i;
+      }
+    }
+    __syncwarp();
+    // H(dof a, dof b) += (sign_a s_a) . P_b for the support pairs a >= b
+    const int npair = nsup * (nsup + 1) / 2;
+    for (int e = lane; e < npair; e += 32) {
+      int a = (int)((sqrtf(8.f * e + 1.f) - 1.f) * 0.5f);
+      if (TRI(a + 1, 0) <= e) a++;
+      if (TRI(a, 0) > e) a--;
+      const int b = e - TRI(a, 0);
+      const int da = s.u.hs.dof[a], db = s.u.hs.dof[b];
+      const float sa = ((m2 >> da) & 1ull) ? 1.f : -1.f;
+      const float* P = s.u.hs.P[b];
+      const float v = sa * (s.dw[da][0] * P[0] + s.dw[da][1] * P[1] + s.dw[da][2] * P[2] + s.dv[da][0] * P[3]
+                            + s.dv[da][1] * P[4] + s.dv[da][2] * P[5]);
+      s.L[TRI(da, db)] += v;
+    }
+    __syncwarp();
+  }
+}
+
+// Newton from the warm start (or qacc_smooth when that costs less); returns the iterations run
+__device__ int newton(World& s, int iterations, int lane) {
+  const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
+  refresh(s, lane);
+  float cost = total_cost(s, lane);
+  // keep the warm start's qacc, Ma, jar in tmp / p / jv in case it stays the start
+  for (int i = lane; i < NV; i += 32) { s.tmp[i] = s.qacc[i]; s.qacc[i] = s.qacc0[i]; s.p[i] = s.Ma[i]; }
+  for (int r = lane; r < s.nefc; r += 32) s.efc_jv[r] = s.efc_jar[r];
+  __syncwarp();
+  refresh(s, lane);
+  const float cost0 = total_cost(s, lane);
+  if (cost0 > cost) {
+    for (int i = lane; i < NV; i += 32) { s.qacc[i] = s.tmp[i]; s.Ma[i] = s.p[i]; }
+    for (int r = lane; r < s.nefc; r += 32) s.efc_jar[r] = s.efc_jv[r];
+    __syncwarp();
+  } else {
+    cost = cost0;
+  }
+  newton_grad(s, lane);
+  PROF(s, 6);
+  int it = 0;
+  bool same_zones = false;  // no row changed its zone in the last step: H and its factor in s.L are still exact
+  while (it < iterations) {
+    if (!same_zones) {
+      hessian(s, lane);
+      PROF(s, 7);
+      chol_factor(s.L, s.L, s.dinv, lane);
+      PROF(s, 8);
+    }
+    for (int i = lane; i < NV; i += 32) s.p[i] = -s.grad[i];
+    __syncwarp();
+    chol_solve(s.L, s.dinv, s.p, lane);
+    PROF(s, 9);
+    // exact line search along p: the cost is piecewise quadratic in alpha
+    rows_jv(s, s.p, s.efc_jv, lane);
+    matvec(s.M, s.p, s.Mp, lane);
+    float a1 = 0.f, a2 = 0.f;
+    for (int i = lane; i < NV; i += 32) { a1 += (s.Ma[i] - s.qsm[i]) * s.p[i]; a2 += s.p[i] * s.Mp[i]; }
+    a1 = warp_sum(a1);
+    a2 = warp_sum(a2);
+    const int nefc = s.nefc;
+    float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE];
+#pragma unroll
+    for (int t = 0; t < ROWS_PER_LANE; t++) {
+      const int r = lane + 32 * t;
+      const bool v = r < nefc;
+      rx[t] = v ? s.efc_jar[r] : 0.f;
+      rj[t] = v ? s.efc_jv[r] : 0.f;
+      rD[t] = v ? s.efc_D[r] : 0.f;
+    }
+    float alpha = 0.f, lo = 0.f, hi = 1e30f, d0 = 0.f;
+    unsigned zprev = 0u;
+    bool nwt = false;
+    for (int k = 0; k <= 40; k++) {
+      PROF_COUNT(17, 1);
+      float fd = 0.f, fdd = 0.f;
+      unsigned z = 0u;
+#pragma unroll
+      for (int t = 0; t < ROWS_PER_LANE; t++) {
+        const float x = rx[t] + alpha * rj[t];
+        if (x < 0.f) { z |= 1u << t; fd += rD[t] * x * rj[t]; fdd += rD[t] * rj[t] * rj[t]; }
+      }
+      if (__all_sync(FULL, nwt && z == zprev)) break;  // the Newton step kept every row on its piece: exact minimum
+      if (k == 40) break;
+      fd = warp_sum(fd) + a1 + alpha * a2;
+      fdd = warp_sum(fdd) + a2;
+      if (k == 0) { d0 = fd; if (d0 >= 0.f) break; }
+      if (fabsf(fd) <= 1e-7f * fabsf(d0)) break;
+      if (fd < 0.f) lo = alpha; else hi = alpha;
+      float nx = alpha - fd / fdd;
+      nwt = nx > lo && nx < hi;
+      if (!nwt) nx = hi < 1e29f ? 0.5f * (lo + hi) : 2.f * fmaxf(alpha, 1e-6f);
+      zprev = z;
+      alpha = nx;
+    }
+    for (int i = lane; i < NV; i += 32) { s.qacc[i] += alpha * s.p[i]; s.Ma[i] += alpha * s.Mp[i]; }
+    bool chg = false;
+#pragma unroll
+    for (int t = 0; t < ROWS_PER_LANE; t++) {
+      const int r = lane + 32 * t;
+      const float xn = rx[t] + alpha * rj[t];
+      chg |= (xn < 0.f) != (rx[t] < 0.f);
+      if (r < nefc) s.efc_jar[r] = xn;
+    }
+    same_zones = !__any_sync(FULL, chg);
+    __syncwarp();
+    PROF(s, 10);
+    const float newcost = total_cost(s, lane);
+    const float gn = newton_grad(s, lane);
+    const float improvement = scale * (cost - newcost);
+    cost = newcost;
+    it++;
+    PROF(s, 11);
+    PROF_COUNT(16, 1);
+    if (improvement < tol || scale * gn < tol) break;
+  }
+  return it;
+}
+
+// ---- one substep -------------------------------------------------------------------------------------------------
+__device__ void substep(World& s, int iterations, int lane) {
+  const float h = G1_TIMESTEP;
+  PROF_START(s);
+  kinematics(s, lane);
+  dof_motion(s, lane);
+  PROF(s, 0);
+  body_terms(s, lane);
+  PROF(s, 1);
+  mass_and_force(s, lane);
+  PROF(s, 2);
+  // qacc_smooth = M^-1 qfrc_smooth
+  for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
+  for (int i = lane; i < NV; i += 32) s.qacc0[i] = s.qsm[i];
+  __syncwarp();
+  chol_factor(s.L, s.L, s.dinv, lane);
+  chol_solve(s.L, s.dinv, s.qacc0, lane);
+  PROF(s, 3);
+  collision(s, lane);
+  PROF(s, 4);
+  contact_setup(s, lane);
+  make_rows(s, lane);
+  PROF(s, 5);
+  PROF_COUNT(18, s.ncon);
+  PROF_COUNT(19, s.nefc);
+  const int it = newton(s, iterations, lane);
+  // implicitfast: (M + h kv) a_adv = M qacc; qvel += h a_adv; qpos integrated with the new qvel
+  for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
+  __syncwarp();
+  for (int i = lane; i < NV; i += 32) { s.L[TRI(i, i)] += h * ld(g1_dof_kv + i); s.tmp[i] = s.Ma[i]; }
+  __syncwarp();
+  chol_factor(s.L, s.L, s.dinv, lane);
+  chol_solve(s.L, s.dinv, s.tmp, lane);
+  for (int i = lane; i < NV; i += 32) s.qvel[i] += h * s.tmp[i];
+  __syncwarp();
+  if (lane == 0) {
+    s.nit = it;
+    for (int k = 0; k < 3; k++) s.qpos[k] += h * s.qvel[k];
+    const float w[3] = {s.qvel[3], s.qvel[4], s.qvel[5]};
+    const float nw = sqrtf(dot3(w, w));
+    if (nw > 0.f) {
+      float sa, ca;
+      sincosf(0.5f * h * nw, &sa, &ca);
+      const float dq[4] = {ca, sa * w[0] / nw, sa * w[1] / nw, sa * w[2] / nw};
+      const float q[4] = {s.qpos[3], s.qpos[4], s.qpos[5], s.qpos[6]};
+      float o[4];
+      qmul(q, dq, o);
+      const float on = sqrtf(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      for (int k = 0; k < 4; k++) s.qpos[3 + k] = o[k] / on;
+    }
+  }
+  for (int i = 6 + lane; i < NV; i += 32) s.qpos[i + 1] += h * s.qvel[i];
+  __syncwarp();
+  PROF(s, 12);
+  PROF_COUNT(20, 1);
+}
+
+}  // namespace nbg1

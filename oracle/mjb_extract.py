@@ -181,23 +181,40 @@ def derive(m):
     g1[sw], g2[sw] = m["pair_geom2"][sw], m["pair_geom1"][sw]
     names = m["geom_names"]
     foot = np.array([int(names[g1[p]] == "floor" and "foot" in names[g2[p]]) for p in range(NPAIR)], np.int32)
-    return dict(body_depth=depth, dof_kp=kp, dof_kv=kv, dof_frclim=frclim, dof_range=jrange, pair_g1=g1, pair_g2=g2,
+    child = np.zeros((nb, 3), np.int32)
+    nchild = np.zeros(nb, np.int32)
+    for b in range(2, nb):
+        p = m["body_parentid"][b]
+        child[p, nchild[p]] = b
+        nchild[p] += 1
+    dofmask = np.zeros(nb, np.uint64)  # bit i: dof i moves body b (its own dofs and its ancestors')
+    for b in range(1, nb):
+        k, bits = b, 0
+        while k >= 1:
+            for i in range(m["body_dofadr"][k], m["body_dofadr"][k] + m["body_dofnum"][k]):
+                bits |= 1 << int(i)
+            k = m["body_parentid"][k]
+        dofmask[b] = bits
+    return dict(body_nchild=nchild, body_child=child, body_dofmask=dofmask, body_depth=depth, dof_kp=kp, dof_kv=kv, dof_frclim=frclim, dof_range=jrange, pair_g1=g1, pair_g2=g2,
                 pair_foot=foot, torso_body=np.int32(m["body_names"].index("torso_link")))
 
 
 def carr(name, ctype, a, per_line=6):
     a = np.asarray(a).ravel()
     if ctype == "double":
-        vals = [repr(float(x)) if np.isfinite(x) else "1e300" for x in a]
+        vals = [repr(float(x)) if np.isfinite(x) else "1e30" for x in a]  # (no limit: a float-safe 1e30)
+    elif ctype == "unsigned long long":
+        vals = [f"{int(x)}ull" for x in a]
     else:
         vals = [str(int(x)) for x in a]
     lines = [", ".join(vals[i:i + per_line]) for i in range(0, len(vals), per_line)]
+    ctype = "NB_REAL" if ctype == "double" else ctype
     return f"NB_MODEL_CONST {ctype} {name}[{len(a)}] = {{\n  " + ",\n  ".join(lines) + "};\n"
 
 
 def write_header(m, d, path, sha):
-    """The model as C arrays (float64 values, exact decimal round trip). The oracle reads them as double; the CUDA
-    library rounds them to float when it packs its constant block."""
+    """The model as C arrays (float64 values, exact decimal round trip). The oracle instantiates them as double
+    (NB_REAL's default); the CUDA library defines NB_REAL as float, so the compiler rounds each literal once."""
     geoms = sorted(set(d["pair_g1"].tolist()) | set(d["pair_g2"].tolist()))
     assert geoms == list(range(NGEOM))
     pw = m["pair_friction"][:, 0]
@@ -205,7 +222,9 @@ def write_header(m, d, path, sha):
         "// Generated by oracle/mjb_extract.py from the mjlab Unitree G1 model (g1_train.mjb, MuJoCo 3.17 binary,\n"
         f"// sha256 {sha}). Model data: Unitree Robotics, BSD-3-Clause (nablaengine_b200/model/LICENSE).\n"
         "// Do not edit: regenerate with the script.\n#pragma once\n",
-        "#ifndef NB_MODEL_CONST\n#define NB_MODEL_CONST static const\n#endif\n",
+        "#ifndef NB_MODEL_CONST\n#define NB_MODEL_CONST static const\n#endif\n"
+        "#ifndef NB_REAL  // the element type of the real-valued tables (the CUDA library: float)\n#define NB_REAL double\n"
+        "#endif\n",
         f"#define G1_NQ {NQ}\n#define G1_NV {NV}\n#define G1_NU {NU}\n#define G1_NBODY {NBODY}\n"
         f"#define G1_NGEOM {NGEOM}\n#define G1_NPAIR {NPAIR}\n#define G1_TORSO {int(d['torso_body'])}\n"
         f"#define G1_MAXDEPTH {int(d['body_depth'].max())}\n",
@@ -215,6 +234,9 @@ def write_header(m, d, path, sha):
         carr("g1_body_parent", "int", m["body_parentid"]),
         carr("g1_body_depth", "int", d["body_depth"]),
         carr("g1_body_dofadr", "int", m["body_dofadr"]),
+        carr("g1_body_nchild", "int", d["body_nchild"]),
+        carr("g1_body_child", "int", d["body_child"]),
+        carr("g1_body_dofmask", "unsigned long long", d["body_dofmask"], 4),
         carr("g1_body_qposadr", "int", [0, 0] + [m["jnt_qposadr"][m["body_jntadr"][b]] for b in range(2, NBODY)]),
         carr("g1_body_pos", "double", m["body_pos"]),
         carr("g1_body_quat", "double", m["body_quat"]),

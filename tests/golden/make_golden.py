@@ -1,0 +1,63 @@
+"""Generate the committed golden fixtures of tests/golden/ from the reference's own data files.
+
+Run once where the reference repository is readable: python tests/golden/make_golden.py --ref <reference checkout>.
+The outputs are small subsets of the reference's Apache-2.0 benchmark data (benchmarks/data, fixtures/mjlab):
+
+  truth_check.npz  the 64 "check" states of each corpus mf_s0..mf_s3 (inputs and MuJoCo C float64 forward truth at
+                   2000 iterations, tolerance 1e-13; model_flags 0 = MuJoCo C and MuJoCo Warp agree on the state)
+  truth_grad.npz   mf_s0's gradient states: inputs, the 3 stored cotangents, the FD VJP truth (h = 1e-6) and its
+                   floor (h = 1e-7) in the tangent basis (qpos tangent 35, qvel 35, ctrl 29), validity bits, groups
+  mjw_sample.npz   the first 256 states of mf_s0 with MuJoCo Warp 3.17's one-step outputs (50 iterations, float32)
+                   and its per-substep contact / row / iteration counts
+
+Nothing at test time reads the reference; the tests read these files.
+"""
+import argparse
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+INPUTS = ("qpos", "qvel", "qacc_warmstart", "ctrl", "friction", "com")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", required=True, help="the reference repository root")
+    a = ap.parse_args()
+    ref = Path(a.ref)
+    data = ref / "benchmarks" / "data"
+    out = {k: [] for k in INPUTS + ("check_out", "model_flags", "corpus", "index")}
+    for s in range(4):
+        c, t = np.load(data / f"mf_s{s}.npz"), np.load(data / "truth" / f"mf_s{s}.npz")
+        idx = t["check_index"]
+        for k in INPUTS:
+            out[k].append(c[k][idx])
+        out["check_out"].append(t["check_out"])
+        out["model_flags"].append(t["model_flags"][idx])
+        out["corpus"].append(np.full(len(idx), s, np.int8))
+        out["index"].append(idx)
+    np.savez_compressed(HERE / "truth_check.npz", **{k: np.concatenate(v) for k, v in out.items()})
+
+    c, t = np.load(data / "mf_s0.npz"), np.load(data / "truth" / "mf_s0.npz")
+    idx = t["index"]
+    g = {k: c[k][idx] for k in INPUTS}
+    g.update(cot_qpos=c["cot_qpos"][idx], cot_qvel=c["cot_qvel"][idx], index=idx, out=t["out"],
+             fd_vjp=t["fd_vjp"], fd_vjp_floor=t["fd_vjp_floor"], bad=t["bad"], model_flags=t["model_flags"][idx])
+    for k in t.files:
+        if k.startswith("group_"):
+            g[k] = t[k]
+    np.savez_compressed(HERE / "truth_grad.npz", **g)
+
+    m = np.load(ref / "fixtures" / "mjlab" / "mjw317_mf_s0.npz")
+    n = 256
+    w = {k: c[k][:n] for k in INPUTS}
+    w.update(out_qpos=m["out_qpos"][:n], out_qvel=m["out_qvel"][:n], ncon=m["ncon"][:n], nefc=m["nefc"][:n],
+             niter=m["niter"][:n], model_flags=t["model_flags"][:n])
+    np.savez_compressed(HERE / "mjw_sample.npz", **w)
+    for f in ("truth_check.npz", "truth_grad.npz", "mjw_sample.npz"):
+        print(f, (HERE / f).stat().st_size, "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,135 @@
+"""Parity of the CUDA forward step (libnabla_g1.so, through the torch API and the C ABI) with the CPU oracle and the
+reference's golden data. Needs a GPU."""
+import numpy as np
+import pytest
+
+import oracle
+from nablaengine_b200 import synthetic
+
+pytestmark = pytest.mark.gpu
+INPUTS = ("qpos", "qvel", "qacc_warmstart", "ctrl", "friction", "com")
+# float32 step against the float64 oracle (same algorithm, 10 iterations): per-world relative error of qvel'
+MEDIAN_TOL, P99_TOL = 2e-6, 1e-4
+
+
+def rel_world(a, b):
+    return np.linalg.norm(a - b, axis=1) / np.maximum(np.linalg.norm(b, axis=1), 1e-9)
+
+
+def gpu_forward(args, iterations=10, substeps=4):
+    import torch
+    from nablaengine_b200 import torch_ffi
+    t = [torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda() for a in args]
+    out = torch_ffi.forward(*t, iterations=iterations, substeps=substeps)
+    torch.cuda.synchronize()
+    return [o.cpu().numpy() for o in out]
+
+
+def check_parity(args, iterations=10, substeps=4, med=MEDIAN_TOL, p99=P99_TOL):
+    q1, v1, w1, info = gpu_forward(args, iterations, substeps)
+    oq, ov, ow, oinfo = oracle.step(*args, iterations=iterations, substeps=substeps)
+    ev = rel_world(v1, ov)
+    assert np.isfinite(v1).all() and np.isfinite(q1).all()
+    assert np.median(ev) <= med, np.median(ev)
+    assert np.percentile(ev, 99) <= p99, np.percentile(ev, 99)
+    return q1, v1, w1, info, oinfo, ev
+
+
+def test_parity_golden_check_states(golden):
+    g = golden("truth_check.npz")
+    args = [g[k] for k in INPUTS]
+    q1, v1, _, info, oinfo, _ = check_parity(args)
+    # contact and row counts equal the oracle's on (almost) every world
+    assert (info[:, 1] == oinfo[:, 1]).mean() >= 0.99
+    assert (info[:, 2] == oinfo[:, 2]).mean() >= 0.99
+    assert (info[:, 3] == oinfo[:, 3]).all()
+    # against MuJoCo's converged float64 truth on the model-ok states (the reference: median 8.5e-7)
+    ok = g["model_flags"] == 0
+    et = rel_world(v1, g["check_out"][:, 36:])
+    assert np.median(et[ok]) <= 5e-6
+
+
+def test_parity_synthetic_forward_config():
+    s = synthetic.config_states("forward", B=1024)
+    args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    check_parity(args)
+
+
+def test_parity_lowered_multicontact():
+    s = synthetic.config_states("vjp", B=512)
+    args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    check_parity(args)
+
+
+def test_mujoco_warp_gate(golden):
+    """The reference's own gate against MuJoCo Warp (50 iterations): qvel median / p99 <= 5e-6 / 5e-5."""
+    g = golden("mjw_sample.npz")
+    _, v1, _, info = gpu_forward([g[k] for k in INPUTS], iterations=50)
+    ok = g["model_flags"] == 0
+    ev = rel_world(v1, g["out_qvel"])
+    assert np.median(ev[ok]) <= 5e-6 and np.percentile(ev[ok], 99) <= 5e-5
+    assert (info[:, 1] == g["ncon"][:, 3]).mean() >= 0.98
+
+
+def test_deterministic_bitwise():
+    s = synthetic.config_states("vjp", B=2048)
+    args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    a = gpu_forward(args)
+    b = gpu_forward(args)
+    for x, y in zip(a, b):
+        assert np.array_equal(x.view(np.uint32) if x.dtype == np.float32 else x,
+                              y.view(np.uint32) if y.dtype == np.float32 else y)
+
+
+def test_substeps_and_iterations_options():
+    s = synthetic.config_states("forward", B=64)
+    args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    for it, ns in ((0, 1), (1, 2), (3, 1), (10, 8)):
+        check_parity(args, iterations=it, substeps=ns, med=5e-6, p99=5e-4)
+
+
+def test_overflow_bits_and_raw_count():
+    s = synthetic.states(8, 7)
+    s["qpos"][:, 2] = 0.05
+    s["qpos"][:, 7:] = 0.0
+    args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    _, _, _, info = gpu_forward(args, substeps=1)
+    _, _, _, oinfo = oracle.step(*args, substeps=1)
+    assert (info[:, 1] == oinfo[:, 1]).all()
+    assert ((info[:, 3] & 4) != 0).tolist() == (info[:, 1] > 64).tolist()
+    assert (info[:, 2] <= 192).all()
+
+
+def test_zero_worlds_and_type_errors():
+    import torch
+    from nablaengine_b200 import torch_ffi
+    e = lambda *s: torch.zeros(s, dtype=torch.float32, device="cuda")  # noqa: E731
+    out = torch_ffi.forward(e(0, 36), e(0, 35), e(0, 35), e(0, 29), e(0), e(0, 3))
+    assert out[0].shape == (0, 36) and out[3].shape == (0, 4)
+    with pytest.raises(TypeError):
+        torch_ffi.forward(e(2, 36).double(), e(2, 35), e(2, 35), e(2, 29), e(2), e(2, 3))
+    with pytest.raises(TypeError):
+        torch_ffi.forward(e(2, 36), e(2, 34), e(2, 35), e(2, 29), e(2), e(2, 3))
+    with pytest.raises(TypeError):
+        torch_ffi.forward(e(2, 36)[:, :36].t().contiguous().t(), e(2, 35), e(2, 35), e(2, 29), e(2), e(2, 3))
+
+
+def test_cuda_graph_capture_replay():
+    import torch
+    from nablaengine_b200 import torch_ffi
+    s = synthetic.config_states("forward", B=256)
+    t = {k: torch.from_numpy(v).cuda() for k, v in s.items()}
+    torch_ffi.init(0)
+    ref = torch_ffi.forward(t["qpos"], t["qvel"], t["warm"], t["ctrl"], t["friction"], t["com"])
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        torch_ffi.forward(t["qpos"], t["qvel"], t["warm"], t["ctrl"], t["friction"], t["com"])
+    torch.cuda.current_stream().wait_stream(side)
+    with torch.cuda.graph(g):
+        out = torch_ffi.forward(t["qpos"], t["qvel"], t["warm"], t["ctrl"], t["friction"], t["com"])
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(ref, out):
+        assert torch.equal(a, b)

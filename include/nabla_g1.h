@@ -48,6 +48,15 @@ int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* q
                   const float* ctrl, const float* friction, const float* com, int iterations, int nsub, float* qpos_out,
                   float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work);
 
+/* nb_g1_forward plus the per-substep work counters stats (B, nsub, 8) int32: contacts kept, constraint rows, Newton
+ * iterations, line-search evaluations, Hessian factorisations, broad-phase candidate pairs, contacts found, 0; the
+ * outputs are bitwise those of nb_g1_forward. The counters feed the
+ * FLOP count of a step (the roofline of the benchmark). No counterpart in the reference's ABI: it exposes the same
+ * counts through its debug profile build (src/nablaengine/g1_engine/step.py:44-53 PROF_PHASES). */
+int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                        const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                        float* qpos_out, float* qvel_out, float* warm_out, int* info, int* stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,7 +10,7 @@ from pathlib import Path
 from . import build as _build
 
 HEADER = Path(__file__).resolve().parents[1] / "include" / "nabla_g1.h"
-EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward")
+EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward", "nb_g1_forward_stats")
 ABI_VERSION = 1
 NQ, NV, NU, NBODY, MAXCON, NEFC = 36, 35, 29, 31, 64, 192
 
@@ -45,6 +45,8 @@ def load(path=None, build_if_missing=True):
         lib.nb_g1_upload.argtypes, lib.nb_g1_upload.restype = [vp, vp], i32
         lib.nb_g1_forward.argtypes = [vp, i32] + [vp] * 6 + [i32, i32] + [vp] * 7
         lib.nb_g1_forward.restype = i32
+        lib.nb_g1_forward_stats.argtypes = [vp, i32] + [vp] * 6 + [i32, i32] + [vp] * 5
+        lib.nb_g1_forward_stats.restype = i32
         sizes = (ctypes.c_longlong * 8)()
         lib.nb_g1_sizes(sizes)
         want = (NQ, NV, NU, NBODY, MAXCON, NEFC)

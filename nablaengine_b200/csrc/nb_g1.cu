@@ -17,7 +17,7 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
                                                       const float* __restrict__ com, int iterations, int nsub,
                                                       float* __restrict__ oq, float* __restrict__ ov,
                                                       float* __restrict__ ow, int* __restrict__ info,
-                                                      float* __restrict__ ocon) {
+                                                      float* __restrict__ ocon, int* __restrict__ stats) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * WPB + warp;
@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   if (lane < 3) s.com[lane] = com[w64 * 3 + lane];
   if (lane == 0) { s.fric = fric[w]; s.unsup = 0; s.nit = 0; }
   __syncwarp();
-  for (int k = 0; k < nsub; k++) substep(s, iterations, lane);
+  for (int k = 0; k < nsub; k++) substep(s, iterations, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr);
   for (int i = lane; i < NQ; i += 32) oq[w64 * NQ + i] = s.qpos[i];
   for (int i = lane; i < NV; i += 32) { ov[w64 * NV + i] = s.qvel[i]; ow[w64 * NV + i] = s.qacc[i]; }
   if (lane == 0) {
@@ -72,10 +72,10 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
   return (int)cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
 }
 
-int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
-                  const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
-                  float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work) {
-  (void)work;
+static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                          const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                          float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape,
+                          int* stats) {
   if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return (int)cudaErrorInvalidValue;
   if (tape) return (int)cudaErrorNotSupported;
   if (nw == 0) return 0;
@@ -83,8 +83,24 @@ int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* q
     return (int)cudaErrorInvalidValue;
   const int blocks = (nw + WPB - 1) / WPB;
   k_forward<<<blocks, WPB * 32, SMEM, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
-                                                qvel_out, warm_out, info, ocon);
+                                                qvel_out, warm_out, info, ocon, stats);
   return (int)cudaGetLastError();
+}
+
+int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                  const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                  float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work) {
+  (void)work;
+  return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
+                        warm_out, info, ocon, tape, nullptr);
+}
+
+int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                        const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                        float* qpos_out, float* qvel_out, float* warm_out, int* info, int* stats) {
+  if (!stats) return (int)cudaErrorInvalidValue;
+  return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
+                        warm_out, info, nullptr, nullptr, stats);
 }
 
 #ifdef NB_PROFILE

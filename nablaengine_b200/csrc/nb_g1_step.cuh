@@ -66,7 +66,7 @@ struct __align__(16) World {
   float con_C[MAXCON][5];               // Hessian coefficients of a contact's rows: nn, n1, 11, n2, 22
   short lim_row[NV];                    // the dof's limit row, or -1
   unsigned char con_grp[MAXCON], grp_lead[MAXCON];
-  int ngroup, pad2_;
+  int ngroup, nls, nfact, pad3_;        // groups; line-search evaluations, factorisations (work counters)
   int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
   int con_pair[MAXCON];
   unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
@@ -643,6 +643,7 @@ __device__ void collision(World& s, int lane) {
   }
   unsup = (int)__reduce_or_sync(FULL, (unsigned)unsup);
   if (lane == 0) {
+    s.ncand = ncand;
     s.ncon_raw = total;
     s.ncon = min(total, MAXCON);
     s.unsup |= unsup | (total > MAXCON ? CONTACT_OVERFLOW : 0);
@@ -1035,6 +1036,7 @@ __device__ void hessian(World& s, int lane) {
 
 // Newton from the warm start (or qacc_smooth when that costs less); returns the iterations run
 __device__ int newton(World& s, int iterations, int lane) {
+  if (lane == 0) { s.nls = 0; s.nfact = 0; }
   const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
   refresh(s, lane);
   float cost = total_cost(s, lane);
@@ -1057,6 +1059,7 @@ __device__ int newton(World& s, int iterations, int lane) {
   bool same_zones = false;  // no row changed its zone in the last step: H and its factor in s.L are still exact
   while (it < iterations) {
     if (!same_zones) {
+      if (lane == 0) s.nfact++;
       hessian(s, lane);
       PROF(s, 7);
       chol_factor(s.L, s.L, s.dinv, lane);
@@ -1097,6 +1100,7 @@ __device__ int newton(World& s, int iterations, int lane) {
       }
       if (__all_sync(FULL, nwt && z == zprev)) break;  // the Newton step kept every row on its piece: exact minimum
       if (k == 40) break;
+      if (lane == 0) s.nls++;
       fd = warp_sum(fd) + a1 + alpha * a2;
       fdd = warp_sum(fdd) + a2;
       if (k == 0) { d0 = fd; if (d0 >= 0.f) break; }
@@ -1133,7 +1137,9 @@ __device__ int newton(World& s, int iterations, int lane) {
 }
 
 // ---- one substep -------------------------------------------------------------------------------------------------
-__device__ void substep(World& s, int iterations, int lane) {
+// stats: null, or this world's 8 counters of the substep (contacts kept, rows, Newton iterations, line-search
+// evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
+__device__ void substep(World& s, int iterations, int lane, int* stats) {
   const float h = G1_TIMESTEP;
   PROF_START(s);
   kinematics(s, lane);
@@ -1158,6 +1164,10 @@ __device__ void substep(World& s, int iterations, int lane) {
   PROF_COUNT(18, s.ncon);
   PROF_COUNT(19, s.nefc);
   const int it = newton(s, iterations, lane);
+  if (stats && lane == 0) {
+    stats[0] = s.ncon; stats[1] = s.nefc; stats[2] = it; stats[3] = s.nls;
+    stats[4] = s.nfact; stats[5] = s.ncand; stats[6] = s.ncon_raw; stats[7] = 0;
+  }
   // implicitfast: (M + h kv) a_adv = M qacc; qvel += h a_adv; qpos integrated with the new qvel
   for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
   __syncwarp();

@@ -511,6 +511,7 @@ template <class T> struct Solver {
         for (int i = 0; i < NV; i++) g[i] += w.J[r][i] * w.D[r] * jar[r];
   }
   // returns the iterations run; conv: the stopping test passed
+  int ls_steps = 0;  // line-search evaluations (the FLOP counter's l)
   int solve(int iterations, T tol, bool* conv) {
     T* a = w.qacc;
     const T scale = T(1) / (T(G1_MEANINERTIA) * NV);
@@ -575,6 +576,7 @@ template <class T> struct Solver {
         }
         if (newton && z == zprev) break;  // the last Newton step kept every row on its piece: exact minimiser
         if (k == 40) break;
+        ls_steps++;
         fd += a1 + alpha * a2;
         fdd += a2;
         if (k == 0) { d0 = fd; if (d0 >= 0) break; }
@@ -602,7 +604,7 @@ template <class T> struct Solver {
   }
 };
 
-template <class T> int substep(World<T>& w, int iterations, T tol) {
+template <class T> int substep(World<T>& w, int iterations, T tol, int* stats) {
   const T h = T(G1_TIMESTEP);
   kinematics(w);
   dynamics(w);
@@ -614,6 +616,7 @@ template <class T> int substep(World<T>& w, int iterations, T tol) {
   Solver<T> sv(w);
   bool conv;
   int it = sv.solve(iterations, tol, &conv);
+  if (stats) { stats[0] = (int)w.con.size(); stats[1] = w.nrow; stats[2] = it; stats[3] = sv.ls_steps; }
   // implicitfast: (M + h kv) a_adv = M a*
   T A[NV][NV], rhs[NV], adv[NV];
   for (int i = 0; i < NV; i++) {
@@ -644,7 +647,7 @@ template <class T> int substep(World<T>& w, int iterations, T tol) {
 template <class T>
 void step_world(int iw, const double* qpos, const double* qvel, const double* warm, const double* ctrl,
                 const double* fric, const double* com, int iterations, int nsub, double tol, double* oq, double* ov,
-                double* ow, int* info) {
+                double* ow, int* info, int* stats) {
   World<T>* w = new World<T>();
   T c[NU];
   for (int i = 0; i < NQ; i++) w->qpos[i] = T(qpos[(size_t)iw * NQ + i]);
@@ -655,7 +658,7 @@ void step_world(int iw, const double* qpos, const double* qvel, const double* wa
   w->com = v3(T(com[3 * iw]), T(com[3 * iw + 1]), T(com[3 * iw + 2]));
   w->unsupported = 0;
   int it = 0;
-  for (int k = 0; k < nsub; k++) it = substep(*w, iterations, T(tol));
+  for (int k = 0; k < nsub; k++) it = substep(*w, iterations, T(tol), stats ? stats + ((size_t)iw * nsub + k) * 4 : nullptr);
   for (int i = 0; i < NQ; i++) oq[(size_t)iw * NQ + i] = double(w->qpos[i]);
   for (int i = 0; i < NV; i++) { ov[(size_t)iw * NV + i] = double(w->qvel[i]); ow[(size_t)iw * NV + i] = double(w->qacc[i]); }
   info[4 * iw] = it;
@@ -672,16 +675,18 @@ extern "C" {
 // One control step of nw worlds (row-major float64 arrays, as the C-ABI's float32 ones): nsub substeps of the
 // reference's algorithm, Newton capped at `iterations` with tolerance `tol` (the model's 1e-8 by default).
 // precision: 64 float64 arithmetic, 32 float32. nthreads: OpenMP threads (0: all).
+// stats: NULL or (nw, nsub, 4) int32 per substep: contacts kept, constraint rows, Newton iterations, line-search
+// evaluations (the inputs of the FLOP count of a step)
 int g1_oracle_step(int nw, const double* qpos, const double* qvel, const double* warm, const double* ctrl,
                    const double* fric, const double* com, int iterations, int nsub, double tol, int precision,
-                   int nthreads, double* oq, double* ov, double* ow, int* info) {
+                   int nthreads, double* oq, double* ov, double* ow, int* info, int* stats) {
   if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return 1;
 #pragma omp parallel for schedule(dynamic, 4) num_threads(nthreads > 0 ? nthreads : omp_get_max_threads())
   for (int w = 0; w < nw; w++) {
     if (precision == 32)
-      step_world<float>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info);
+      step_world<float>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info, stats);
     else
-      step_world<double>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info);
+      step_world<double>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info, stats);
   }
   return 0;
 }

@@ -50,7 +50,6 @@ __device__ unsigned long long g_prof[NPROF];
 #endif
 
 struct __align__(16) World {
-  unsigned long long con_m1[MAXCON], con_m2[MAXCON];  // dofs that move only body 1 / only body 2 of the contact
   float qpos[NQ], qvel[NV], qacc[NV], ctrl[NU], com[3], fric;
   float Q[NB][4], X[NB][3];            // body poses
   float dw[NV][3], dv[NV][3];          // dof motion about O: angular axis, velocity of the point O
@@ -58,12 +57,11 @@ struct __align__(16) World {
   float M[NTRI], L[NTRI];              // mass matrix (with armature), factor scratch
   float qsm[NV], qacc0[NV], Ma[NV], grad[NV], p[NV], Mp[NV], tmp[NV], dinv[NV + 1];
   union {
-    struct { float om[NB][3], vo[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
+    struct { float om[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
     struct { float gx[NG][3], gq[NG][4]; unsigned short cand[NP + 2]; } col;                 // collision phase
     struct { float K[21], P[KDOF][6]; unsigned char dof[KDOF]; } hs;                        // Hessian assembly
   } u;
   unsigned long long grp_mask[MAXCON];  // contacts of group g (same body pair) as bits
-  float con_C[MAXCON][5];               // Hessian coefficients of a contact's rows: nn, n1, 11, n2, 22
   short lim_row[NV];                    // the dof's limit row, or -1
   unsigned char con_grp[MAXCON], grp_lead[MAXCON];
   int ngroup, nls, nfact, pad3_;        // groups; line-search evaluations, factorisations (work counters)
@@ -72,9 +70,12 @@ struct __align__(16) World {
   unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
   float con_dist[MAXCON], con_mu[MAXCON];
   float con_fr[MAXCON][9];             // frame rows: normal, tangent 1, tangent 2
-  float con_cv[MAXCON][9];             // (pos - O) x frame row
   float con_pos[MAXCON][3];
-  union { float jd[MAXCON][3]; float wr[MAXCON][6]; } cs;  // J_d v per frame row / the contact wrench at O
+  union {  // per-contact scratch, each consumed by the phase that writes it
+    float jd[MAXCON][3];  // J_d v per frame row
+    float wr[MAXCON][6];  // the contact wrench at O (moment, force)
+    float C[MAXCON][5];   // Hessian coefficients of the contact's rows: nn, n1, 11, n2, 22 (and the group key)
+  } cs;
   float efc_D[NEFC], efc_aref[NEFC], efc_jar[NEFC], efc_jv[NEFC];
   short efc_a[NEFC];                   // dof (limit row) or contact
   signed char efc_b[NEFC];             // limit sign, or the contact row t (n + mu t1, n - mu t1, n + mu t2, ...)
@@ -119,7 +120,7 @@ __device__ __forceinline__ float sym(const float* A, int i, int j) { return j <=
 // ---- smooth dynamics ---------------------------------------------------------------------------------------------
 // Forward kinematics with velocities and the velocity-product accelerations (qacc = 0; gravity enters as the
 // base acceleration -g), one depth level at a time (lane = body).
-__device__ void kinematics(World& s, int lane) {
+__device__ __noinline__ void kinematics(World& s, int lane) {
   const int b = lane;
   const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
   if (lane == 0) {
@@ -137,17 +138,16 @@ __device__ void kinematics(World& s, int lane) {
         for (int k = 0; k < 3; k++) {
           s.X[1][k] = s.qpos[k];
           s.u.sm.om[1][k] = om[k];
-          s.u.sm.vo[1][k] = s.qvel[k];
           s.u.sm.al[1][k] = 0.f;
           s.u.sm.ao[1][k] = 0.f;
         }
         s.u.sm.ao[1][2] = -G1_GRAVITY_Z;
       } else {
         const int p = ldi(g1_body_parent + b);
-        float Qp[4], Xp[3], omp[3], vop[3], alp[3], aop[3];
+        float Qp[4], Xp[3], omp[3], alp[3], aop[3];
         for (int k = 0; k < 4; k++) Qp[k] = s.Q[p][k];
         for (int k = 0; k < 3; k++) {
-          Xp[k] = s.X[p][k]; omp[k] = s.u.sm.om[p][k]; vop[k] = s.u.sm.vo[p][k];
+          Xp[k] = s.X[p][k]; omp[k] = s.u.sm.om[p][k];
           alp[k] = s.u.sm.al[p][k]; aop[k] = s.u.sm.ao[p][k];
         }
         const float bq[4] = {ld(g1_body_quat + 4 * b), ld(g1_body_quat + 4 * b + 1), ld(g1_body_quat + 4 * b + 2),
@@ -175,7 +175,6 @@ __device__ void kinematics(World& s, int lane) {
         for (int k = 0; k < 3; k++) {
           s.X[b][k] = X[k];
           s.u.sm.om[b][k] = omp[k] + wd[k];
-          s.u.sm.vo[b][k] = vop[k] + u1[k];
           s.u.sm.al[b][k] = alp[k] + u2[k];
           s.u.sm.ao[b][k] = aop[k] + u3[k] + wr_[k];
         }
@@ -186,7 +185,7 @@ __device__ void kinematics(World& s, int lane) {
 }
 
 // the dofs' motion vectors about O = the root origin (lane = dof)
-__device__ void dof_motion(World& s, int lane) {
+__device__ __noinline__ void dof_motion(World& s, int lane) {
   const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
   for (int i = lane; i < NV; i += 32) {
     float w[3] = {0.f, 0.f, 0.f}, v[3] = {0.f, 0.f, 0.f};
@@ -210,7 +209,7 @@ __device__ void dof_motion(World& s, int lane) {
 
 // per body: the Newton-Euler wrench at O and the spatial inertia about O (lane = body), then both summed over
 // subtrees (leaves first)
-__device__ void body_terms(World& s, int lane) {
+__device__ __noinline__ void body_terms(World& s, int lane) {
   const int b = lane;
   const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
   if (b >= 1 && b < NB) {
@@ -299,7 +298,7 @@ __device__ __forceinline__ void apply_inertia(const float* J, const float* w, co
 }
 
 // mass matrix rows (lane = dof: entries with its ancestor dofs) and qfrc_smooth = clamped actuator force - bias
-__device__ void mass_and_force(World& s, int lane) {
+__device__ __noinline__ void mass_and_force(World& s, int lane) {
   for (int e = lane; e < NTRI; e += 32) s.M[e] = 0.f;
   __syncwarp();
   for (int i = lane; i < NV; i += 32) {
@@ -330,82 +329,141 @@ __device__ void mass_and_force(World& s, int lane) {
 }
 
 // ---- dense Cholesky and solves --------------------------------------------------------------------------------
-// chol_factor: A = L L' (then chol_solve: b <- A^-1 b). The factorisation runs in registers: lane l holds row l (a0) and, for
-// l < NV - 32, row l + 32 (a1), all NV entries of the symmetric row (the update of the entries above the diagonal
-// is the symmetric Schur complement, never read as L); step k scales column k by 1 / sqrt(pivot) (rsqrt refined by
-// one Newton step) and broadcasts L(j, k) from row j's lane with one shuffle per j. Every index is a compile-time
-// constant after unrolling, so nothing spills to local memory. L (packed lower, true diagonal) and 1 / diag(L) are
-// written to shared memory for the triangular solves and for later re-solves (chol_solve). A is read completely
-// before L is written, so L may alias A.
+// chol_factor: A = L L' (then chol_solve: b <- A^-1 b), left-looking (Crout) in blocks of 4 columns, in shared
+// memory, with compact code (rolled loops: a fully unrolled register factorisation is ~100 KB of instructions,
+// beyond the instruction cache). Block k0: phase 1 forms for every row i >= k0 the dot products
+// S_i^c = sum_{j<k0} L(i, j) L(c, j) for the block's columns c (lane l owns row l: its own row read once per j for
+// all four columns, rows c as broadcasts; the tail rows 32..34 split their sums over the lanes, j = lane, and reduce
+// with shuffles); phase 2 finishes the block's columns one after another with the in-block terms (row c's entries
+// from its lane by shuffle), the pivot from row c's lane, and L(i, c) = t_i / sqrt(pivot) (rsqrt refined by one
+// Newton step; the inverse also goes to dinv for the solves). A may alias L: A(i, c) is read by the lane owning row i
+// when column c is finished, just before L(i, c) replaces it.
 __device__ __forceinline__ float rsqrt_nr(float x) {
   float r = rsqrtf(x);
   return r * (1.5f - 0.5f * x * r * r);
 }
 
+constexpr int CB = 4;  // column block
+constexpr int NT = NV - 32;  // tail rows 32 .. NV - 1, finished on lanes 0 .. NT - 1
+
 __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, int lane) {
-  static_assert(NV > 32 && NV - 32 == 3, "rows 0..31 in lanes, a 3-row tail");
-  // lane l: row l of the leading 32 x 32 block (all 32 entries), the tail entries T[t] = A(32 + t, l) (column l of
-  // the 3 x 32 tail block), and the 3 x 3 trailing block C (the same on every lane)
-  float a[32], T[3], C[6];
+  static_assert(NV > 32 && NT <= CB, "block 0 holds every row beyond 32");
+  // Block k0 (columns k0 .. k0 + 3): lane l owns row r = k0 + l (rows k0 .. NV - 1 fit 32 lanes for k0 >= NT);
+  // in block 0 the rows 32 .. 34 are a second row of lanes 0 .. NT - 1 (block 0 has no phase 1)
+#pragma unroll 1
+  for (int k0 = 0; k0 < NV; k0 += CB) {
+    const int nb = min(CB, NV - k0);
+    const int r = k0 + lane;        // this lane's row (valid when < NV)
+    const int r2 = 32 + lane;       // block 0 only: the second row (lanes < NT)
+    const bool has2 = k0 == 0 && lane < NT;
+    // phase 1: S[c] = sum_{j<k0} L(r, j) L(k0 + c, j)
+    float S[CB] = {0.f, 0.f, 0.f, 0.f};
+    if (r < NV && k0 > 0) {
+      const float* Li = L + TRI(r, 0);
+      const float* L0 = L + TRI(k0, 0);
+#pragma unroll 1
+      for (int j = 0; j < k0; j++) {
+        const float lij = Li[j];
+        S[0] += lij * L0[j];
+        if (nb > 1) S[1] += lij * L0[(k0 + 1) + j];        // row k0 + 1 starts k0 + 1 entries after row k0
+        if (nb > 2) S[2] += lij * L0[(2 * k0 + 3) + j];    // row k0 + 2
+        if (nb > 3) S[3] += lij * L0[(3 * k0 + 6) + j];    // row k0 + 3
+      }
+    }
+    // phase 2: the block's columns in order; lane l keeps its row's new entries lo[c] (and the second row's, lt[c])
+    float lo[CB] = {0.f, 0.f, 0.f, 0.f}, lt[CB] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int j = 0; j < 32; j++) a[j] = j <= lane ? A[TRI(lane, j)] : A[TRI(j, lane)];
+    for (int c = 0; c < CB; c++) {
+      if (c >= nb) break;
+      const int col = k0 + c;
+      float t0 = 0.f, t1 = 0.f;
+      if (r >= col && r < NV) t0 = A[TRI(r, col)] - S[c];
+      if (has2) t1 = A[TRI(r2, col)];
 #pragma unroll
-  for (int t = 0; t < 3; t++) T[t] = A[TRI(32 + t, lane)];
-  C[0] = A[TRI(32, 32)]; C[1] = A[TRI(33, 32)]; C[2] = A[TRI(33, 33)];
-  C[3] = A[TRI(34, 32)]; C[4] = A[TRI(34, 33)]; C[5] = A[TRI(34, 34)];
-  __syncwarp();
-#pragma unroll
-  for (int k = 0; k < 32; k++) {
-    const float dkk = fmaxf(__shfl_sync(FULL, a[k], k), 1e-30f);
-    const float inv = rsqrt_nr(dkk);
-    if (lane == 0) dinv[k] = inv;
-    if (lane > k) a[k] *= inv; else if (lane == k) a[k] = dkk * inv;
-    if (lane == k) { T[0] *= inv; T[1] *= inv; T[2] *= inv; }  // tail column k: L(32 + t, k)
-    const float t0 = __shfl_sync(FULL, T[0], k), t1 = __shfl_sync(FULL, T[1], k), t2 = __shfl_sync(FULL, T[2], k);
-#pragma unroll
-    for (int j = k + 1; j < 32; j++) a[j] -= a[k] * __shfl_sync(FULL, a[k], j);
-    if (lane > k) { T[0] -= t0 * a[k]; T[1] -= t1 * a[k]; T[2] -= t2 * a[k]; }
-    C[0] -= t0 * t0; C[1] -= t1 * t0; C[2] -= t1 * t1; C[3] -= t2 * t0; C[4] -= t2 * t1; C[5] -= t2 * t2;
+      for (int m = 0; m < CB; m++) {
+        if (m >= c) break;
+        // L(col, k0 + m): row col is lane col - k0's own row, except the block-0 rows beyond 32
+        const float lcm = (col - k0) < 32 ? __shfl_sync(FULL, lo[m], col - k0) : __shfl_sync(FULL, lt[m], col - 32);
+        t0 -= lo[m] * lcm;
+        t1 -= lt[m] * lcm;
+      }
+      const float tkk = __shfl_sync(FULL, t0, c);  // row col is lane c (col - k0 < 32 always: col <= k0 + 3)
+      const float inv = rsqrt_nr(fmaxf(tkk, 1e-30f));
+      lo[c] = r > col ? t0 * inv : (r == col ? tkk * inv : 0.f);
+      lt[c] = has2 ? t1 * inv : 0.f;
+      if (r >= col && r < NV) L[TRI(r, col)] = lo[c];
+      if (has2) L[TRI(r2, col)] = lt[c];
+      if (lane == 0) dinv[col] = inv;
+    }
+    __syncwarp();
   }
-  // the 3 x 3 tail factor (every lane, redundantly)
-  const float i0 = rsqrt_nr(fmaxf(C[0], 1e-30f));
-  const float l00 = C[0] * i0, l10 = C[1] * i0, l20 = C[3] * i0;
-  const float c11 = C[2] - l10 * l10, i1 = rsqrt_nr(fmaxf(c11, 1e-30f)), l11 = c11 * i1;
-  const float l21 = (C[4] - l20 * l10) * i1;
-  const float c22 = C[5] - l20 * l20 - l21 * l21, i2 = rsqrt_nr(fmaxf(c22, 1e-30f)), l22 = c22 * i2;
-#pragma unroll
-  for (int j = 0; j < 32; j++)
-    if (j <= lane) L[TRI(lane, j)] = a[j];
-#pragma unroll
-  for (int t = 0; t < 3; t++) L[TRI(32 + t, lane)] = T[t];
-  if (lane == 0) {
-    L[TRI(32, 32)] = l00; L[TRI(33, 32)] = l10; L[TRI(33, 33)] = l11;
-    L[TRI(34, 32)] = l20; L[TRI(34, 33)] = l21; L[TRI(34, 34)] = l22;
-    dinv[32] = i0; dinv[33] = i1; dinv[34] = i2;
-  }
-  __syncwarp();
 }
 
-// b <- (L L')^-1 b with the factor L and dinv = 1 / diag(L) in shared memory; lane l keeps entries l, l + 32 in
-// registers; the forward pass reads column k (L(lane, k): distinct banks for the 32 lanes), the backward pass row k
-__device__ void chol_solve(const float* L, const float* dinv, float* b, int lane) {
+// b <- (L L')^-1 b with the factor L and dinv = 1 / diag(L) in shared memory; lane l keeps entries l and l + 32 in
+// registers. Both substitutions go in blocks of 4: the block's 4 unknowns are solved redundantly on every lane from
+// the block's diagonal entries (broadcast loads) and their current values (shuffles), then every other entry is
+// updated with the block's 4 columns (forward: L(i, block), backward: L(block, i), read as rows)
+__device__ __noinline__ void chol_solve(const float* L, const float* dinv, float* b, int lane) {
   float y0 = b[lane], y1 = lane + 32 < NV ? b[lane + 32] : 0.f;
   __syncwarp();
-#pragma unroll 5
-  for (int k = 0; k < NV; k++) {
-    const float yk = __shfl_sync(FULL, k < 32 ? y0 : y1, k & 31) * dinv[k];
-    if (lane == k) y0 = yk;
-    else if (lane > k) y0 -= L[TRI(lane, k)] * yk;
-    if (lane + 32 == k) y1 = yk;
-    else if (lane + 32 > k && lane + 32 < NV) y1 -= L[TRI(lane + 32, k)] * yk;
+#pragma unroll 1
+  for (int k0 = 0; k0 < NV; k0 += CB) {
+    const int nb = min(CB, NV - k0);
+    float x[CB];
+#pragma unroll
+    for (int c = 0; c < CB; c++) {
+      const int r = k0 + c;
+      x[c] = c < nb ? __shfl_sync(FULL, r < 32 ? y0 : y1, r & 31) : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < CB; c++) {
+      if (c >= nb) break;
+      const int r = k0 + c;
+      float v = x[c];
+#pragma unroll
+      for (int m = 0; m < CB; m++)
+        if (m < c) v -= L[TRI(r, k0 + m)] * x[m];
+      x[c] = v * dinv[r];
+    }
+#pragma unroll
+    for (int c = 0; c < CB; c++) {
+      if (c >= nb) break;
+      const int r = k0 + c;
+      if (lane == r) y0 = x[c];
+      if (lane + 32 == r) y1 = x[c];
+      if (lane > k0 + nb - 1) y0 -= L[TRI(lane, r)] * x[c];
+      if (lane + 32 < NV && lane + 32 > k0 + nb - 1) y1 -= L[TRI(lane + 32, r)] * x[c];
+    }
   }
-#pragma unroll 5
-  for (int k = NV - 1; k >= 0; k--) {
-    const float xk = __shfl_sync(FULL, k < 32 ? y0 : y1, k & 31) * dinv[k];
-    if (lane == k) y0 = xk;
-    else if (lane < k) y0 -= L[TRI(k, lane)] * xk;
-    if (lane + 32 == k) y1 = xk;
-    else if (lane + 32 < k) y1 -= L[TRI(k, lane + 32)] * xk;
+  const int last = ((NV - 1) / CB) * CB;
+#pragma unroll 1
+  for (int k0 = last; k0 >= 0; k0 -= CB) {
+    const int nb = min(CB, NV - k0);
+    float x[CB];
+#pragma unroll
+    for (int c = 0; c < CB; c++) {
+      const int r = k0 + c;
+      x[c] = c < nb ? __shfl_sync(FULL, r < 32 ? y0 : y1, r & 31) : 0.f;
+    }
+#pragma unroll
+    for (int c = CB - 1; c >= 0; c--) {
+      if (c >= nb) continue;
+      const int r = k0 + c;
+      float v = x[c];
+#pragma unroll
+      for (int m = 0; m < CB; m++)
+        if (m > c && m < nb) v -= L[TRI(k0 + m, r)] * x[m];
+      x[c] = v * dinv[r];
+    }
+#pragma unroll
+    for (int c = 0; c < CB; c++) {
+      if (c >= nb) break;
+      const int r = k0 + c;
+      if (lane == r) y0 = x[c];
+      if (lane + 32 == r) y1 = x[c];
+      if (lane < k0) y0 -= L[TRI(r, lane)] * x[c];
+      if (lane + 32 < k0) y1 -= L[TRI(r, lane + 32)] * x[c];
+    }
   }
   b[lane] = y0;
   if (lane + 32 < NV) b[lane + 32] = y1;
@@ -413,10 +471,10 @@ __device__ void chol_solve(const float* L, const float* dinv, float* b, int lane
 }
 
 // out = A v (A symmetric, packed)
-__device__ void matvec(const float* A, const float* v, float* out, int lane) {
+__device__ __noinline__ void matvec(const float* A, const float* v, float* out, int lane) {
   for (int i = lane; i < NV; i += 32) {
     float a0 = 0.f, a1 = 0.f;
-#pragma unroll
+#pragma unroll 6
     for (int j = 0; j < NV; j += 2) {
       a0 += sym(A, i, j) * v[j];
       if (j + 1 < NV) a1 += sym(A, i, j + 1) * v[j + 1];
@@ -424,6 +482,14 @@ __device__ void matvec(const float* A, const float* v, float* out, int lane) {
     out[i] = a0 + a1;
   }
   __syncwarp();
+}
+
+// the dofs that move only body 1 (m1, Jacobian sign -1) / only body 2 (m2, sign +1) of contact pair pr
+__device__ __forceinline__ void pair_masks(int pr, unsigned long long* m1, unsigned long long* m2) {
+  const unsigned long long a = g1_body_dofmask[ldi(g1_geom_body + ldi(g1_pair_g1 + pr))];
+  const unsigned long long b = g1_body_dofmask[ldi(g1_geom_body + ldi(g1_pair_g2 + pr))];
+  *m1 = a & ~b;
+  *m2 = b & ~a;
 }
 
 // ---- collision ---------------------------------------------------------------------------------------------------
@@ -470,7 +536,7 @@ __device__ __forceinline__ bool bounding(const World& s, int pr) {
 
 // Narrow phase of candidate pair pr: returns the number of contacts (0..2, dist < 0) and, when write is set,
 // stores them at contact slots base, base + 1 (those below MAXCON). MuJoCo Warp's primitives at margin 0.
-__device__ int collide(World& s, int pr, bool write, int base, int* unsup) {
+__device__ __noinline__ int collide(World& s, int pr, bool write, int base, int* unsup) {
   const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
   const int t1 = ldi(g1_geom_type + g1), t2 = ldi(g1_geom_type + g2);
   float p1[3], p2[3];
@@ -605,7 +671,7 @@ __device__ int collide(World& s, int pr, bool write, int base, int* unsup) {
 
 // geom poses, broad phase (ballot-compacted candidates in pair order), narrow phase in two passes (count, prefix
 // sum over the warp, write): contacts in pair order, deterministic
-__device__ void collision(World& s, int lane) {
+__device__ __noinline__ void collision(World& s, int lane) {
   for (int g = lane; g < NG; g += 32) {
     const int b = ldi(g1_geom_body + g);
     const float gp[3] = {ld(g1_geom_pos + 3 * g), ld(g1_geom_pos + 3 * g + 1), ld(g1_geom_pos + 3 * g + 2)};
@@ -655,21 +721,18 @@ __device__ void collision(World& s, int lane) {
 // the contacts between the same two bodies (in contact order, numbered by their first contact), which share the
 // support and the sign of every Jacobian column, so the Hessian and J' f treat a group as one spatial stiffness /
 // one wrench
-__device__ void contact_setup(World& s, int lane) {
+__device__ __noinline__ void contact_setup(World& s, int lane) {
   const int ncon = s.ncon;
   const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  __syncwarp();
   for (int c = lane; c < ncon; c += 32) {
     const int pr = s.con_pair[c];
     // condim 1 (frictionless) contacts: mu = 0 makes the pyramid formulas below reduce to the normal row
     s.con_mu[c] = ldi(g1_pair_dim + pr) != 3 ? 0.f : (ldi(g1_pair_foot + pr) ? s.fric : ld(g1_pair_mu + pr));
-    const float r[3] = {s.con_pos[c][0] - O[0], s.con_pos[c][1] - O[1], s.con_pos[c][2] - O[2]};
-    for (int d = 0; d < 3; d++) cross(r, s.con_fr[c] + 3 * d, s.con_cv[c] + 3 * d);
-    const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
-    const unsigned long long m1 = g1_body_dofmask[b1], m2 = g1_body_dofmask[b2];
-    s.con_m1[c] = m1 & ~m2;
-    s.con_m2[c] = m2 & ~m1;
+    // the contact point relative to O (the frame rows' moments are (pos - O) x row)
+    for (int k = 0; k < 3; k++) s.con_pos[c][k] -= O[k];
   }
-  // group leaders: the first contact of each (body1, body2); the key is kept in con_C[c][0] for a moment
+  // group leaders: the first contact of each (body1, body2); the key is kept in cs.C[c][0] for a moment
   int ngroup = 0;
   for (int c0 = 0; c0 < ncon; c0 += 32) {
     const int c = c0 + lane;
@@ -678,14 +741,14 @@ __device__ void contact_setup(World& s, int lane) {
       const int pr = s.con_pair[c];
       key = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)) * 32 + ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
       for (int e = 0; e < c0; e++)  // an earlier chunk (only past 32 contacts)
-        if (__float_as_int(s.con_C[e][0]) == key) { lead = e; break; }
+        if (__float_as_int(s.cs.C[e][0]) == key) { lead = e; break; }
     }
     const unsigned same = __match_any_sync(FULL, key);
     if (lead == c) lead = c0 + __ffs(same) - 1;
     const bool leader = c < ncon && lead == c;
     const unsigned bal = __ballot_sync(FULL, leader);
     if (c < ncon) {
-      s.con_C[c][0] = __int_as_float(key);
+      s.cs.C[c][0] = __int_as_float(key);
       s.grp_lead[c] = (unsigned char)lead;
       if (leader) s.con_grp[c] = (unsigned char)(ngroup + __popc(bal & ((1u << lane) - 1u)));
     }
@@ -706,7 +769,7 @@ __device__ void contact_setup(World& s, int lane) {
 
 // ---- constraint rows -----------------------------------------------------------------------------------------------
 // body spatial motion at O for the generalised vector v (lane = body: a sum over its ancestor dofs)
-__device__ void body_motion(World& s, const float* v, int lane) {
+__device__ __noinline__ void body_motion(World& s, const float* v, int lane) {
   if (lane < NB) {
     float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     unsigned long long m = g1_body_dofmask[lane];
@@ -722,20 +785,23 @@ __device__ void body_motion(World& s, const float* v, int lane) {
 }
 
 // J_d v of every contact's frame rows (after body_motion(v))
-__device__ void contact_jv(World& s, int lane) {
+__device__ __noinline__ void contact_jv(World& s, int lane) {
   const int ncon = s.ncon;
   for (int c = lane; c < ncon; c += 32) {
     const int pr = s.con_pair[c];
     const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
-    float dV[6];
+    float dV[6], u[3];
     for (int k = 0; k < 6; k++) dV[k] = s.BV[b2][k] - s.BV[b1][k];
-    for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(s.con_fr[c] + 3 * d, dV + 3) + dot3(s.con_cv[c] + 3 * d, dV);
+    // the relative velocity at the contact point: v_O + w x (pos - O); frame row d: row . that
+    cross(dV, s.con_pos[c], u);
+    for (int k = 0; k < 3; k++) u[k] += dV[3 + k];
+    for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(s.con_fr[c] + 3 * d, u);
   }
   __syncwarp();
 }
 
 // J v of every row into out (contact rows from cs.jd, limit rows from v)
-__device__ void rows_jv(World& s, const float* v, float* out, int lane) {
+__device__ __noinline__ void rows_jv(World& s, const float* v, float* out, int lane) {
   body_motion(s, v, lane);
   contact_jv(s, lane);
   const int nefc = s.nefc;
@@ -751,27 +817,25 @@ __device__ void rows_jv(World& s, const float* v, float* out, int lane) {
 }
 
 // refsafe impedance at the row position pos: stiffness k, damping b, impedance imp (solimp power 2 folded)
-__device__ __forceinline__ void impedance(const float* solref, const float* solimp, float pos, float h, float* k,
+__device__ __noinline__ void impedance(const float* solref, const float* solimp, float pos, float h, float* k,
                                           float* b, float* imp) {
   const float tc = fmaxf(solref[0], 2.f * h), dr = solref[1];
   const float dmin = fminf(fmaxf(solimp[0], 1e-4f), 0.9999f), dmax = fminf(fmaxf(solimp[1], 1e-4f), 0.9999f);
   const float width = fmaxf(1e-15f, solimp[2]), mid = fminf(fmaxf(solimp[3], 1e-4f), 0.9999f);
-  const float power = fmaxf(1.f, solimp[4]);
   *k = 1.f / fmaxf(1e-15f, dmax * dmax * tc * tc * dr * dr);
   *b = 2.f / fmaxf(1e-15f, dmax * tc);
   const float x = fabsf(pos) / width;
   if (x >= 1.f) *imp = dmax;
   else if (x <= 0.f) *imp = dmin;
   else {
-    float y;
-    if (power == 2.f) y = x <= mid ? x * x / mid : 1.f - (1.f - x) * (1.f - x) / (1.f - mid);
-    else y = x <= mid ? powf(x, power) / powf(mid, power - 1.f) : 1.f - powf(1.f - x, power) / powf(1.f - mid, power - 1.f);
+    // solimp power 2 on every row of the model (the generator checks it): x^2 / mid, 1 - (1 - x)^2 / (1 - mid)
+    const float y = x <= mid ? x * x / mid : 1.f - (1.f - x) * (1.f - x) / (1.f - mid);
     *imp = fminf(fmaxf(dmin + y * (dmax - dmin), dmin), dmax);
   }
 }
 
 // constraint rows: hinge limits (dof order), then per contact 4 pyramid rows (condim 3) or 1 normal row
-__device__ void make_rows(World& s, int lane) {
+__device__ __noinline__ void make_rows(World& s, int lane) {
   const float h = G1_TIMESTEP;
   const unsigned below = (1u << lane) - 1u;
   for (int i = lane; i < NV; i += 32) s.lim_row[i] = -1;
@@ -859,14 +923,14 @@ __device__ void make_rows(World& s, int lane) {
 
 // ---- Newton solver -------------------------------------------------------------------------------------------------
 // Ma = M a and jar = J a - aref at the current qacc
-__device__ void refresh(World& s, int lane) {
+__device__ __noinline__ void refresh(World& s, int lane) {
   matvec(s.M, s.qacc, s.Ma, lane);
   rows_jv(s, s.qacc, s.efc_jar, lane);
   for (int r = lane; r < s.nefc; r += 32) s.efc_jar[r] -= s.efc_aref[r];
   __syncwarp();
 }
 
-__device__ float total_cost(World& s, int lane) {
+__device__ __noinline__ float total_cost(World& s, int lane) {
   float g = 0.f;
   for (int i = lane; i < NV; i += 32) g += 0.5f * (s.Ma[i] - s.qsm[i]) * (s.qacc[i] - s.qacc0[i]);
   for (int r = lane; r < s.nefc; r += 32) {
@@ -879,7 +943,7 @@ __device__ float total_cost(World& s, int lane) {
 // grad = M qacc - qfrc_smooth - J' f with f = -D jar on the active rows; returns |grad|. J' f: each contact's
 // wrench at O from its rows' forces, summed per group (members in contact order), then per dof the groups whose
 // support holds it (sign +1 on body 2's chain, -1 on body 1's) and the dof's limit row
-__device__ float newton_grad(World& s, int lane) {
+__device__ __noinline__ float newton_grad(World& s, int lane) {
   const int ncon = s.ncon, ngroup = s.ngroup;
   for (int c = lane; c < ncon; c += 32) {
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
@@ -892,7 +956,8 @@ __device__ float newton_grad(World& s, int lane) {
     const float F[3] = {f[0] + f[1] + f[2] + f[3], mu * (f[0] - f[1]), mu * (f[2] - f[3])};
     float w[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int d = 0; d < 3; d++)
-      for (int k = 0; k < 3; k++) { w[k] += F[d] * s.con_cv[c][3 * d + k]; w[3 + k] += F[d] * s.con_fr[c][3 * d + k]; }
+      for (int k = 0; k < 3; k++) w[3 + k] += F[d] * s.con_fr[c][3 * d + k];
+    cross(s.con_pos[c], w + 3, w);  // moment about O: (pos - O) x force
     for (int k = 0; k < 6; k++) s.cs.wr[c][k] = w[k];
   }
   __syncwarp();
@@ -925,7 +990,9 @@ __device__ float newton_grad(World& s, int lane) {
     const unsigned long long bit = 1ull << i;
     for (int g = 0; g < ngroup; g++) {
       const int c = __ffsll((long long)s.grp_mask[g]) - 1;
-      const float sg = (s.con_m2[c] & bit) ? 1.f : ((s.con_m1[c] & bit) ? -1.f : 0.f);
+      unsigned long long m1, m2;
+      pair_masks(s.con_pair[c], &m1, &m2);
+      const float sg = (m2 & bit) ? 1.f : ((m1 & bit) ? -1.f : 0.f);
       if (sg != 0.f) jtf += sg * (dot3(w, s.cs.wr[c]) + dot3(v, s.cs.wr[c] + 3));
     }
     const float g = s.Ma[i] - s.qsm[i] - jtf;
@@ -940,7 +1007,7 @@ __device__ float newton_grad(World& s, int lane) {
 // frame rows and C the 3 x 3 sum of D u u' over its quadratic pyramid rows u = n +- mu t_k; J_f = G S with G the
 // 3 x 6 rows (moment, frame) and S the dofs' motion vectors, so a group of contacts adds S' K S with the 6 x 6
 // spatial stiffness K = sum G' C G, on the group's support with the columns' signs
-__device__ void hessian(World& s, int lane) {
+__device__ __noinline__ void hessian(World& s, int lane) {
   const int ncon = s.ncon, ngroup = s.ngroup;
   for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
   for (int c = lane; c < ncon; c += 32) {
@@ -948,11 +1015,11 @@ __device__ void hessian(World& s, int lane) {
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     for (int t = 0; t < nr; t++) d[t] = s.efc_jar[r0 + t] < 0.f ? s.efc_D[r0 + t] : 0.f;
     const float mu = s.con_mu[c];
-    s.con_C[c][0] = d[0] + d[1] + d[2] + d[3];
-    s.con_C[c][1] = mu * (d[0] - d[1]);
-    s.con_C[c][2] = mu * mu * (d[0] + d[1]);
-    s.con_C[c][3] = mu * (d[2] - d[3]);
-    s.con_C[c][4] = mu * mu * (d[2] + d[3]);
+    s.cs.C[c][0] = d[0] + d[1] + d[2] + d[3];
+    s.cs.C[c][1] = mu * (d[0] - d[1]);
+    s.cs.C[c][2] = mu * mu * (d[0] + d[1]);
+    s.cs.C[c][3] = mu * (d[2] - d[3]);
+    s.cs.C[c][4] = mu * mu * (d[2] + d[3]);
   }
   __syncwarp();
   for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
@@ -970,12 +1037,15 @@ __device__ void hessian(World& s, int lane) {
       while (m) {
         const int c = __ffsll((long long)m) - 1;
         m &= m - 1ull;
-        const float* C = s.con_C[c];
+        const float* C = s.cs.C[c];
         if (C[0] == 0.f) continue;
+        // G rows (moment (pos - O) x row, row) at components e1 and e2
+        const float* r = s.con_pos[c];
         float x[3], y[3];
         for (int dd = 0; dd < 3; dd++) {
-          x[dd] = e1 < 3 ? s.con_cv[c][3 * dd + e1] : s.con_fr[c][3 * dd + e1 - 3];
-          y[dd] = e2 < 3 ? s.con_cv[c][3 * dd + e2] : s.con_fr[c][3 * dd + e2 - 3];
+          const float* f = s.con_fr[c] + 3 * dd;
+          x[dd] = e1 < 3 ? r[(e1 + 1) % 3] * f[(e1 + 2) % 3] - r[(e1 + 2) % 3] * f[(e1 + 1) % 3] : f[e1 - 3];
+          y[dd] = e2 < 3 ? r[(e2 + 1) % 3] * f[(e2 + 2) % 3] - r[(e2 + 2) % 3] * f[(e2 + 1) % 3] : f[e2 - 3];
         }
         acc += C[0] * x[0] * y[0] + C[1] * (x[0] * y[1] + x[1] * y[0]) + C[2] * x[1] * y[1]
                + C[3] * (x[0] * y[2] + x[2] * y[0]) + C[4] * x[2] * y[2];
@@ -984,7 +1054,9 @@ __device__ void hessian(World& s, int lane) {
     }
     __syncwarp();
     const int lead = __ffsll((long long)gm) - 1;
-    const unsigned long long m1 = s.con_m1[lead], m2 = s.con_m2[lead], sup = m1 | m2;
+    unsigned long long m1, m2;
+    pair_masks(s.con_pair[lead], &m1, &m2);
+    const unsigned long long sup = m1 | m2;
     bool any = false;
     for (int e = 0; e < 21; e++) any |= s.u.hs.K[e] != 0.f;
     __syncwarp();
@@ -1035,7 +1107,7 @@ __device__ void hessian(World& s, int lane) {
 }
 
 // Newton from the warm start (or qacc_smooth when that costs less); returns the iterations run
-__device__ int newton(World& s, int iterations, int lane) {
+__device__ __noinline__ int newton(World& s, int iterations, int lane) {
   if (lane == 0) { s.nls = 0; s.nfact = 0; }
   const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
   refresh(s, lane);

@@ -288,6 +288,7 @@ def main():
     assert (m["pair_solref"] == m["pair_solref"][0]).all() and (m["pair_solimp"] == m["pair_solimp"][0]).all()
     assert (m["jnt_solref"][1:] == m["jnt_solref"][1]).all() and (m["jnt_solimp"][1:] == m["jnt_solimp"][1]).all()
     assert not m["dof_frictionloss"].any() and not m["dof_damping"].any() and not m["jnt_margin"].any()
+    assert m["pair_solimp"][0][4] == 2.0 and m["jnt_solimp"][1][4] == 2.0  # the kernels fold the power-2 impedance
     out = {k: v for k, v in m.items() if isinstance(v, np.ndarray)}
     out.update({k: np.asarray(v) for k, v in d.items()})
     for k in ("body_names", "joint_names", "geom_names"):

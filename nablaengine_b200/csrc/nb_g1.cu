@@ -7,7 +7,16 @@
 
 namespace nbg1 {
 
-constexpr int WPB = 2;  // worlds (warps) per block
+#ifndef NB_WPB
+#define NB_WPB 5
+#endif
+#ifndef NB_LOCKSTEP
+#define NB_LOCKSTEP 1
+#endif
+constexpr int WPB = NB_WPB;  // worlds (warps) per block
+// NB_LOCKSTEP: the worlds of a block run their Newton iterations in lockstep (a block barrier per iteration): the
+// warps of an SM then fetch the same instructions at the same time, instead of each streaming the ~50 KB Newton loop
+// from its own position (the kernel is bound by instruction fetch otherwise)
 constexpr int TAPE_WORDS = 0;
 constexpr long long ABI_VERSION = 1;
 
@@ -21,16 +30,32 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * WPB + warp;
+#if !NB_LOCKSTEP
   if (w >= nw) return;  // whole warps leave; the block has no block-wide barrier
+#endif
+  const bool active = w < nw;  // (lockstep: inactive warps stay for the barriers)
   World& s = reinterpret_cast<World*>(smem)[warp];
-  const size_t w64 = (size_t)w;
+  const size_t w64 = (size_t)(active ? w : 0);
   for (int i = lane; i < NQ; i += 32) s.qpos[i] = qpos[w64 * NQ + i];
   for (int i = lane; i < NV; i += 32) { s.qvel[i] = qvel[w64 * NV + i]; s.qacc[i] = warm[w64 * NV + i]; }
   for (int i = lane; i < NU; i += 32) s.ctrl[i] = ctrl[w64 * NU + i];
   if (lane < 3) s.com[lane] = com[w64 * 3 + lane];
   if (lane == 0) { s.fric = fric[w]; s.unsup = 0; s.nit = 0; }
   __syncwarp();
-  for (int k = 0; k < nsub; k++) substep(s, iterations, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr);
+  for (int k = 0; k < nsub; k++) {
+    if (active) substep_pre(s, lane);
+    while (true) {
+      const bool done = !active || s.ndone || s.nit_cur >= iterations;
+#if NB_LOCKSTEP
+      if (__syncthreads_and(done)) break;
+#else
+      if (done) break;
+#endif
+      if (!done) newton_iter(s, lane);
+    }
+    if (active) substep_post(s, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr);
+  }
+  if (!active) return;
   for (int i = lane; i < NQ; i += 32) oq[w64 * NQ + i] = s.qpos[i];
   for (int i = lane; i < NV; i += 32) { ov[w64 * NV + i] = s.qvel[i]; ow[w64 * NV + i] = s.qacc[i]; }
   if (lane == 0) {
@@ -58,6 +83,9 @@ static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
 }  // namespace nbg1
 
 using namespace nbg1;
+#ifdef NB_PROFILE
+static size_t g_prof_smem = 0;  // profile builds: a larger dynamic shared-memory size per block (lower occupancy)
+#endif
 
 extern "C" {
 
@@ -85,7 +113,13 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
   if (!qpos || !qvel || !warm || !ctrl || !friction || !com || !qpos_out || !qvel_out || !warm_out || !info)
     return (int)cudaErrorInvalidValue;
   const int blocks = (nw + WPB - 1) / WPB;
-  k_forward<<<blocks, WPB * 32, SMEM, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
+#ifdef NB_PROFILE
+  const size_t smem = g_prof_smem > SMEM ? g_prof_smem : SMEM;
+  if (smem != SMEM) cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+#else
+  const size_t smem = SMEM;
+#endif
+  k_forward<<<blocks, WPB * 32, smem, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
                                                 qvel_out, warm_out, info, ocon, stats);
   return (int)cudaGetLastError();
 }
@@ -108,6 +142,10 @@ int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const fl
 
 #ifdef NB_PROFILE
 // profile builds only: read and clear the phase counters (not part of the product ABI)
+int nb_g1_profile_set_smem(long long bytes) {
+  g_prof_smem = (size_t)bytes;
+  return 0;
+}
 int nb_g1_profile_read(unsigned long long* out, int n) {
   unsigned long long h[NPROF] = {};
   cudaError_t e = cudaMemcpyFromSymbol(h, g_prof, sizeof(h));

@@ -26,6 +26,7 @@ namespace nbg1 {
 
 constexpr int NQ = G1_NQ, NV = G1_NV, NU = G1_NU, NB = G1_NBODY, NG = G1_NGEOM, NP = G1_NPAIR;
 constexpr int MAXCON = 64, NEFC = 192, KDOF = 16, MAXD = G1_MAXDEPTH;
+static_assert(G1_NV == G1_NBODY + 4, "dof d >= 6 is the hinge of body d - 4 (one hinge per body after the root)");
 constexpr int NTRI = NV * (NV + 1) / 2;
 constexpr unsigned FULL = 0xffffffffu;
 constexpr int ROWS_PER_LANE = (NEFC + 31) / 32;
@@ -65,6 +66,8 @@ struct __align__(16) World {
   short lim_row[NV];                    // the dof's limit row, or -1
   unsigned char con_grp[MAXCON], grp_lead[MAXCON];
   int ngroup, nls, nfact, pad3_;        // groups; line-search evaluations, factorisations (work counters)
+  float ncost;                          // Newton state between iterations: cost, iterations, converged, same zones
+  int nit_cur, ndone, nsame;
   int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
   int con_pair[MAXCON];
   unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
@@ -471,16 +474,28 @@ __device__ __noinline__ void chol_solve(const float* L, const float* dinv, float
 }
 
 // out = A v (A symmetric, packed)
+// (rows 0..31: one row per lane over all 35 columns; rows 32..34: split over the lanes, column j = lane, with the
+// 3 x 3 tail block on lanes 0..2, and warp reductions)
 __device__ __noinline__ void matvec(const float* A, const float* v, float* out, int lane) {
-  for (int i = lane; i < NV; i += 32) {
-    float a0 = 0.f, a1 = 0.f;
+  float a0 = 0.f, a1 = 0.f;
 #pragma unroll 6
-    for (int j = 0; j < NV; j += 2) {
-      a0 += sym(A, i, j) * v[j];
-      if (j + 1 < NV) a1 += sym(A, i, j + 1) * v[j + 1];
-    }
-    out[i] = a0 + a1;
+  for (int j = 0; j < NV - 1; j += 2) {
+    a0 += sym(A, lane, j) * v[j];
+    a1 += sym(A, lane, j + 1) * v[j + 1];
   }
+  if (NV & 1) a0 += A[TRI(NV - 1, lane)] * v[NV - 1];
+  float t[NT];
+#pragma unroll
+  for (int m = 0; m < NT; m++) {
+    t[m] = A[TRI(32 + m, lane)] * v[lane];
+    if (lane < NT) t[m] += sym(A, 32 + m, 32 + lane) * v[32 + lane];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int m = 0; m < NT; m++) t[m] += __shfl_xor_sync(FULL, t[m], o);
+  out[lane] = a0 + a1;
+  if (lane < NT) out[32 + lane] = lane == 0 ? t[0] : (lane == 1 ? t[1] : t[2]);
   __syncwarp();
 }
 
@@ -770,17 +785,31 @@ __device__ __noinline__ void contact_setup(World& s, int lane) {
 // ---- constraint rows -----------------------------------------------------------------------------------------------
 // body spatial motion at O for the generalised vector v (lane = body: a sum over its ancestor dofs)
 __device__ __noinline__ void body_motion(World& s, const float* v, int lane) {
-  if (lane < NB) {
-    float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    unsigned long long m = g1_body_dofmask[lane];
-    while (m) {
-      const int i = __ffsll((long long)m) - 1;
-      m &= m - 1ull;
-      const float vi = v[i];
-      for (int k = 0; k < 3; k++) { a[k] += vi * s.dw[i][k]; a[3 + k] += vi * s.dv[i][k]; }
+  // own contribution of body b (lane): its hinge's v_d (dw, dv); the root: its 6 dofs (translations e_k, rotations
+  // about O); then the sums over the ancestors by pointer jumping (ceil(log2(depth + 1)) = 4 rounds: add the value
+  // held by the current ancestor pointer, then jump the pointer; the world body holds 0 and points to itself)
+  static_assert(MAXD < 16, "4 pointer-jumping rounds");
+  float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int par = 0;
+  if (lane == 1) {
+    for (int k = 0; k < 3; k++) {
+      a[3 + k] = v[k];
+      a[k] = v[3] * s.dw[3][k] + v[4] * s.dw[4][k] + v[5] * s.dw[5][k];
     }
-    for (int k = 0; k < 6; k++) s.BV[lane][k] = a[k];
+  } else if (lane >= 2 && lane < NB) {
+    const int d = lane + 4;  // the hinge dof of body b >= 2 (dofs in body order)
+    const float vd = v[d];
+    for (int k = 0; k < 3; k++) { a[k] = vd * s.dw[d][k]; a[3 + k] = vd * s.dv[d][k]; }
+    par = ldi(g1_body_parent + lane);
   }
+#pragma unroll
+  for (int round = 0; round < 4; round++) {
+#pragma unroll
+    for (int k = 0; k < 6; k++) a[k] += __shfl_sync(FULL, a[k], par);
+    par = __shfl_sync(FULL, par, par);
+  }
+  if (lane < NB)
+    for (int k = 0; k < 6; k++) s.BV[lane][k] = a[k];
   __syncwarp();
 }
 
@@ -943,7 +972,7 @@ __device__ __noinline__ float total_cost(World& s, int lane) {
 // grad = M qacc - qfrc_smooth - J' f with f = -D jar on the active rows; returns |grad|. J' f: each contact's
 // wrench at O from its rows' forces, summed per group (members in contact order), then per dof the groups whose
 // support holds it (sign +1 on body 2's chain, -1 on body 1's) and the dof's limit row
-__device__ __noinline__ float newton_grad(World& s, int lane) {
+__device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   const int ncon = s.ncon, ngroup = s.ngroup;
   for (int c = lane; c < ncon; c += 32) {
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
@@ -978,29 +1007,42 @@ __device__ __noinline__ float newton_grad(World& s, int lane) {
     if (on) s.cs.wr[__ffsll((long long)s.grp_mask[g]) - 1][e] = acc;
     __syncwarp();
   }
-  float gn = 0.f;
-  for (int i = lane; i < NV; i += 32) {
-    float jtf = 0.f;
-    const int lr = s.lim_row[i];
-    if (lr >= 0) {
-      const float x = s.efc_jar[lr];
-      if (x < 0.f) jtf = s.efc_b[lr] * (-s.efc_D[lr] * x);
-    }
-    const float w[3] = {s.dw[i][0], s.dw[i][1], s.dw[i][2]}, v[3] = {s.dv[i][0], s.dv[i][1], s.dv[i][2]};
-    const unsigned long long bit = 1ull << i;
-    for (int g = 0; g < ngroup; g++) {
-      const int c = __ffsll((long long)s.grp_mask[g]) - 1;
-      unsigned long long m1, m2;
-      pair_masks(s.con_pair[c], &m1, &m2);
-      const float sg = (m2 & bit) ? 1.f : ((m1 & bit) ? -1.f : 0.f);
-      if (sg != 0.f) jtf += sg * (dot3(w, s.cs.wr[c]) + dot3(v, s.cs.wr[c] + 3));
-    }
-    const float g = s.Ma[i] - s.qsm[i] - jtf;
-    s.grad[i] = g;
-    gn += g * g;
+  // lane l: dof 3 + l (dofs 3..34 in one pass); dofs 0..2 (the root translations, motion e_k) get the linear force
+  // of the groups whose support holds them (every lane accumulates those three sums)
+  const int i = lane + 3;
+  float jtf = 0.f, ft[3] = {0.f, 0.f, 0.f};
+  const int lr = s.lim_row[i];
+  if (lr >= 0) {
+    const float x = s.efc_jar[lr];
+    if (x < 0.f) jtf = s.efc_b[lr] * (-s.efc_D[lr] * x);
+  }
+  const float w[3] = {s.dw[i][0], s.dw[i][1], s.dw[i][2]}, v[3] = {s.dv[i][0], s.dv[i][1], s.dv[i][2]};
+  const unsigned long long bit = 1ull << i;
+  for (int g = 0; g < ngroup; g++) {
+    const int c = __ffsll((long long)s.grp_mask[g]) - 1;
+    unsigned long long m1, m2;
+    pair_masks(s.con_pair[c], &m1, &m2);
+    const float* W = s.cs.wr[c];
+    const float sg = (m2 & bit) ? 1.f : ((m1 & bit) ? -1.f : 0.f);
+    if (sg != 0.f) jtf += sg * (dot3(w, W) + dot3(v, W + 3));
+    const float st = (m2 & 1ull) ? 1.f : ((m1 & 1ull) ? -1.f : 0.f);  // the root dofs: all on a chain or none
+    for (int k = 0; k < 3; k++) ft[k] += st * W[3 + k];
+  }
+  const float g = s.Ma[i] - s.qsm[i] - jtf;
+  s.grad[i] = g;
+  float gn = g * g;
+  if (lane < 3) {
+    const float g0 = s.Ma[lane] - s.qsm[lane] - (lane == 0 ? ft[0] : (lane == 1 ? ft[1] : ft[2]));
+    s.grad[lane] = g0;
+    gn += g0 * g0;
   }
   __syncwarp();
-  return sqrtf(warp_sum(gn));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {  // |grad|^2 and the caller's sum (the new cost), one butterfly
+    gn += __shfl_xor_sync(FULL, gn, o);
+    extra += __shfl_xor_sync(FULL, extra, o);
+  }
+  return make_float2(sqrtf(gn), extra);
 }
 
 // H = M + J' D J over the quadratic rows, into s.L (lower triangle). A contact's rows add J_f' C J_f with J_f its
@@ -1062,11 +1104,13 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     __syncwarp();
     if (!any) continue;  // (uniform) no quadratic row in the group
     const int nsup = __popcll(sup);
-    // P_k = K s_i for the support dofs i (rank k), signed
-    for (int h = 0; h < 2; h++) {
-      const int i = lane + 32 * h;
-      if (i < NV && ((sup >> i) & 1ull)) {
-        const int k = __popcll(sup & ((1ull << i) - 1ull));
+    // P_k = K s_i for the support dofs i (rank k: the k-th set bit of the support), signed
+    {
+      const int k = lane;
+      const unsigned slo = (unsigned)sup, shi = (unsigned)(sup >> 32);
+      const int nlo = __popc(slo);
+      if (k < nsup) {
+        const int i = k < nlo ? (int)__fns(slo, 0, k + 1) : 32 + (int)__fns(shi, 0, k - nlo + 1);
         const float sg = ((m2 >> i) & 1ull) ? 1.f : -1.f;
         const float* K = s.u.hs.K;
         const float v[6] = {sg * s.dw[i][0], sg * s.dw[i][1], sg * s.dw[i][2], sg * s.dv[i][0], sg * s.dv[i][1],
@@ -1106,10 +1150,12 @@ __device__ __noinline__ void hessian(World& s, int lane) {
   }
 }
 
-// Newton from the warm start (or qacc_smooth when that costs less); returns the iterations run
-__device__ __noinline__ int newton(World& s, int iterations, int lane) {
+// Newton from the warm start (or qacc_smooth when that costs less): newton_begin picks the start and forms the
+// gradient; newton_iter runs one iteration (Hessian and factor unless no row changed its zone, solve, exact line
+// search, update, gradient, stopping test). The state between iterations (cost, count, converged, same zones) lives
+// in the world record, so the caller can run the iterations of several worlds in lockstep.
+__device__ __noinline__ void newton_begin(World& s, int lane) {
   if (lane == 0) { s.nls = 0; s.nfact = 0; }
-  const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
   refresh(s, lane);
   float cost = total_cost(s, lane);
   // keep the warm start's qacc, Ma, jar in tmp / p / jv in case it stays the start
@@ -1125,94 +1171,108 @@ __device__ __noinline__ int newton(World& s, int iterations, int lane) {
   } else {
     cost = cost0;
   }
-  newton_grad(s, lane);
-  PROF(s, 6);
-  int it = 0;
-  bool same_zones = false;  // no row changed its zone in the last step: H and its factor in s.L are still exact
-  while (it < iterations) {
-    if (!same_zones) {
-      if (lane == 0) s.nfact++;
-      hessian(s, lane);
-      PROF(s, 7);
-      chol_factor(s.L, s.L, s.dinv, lane);
-      PROF(s, 8);
-    }
-    for (int i = lane; i < NV; i += 32) s.p[i] = -s.grad[i];
-    __syncwarp();
-    chol_solve(s.L, s.dinv, s.p, lane);
-    PROF(s, 9);
-    // exact line search along p: the cost is piecewise quadratic in alpha
-    rows_jv(s, s.p, s.efc_jv, lane);
-    matvec(s.M, s.p, s.Mp, lane);
-    float a1 = 0.f, a2 = 0.f;
-    for (int i = lane; i < NV; i += 32) { a1 += (s.Ma[i] - s.qsm[i]) * s.p[i]; a2 += s.p[i] * s.Mp[i]; }
-    a1 = warp_sum(a1);
-    a2 = warp_sum(a2);
-    const int nefc = s.nefc;
-    float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE];
-#pragma unroll
-    for (int t = 0; t < ROWS_PER_LANE; t++) {
-      const int r = lane + 32 * t;
-      const bool v = r < nefc;
-      rx[t] = v ? s.efc_jar[r] : 0.f;
-      rj[t] = v ? s.efc_jv[r] : 0.f;
-      rD[t] = v ? s.efc_D[r] : 0.f;
-    }
-    float alpha = 0.f, lo = 0.f, hi = 1e30f, d0 = 0.f;
-    unsigned zprev = 0u;
-    bool nwt = false;
-    for (int k = 0; k <= 40; k++) {
-      PROF_COUNT(17, 1);
-      float fd = 0.f, fdd = 0.f;
-      unsigned z = 0u;
-#pragma unroll
-      for (int t = 0; t < ROWS_PER_LANE; t++) {
-        const float x = rx[t] + alpha * rj[t];
-        if (x < 0.f) { z |= 1u << t; fd += rD[t] * x * rj[t]; fdd += rD[t] * rj[t] * rj[t]; }
-      }
-      if (__all_sync(FULL, nwt && z == zprev)) break;  // the Newton step kept every row on its piece: exact minimum
-      if (k == 40) break;
-      if (lane == 0) s.nls++;
-      fd = warp_sum(fd) + a1 + alpha * a2;
-      fdd = warp_sum(fdd) + a2;
-      if (k == 0) { d0 = fd; if (d0 >= 0.f) break; }
-      if (fabsf(fd) <= 1e-7f * fabsf(d0)) break;
-      if (fd < 0.f) lo = alpha; else hi = alpha;
-      float nx = alpha - fd / fdd;
-      nwt = nx > lo && nx < hi;
-      if (!nwt) nx = hi < 1e29f ? 0.5f * (lo + hi) : 2.f * fmaxf(alpha, 1e-6f);
-      zprev = z;
-      alpha = nx;
-    }
-    for (int i = lane; i < NV; i += 32) { s.qacc[i] += alpha * s.p[i]; s.Ma[i] += alpha * s.Mp[i]; }
-    bool chg = false;
-#pragma unroll
-    for (int t = 0; t < ROWS_PER_LANE; t++) {
-      const int r = lane + 32 * t;
-      const float xn = rx[t] + alpha * rj[t];
-      chg |= (xn < 0.f) != (rx[t] < 0.f);
-      if (r < nefc) s.efc_jar[r] = xn;
-    }
-    same_zones = !__any_sync(FULL, chg);
-    __syncwarp();
-    PROF(s, 10);
-    const float newcost = total_cost(s, lane);
-    const float gn = newton_grad(s, lane);
-    const float improvement = scale * (cost - newcost);
-    cost = newcost;
-    it++;
-    PROF(s, 11);
-    PROF_COUNT(16, 1);
-    if (improvement < tol || scale * gn < tol) break;
+  newton_grad(s, lane, 0.f);
+  if (lane == 0) { s.ncost = cost; s.nit_cur = 0; s.ndone = 0; s.nsame = 0; }
+  __syncwarp();
+}
+
+__device__ __noinline__ void newton_iter(World& s, int lane) {
+  const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
+  const float cost = s.ncost;
+  if (!s.nsame) {  // (no row changed its zone in the last step: H and its factor in s.L are still exact)
+    if (lane == 0) s.nfact++;
+    hessian(s, lane);
+    PROF(s, 7);
+    chol_factor(s.L, s.L, s.dinv, lane);
+    PROF(s, 8);
   }
-  return it;
+  for (int i = lane; i < NV; i += 32) s.p[i] = -s.grad[i];
+  __syncwarp();
+  chol_solve(s.L, s.dinv, s.p, lane);
+  PROF(s, 9);
+  // exact line search along p: the cost is piecewise quadratic in alpha
+  rows_jv(s, s.p, s.efc_jv, lane);
+  matvec(s.M, s.p, s.Mp, lane);
+  float a1 = 0.f, a2 = 0.f;
+  for (int i = lane; i < NV; i += 32) { a1 += (s.Ma[i] - s.qsm[i]) * s.p[i]; a2 += s.p[i] * s.Mp[i]; }
+  a1 = warp_sum(a1);
+  a2 = warp_sum(a2);
+  const int nefc = s.nefc;
+  float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE];
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++) {
+    const int r = lane + 32 * t;
+    const bool v = r < nefc;
+    rx[t] = v ? s.efc_jar[r] : 0.f;
+    rj[t] = v ? s.efc_jv[r] : 0.f;
+    rD[t] = v ? s.efc_D[r] : 0.f;
+  }
+  float alpha = 0.f, lo = 0.f, hi = 1e30f, d0 = 0.f;
+  unsigned zprev = 0u;
+  bool nwt = false;
+  for (int k = 0; k <= 40; k++) {
+    PROF_COUNT(17, 1);
+    float fd = 0.f, fdd = 0.f;
+    unsigned z = 0u;
+#pragma unroll
+    for (int t = 0; t < ROWS_PER_LANE; t++) {
+      const float x = rx[t] + alpha * rj[t];
+      if (x < 0.f) { z |= 1u << t; fd += rD[t] * x * rj[t]; fdd += rD[t] * rj[t] * rj[t]; }
+    }
+    if (__all_sync(FULL, nwt && z == zprev)) break;  // the Newton step kept every row on its piece: exact minimum
+    if (k == 40) break;
+    if (lane == 0) s.nls++;
+    fd = warp_sum(fd) + a1 + alpha * a2;
+    fdd = warp_sum(fdd) + a2;
+    if (k == 0) { d0 = fd; if (d0 >= 0.f) break; }
+    if (fabsf(fd) <= 1e-7f * fabsf(d0)) break;
+    if (fd < 0.f) lo = alpha; else hi = alpha;
+    float nx = alpha - fd / fdd;
+    nwt = nx > lo && nx < hi;
+    if (!nwt) nx = hi < 1e29f ? 0.5f * (lo + hi) : 2.f * fmaxf(alpha, 1e-6f);
+    zprev = z;
+    alpha = nx;
+  }
+  // move along p; the new cost (0.5 (Ma - qsm)(qacc - qacc_smooth) + the rows' costs) is summed with |grad|
+  float cpart = 0.f;
+  for (int i = lane; i < NV; i += 32) {
+    const float qa = s.qacc[i] + alpha * s.p[i], ma = s.Ma[i] + alpha * s.Mp[i];
+    s.qacc[i] = qa;
+    s.Ma[i] = ma;
+    cpart += 0.5f * (ma - s.qsm[i]) * (qa - s.qacc0[i]);
+  }
+  bool chg = false;
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++) {
+    const int r = lane + 32 * t;
+    const float xn = rx[t] + alpha * rj[t];
+    chg |= (xn < 0.f) != (rx[t] < 0.f);
+    if (xn < 0.f) cpart += 0.5f * rD[t] * xn * xn;
+    if (r < nefc) s.efc_jar[r] = xn;
+  }
+  const bool same_zones = !__any_sync(FULL, chg);
+  __syncwarp();
+  PROF(s, 10);
+  const float2 gc = newton_grad(s, lane, cpart);
+  const float gn = gc.x, newcost = gc.y;
+  const float improvement = scale * (cost - newcost);
+  PROF(s, 11);
+  PROF_COUNT(16, 1);
+  if (lane == 0) {
+    s.ncost = newcost;
+    s.nit_cur++;
+    s.nsame = same_zones;
+    s.ndone = improvement < tol || scale * gn < tol;
+  }
+  __syncwarp();
 }
 
 // ---- one substep -------------------------------------------------------------------------------------------------
 // stats: null, or this world's 8 counters of the substep (contacts kept, rows, Newton iterations, line-search
 // evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
-__device__ void substep(World& s, int iterations, int lane, int* stats) {
-  const float h = G1_TIMESTEP;
+// substep_pre: smooth dynamics, qacc_smooth, collision, rows and the Newton start; substep_post: the work counters,
+// implicitfast and the integration. Between them the caller runs newton_iter until the world is done.
+__device__ __noinline__ void substep_pre(World& s, int lane) {
   PROF_START(s);
   kinematics(s, lane);
   dof_motion(s, lane);
@@ -1235,7 +1295,16 @@ __device__ void substep(World& s, int iterations, int lane, int* stats) {
   PROF(s, 5);
   PROF_COUNT(18, s.ncon);
   PROF_COUNT(19, s.nefc);
-  const int it = newton(s, iterations, lane);
+  newton_begin(s, lane);
+  PROF(s, 6);
+}
+
+// stats: null, or this world's 8 counters of the substep (contacts kept, rows, Newton iterations, line-search
+// evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
+__device__ __noinline__ void substep_post(World& s, int lane, int* stats) {
+  const float h = G1_TIMESTEP;
+  PROF_START(s);
+  const int it = s.nit_cur;
   if (stats && lane == 0) {
     stats[0] = s.ncon; stats[1] = s.nefc; stats[2] = it; stats[3] = s.nls;
     stats[4] = s.nfact; stats[5] = s.ncand; stats[6] = s.ncon_raw; stats[7] = 0;

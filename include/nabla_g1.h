@@ -41,12 +41,28 @@ int nb_g1_upload(const float* consts, cudaStream_t stream);
  * [Newton iterations of the last substep, contacts the last substep's collision found (may exceed 64), constraint
  * rows of the last substep (<= 192), bits 1 unsupported geom pair / 4 contacts beyond 64 dropped / 16 rows beyond
  * 192 dropped, ORed over the substeps]. ocon (B,64,8) may be NULL: the last substep's contacts as (pair, dist,
- * pos[3], normal[3]), pair -1 past the count. tape must be NULL (no tape is recorded by this entry). work:
- * nb_g1_work_bytes(nw) bytes or NULL when that is 0. nw == 0 is a no-op.
+ * pos[3], normal[3]), pair -1 past the count. tape (B, nsub, tape words) may be NULL: else the per-substep records
+ * nb_g1_adjoint reads (the substep's input state, a*, a_adv, the Cholesky factors of the Newton Hessian and of
+ * M + h kv, the contact table, the constraint zones, the actuator clamp masks, flags); the outputs are bitwise the
+ * same with and without it. work: nb_g1_work_bytes(nw) bytes or NULL when that is 0. nw == 0 is a no-op.
  * Replaces `int <pfx>_forward(cudaStream_t, int nw, ...)` (src/nablaengine/jax_ffi.py:266-279). */
 int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
                   const float* ctrl, const float* friction, const float* com, int iterations, int nsub, float* qpos_out,
                   float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work);
+
+/* The adjoint of one control step from its tape: the VJP of (qpos', qvel') with cotangents gq_out (B,36) (qpos form)
+ * and gv_out (B,35), written to gq_in (B,36) (qpos form: root position, 2 xi (x) (0, tangent cotangent) for the root
+ * quaternion xi, hinges), gv_in (B,35) and gctrl (B,29); info (B,) int32: flags of the replay (bit 13: the replayed
+ * constraint rows differ from the forward's). tape: nb_g1_forward's tape of the same nw worlds and nsub substeps;
+ * friction, com: that call's. clamp_kv: 0 (the actuator damping term kept on clamped dofs), 1 (exact), 2 (the soft
+ * clamp with width clamp_soft; ctrl (B,29), that call's setpoints, required); ctrl is ignored otherwise (may be NULL).
+ * normal: the self-contact normal derivative, 0 exact, 1 frozen, 2 regularised below 1e-3 m, 3 frozen below 1e-3 m.
+ * Replaces `int <pfx>_adjoint(cudaStream_t, int nw, int nsub, tape, fric, com, gq_out, gv_out, gq_in, gv_in, gctrl,
+ * info, ctrl, clamp_soft)` (src/nablaengine/jax_ffi.py:228-241), where clamp_kv and normal select one of 12 compiled
+ * libraries; here they are the two trailing arguments of one entry. */
+int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
+                  const float* gq_out, const float* gv_out, float* gq_in, float* gv_in, float* gctrl, int* info,
+                  const float* ctrl, float clamp_soft, int clamp_kv, int normal);
 
 /* nb_g1_forward plus the per-substep work counters stats (B, nsub, 8) int32: contacts kept, constraint rows, Newton
  * iterations, line-search evaluations, Hessian factorisations, broad-phase candidate pairs, contacts found, 0; the

@@ -4,6 +4,7 @@
 // launch with its state resident in shared memory (nb_g1_step.cuh), so a step is a single kernel per call.
 #include "../../include/nabla_g1.h"
 #include "nb_g1_step.cuh"
+#include "nb_g1_adjoint.cuh"
 
 namespace nbg1 {
 
@@ -17,7 +18,7 @@ constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // NB_LOCKSTEP: the worlds of a block run their Newton iterations in lockstep (a block barrier per iteration): the
 // warps of an SM then fetch the same instructions at the same time, instead of each streaming the ~50 KB Newton loop
 // from its own position (the kernel is bound by instruction fetch otherwise)
-constexpr int TAPE_WORDS = 0;
+constexpr int TAPE_WORDS = REC_WORDS;
 constexpr long long ABI_VERSION = 1;
 
 __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __restrict__ qpos,
@@ -26,7 +27,8 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
                                                       const float* __restrict__ com, int iterations, int nsub,
                                                       float* __restrict__ oq, float* __restrict__ ov,
                                                       float* __restrict__ ow, int* __restrict__ info,
-                                                      float* __restrict__ ocon, int* __restrict__ stats) {
+                                                      float* __restrict__ ocon, int* __restrict__ stats,
+                                                      float* __restrict__ tape) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * WPB + warp;
@@ -43,7 +45,8 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   if (lane == 0) { s.fric = fric[w]; s.unsup = 0; s.nit = 0; }
   __syncwarp();
   for (int k = 0; k < nsub; k++) {
-    if (active) substep_pre(s, lane);
+    float* rec = tape && active ? tape + (w64 * nsub + k) * REC_WORDS : nullptr;
+    if (active) substep_pre(s, lane, rec);
     while (true) {
       const bool done = !active || s.ndone || s.nit_cur >= iterations;
 #if NB_LOCKSTEP
@@ -53,7 +56,7 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 #endif
       if (!done) newton_iter(s, lane);
     }
-    if (active) substep_post(s, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr);
+    if (active) substep_post(s, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr, rec);
   }
   if (!active) return;
   for (int i = lane; i < NQ; i += 32) oq[w64 * NQ + i] = s.qpos[i];
@@ -78,6 +81,81 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 }
 
 constexpr size_t SMEM = sizeof(World) * WPB;
+
+// ---- the adjoint ------------------------------------------------------------------------------------------------
+constexpr int AWPB = 1;  // worlds per block of k_adjoint
+struct AdjBlock { World s; Adj a; float cw[32][30]; };
+constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
+
+// tape: nw * nsub records; gq_out (B,36) / gv_out (B,35): cotangents of qpos' / qvel'; outputs gq_in (B,36) (qpos
+// form), gv_in (B,35), gctrl (B,29), info (B,) (replay mismatch bits); ctrl: the step's setpoints (clamp_kv 2 only)
+__global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const float* __restrict__ tape,
+                                                       const float* __restrict__ fric, const float* __restrict__ com,
+                                                       const float* __restrict__ gq_out,
+                                                       const float* __restrict__ gv_out, float* __restrict__ gq_in,
+                                                       float* __restrict__ gv_in, float* __restrict__ gctrl,
+                                                       int* __restrict__ info, const float* __restrict__ ctrl,
+                                                       float clamp_soft, int clamp_kv, int normal) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x * AWPB + warp;
+  if (w >= nw) return;
+  AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
+  World& s = blk.s;
+  Adj& A = blk.a;
+  const size_t w64 = (size_t)w;
+  const float h = G1_TIMESTEP;
+  if (lane == 0) { s.fric = fric[w]; A.normal = normal; }
+  if (lane < 3) s.com[lane] = com[w64 * 3 + lane];
+  for (int i = lane; i < NU; i += 32) { A.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f; A.ub[i] = 0.f; }
+  for (int i = lane; i < NV; i += 32) A.vb[i] = gv_out[w64 * NV + i];
+  // the output cotangent in the dof tangent: the quaternion part at the output quaternion q' (re-integrated from the
+  // last record): 1/2 Im(q'* gq)
+  const float* last = tape + (w64 * nsub + nsub - 1) * REC_WORDS;
+  for (int i = lane; i < NV; i += 32)
+    if (i < 3 || i >= 6) A.qout[i] = gq_out[w64 * NQ + (i < 3 ? i : i + 1)];
+  if (lane == 0) {
+    float q[4] = {last[T_QPOS + 3], last[T_QPOS + 4], last[T_QPOS + 5], last[T_QPOS + 6]};
+    const float wv[3] = {last[T_QVEL + 3] + h * last[T_AADV + 3], last[T_QVEL + 4] + h * last[T_AADV + 4],
+                         last[T_QVEL + 5] + h * last[T_AADV + 5]};
+    const float nw = sqrtf(dot3(wv, wv));
+    if (nw > 0.f) {
+      float sa, ca;
+      sincosf(0.5f * h * nw, &sa, &ca);
+      const float dq[4] = {ca, sa * wv[0] / nw, sa * wv[1] / nw, sa * wv[2] / nw};
+      float o[4];
+      qmul(q, dq, o);
+      const float on = sqrtf(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      for (int k = 0; k < 4; k++) q[k] = o[k] / on;
+    }
+    const float g[4] = {gq_out[w64 * NQ + 3], gq_out[w64 * NQ + 4], gq_out[w64 * NQ + 5], gq_out[w64 * NQ + 6]};
+    const float qc[4] = {q[0], -q[1], -q[2], -q[3]};
+    float m[4];
+    qmul(qc, g, m);
+    const float n2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+    for (int k = 0; k < 3; k++) A.qout[3 + k] = 0.5f * m[1 + k] / n2;
+  }
+  __syncwarp();
+  int flags = 0;
+  for (int k = nsub - 1; k >= 0; k--)
+    flags |= adj_substep(s, A, tape + (w64 * nsub + k) * REC_WORDS, clamp_kv, clamp_soft, blk.cw, lane);
+  // the input qpos gradient in qpos form: (q_lin, 2 xi (0, q_rot), q_hinge), xi the input quaternion
+  const float* first = tape + w64 * nsub * REC_WORDS;
+  for (int i = lane; i < NV; i += 32) {
+    if (i < 3) gq_in[w64 * NQ + i] = A.qout[i];
+    else if (i >= 6) gq_in[w64 * NQ + i + 1] = A.qout[i];
+    gv_in[w64 * NV + i] = A.vb[i];
+  }
+  for (int i = lane; i < NU; i += 32) gctrl[w64 * NU + i] = A.ub[i];
+  if (lane == 0) {
+    const float xi[4] = {first[T_QPOS + 3], first[T_QPOS + 4], first[T_QPOS + 5], first[T_QPOS + 6]};
+    const float t[4] = {0.f, A.qout[3], A.qout[4], A.qout[5]};
+    float o[4];
+    qmul(xi, t, o);
+    for (int k = 0; k < 4; k++) gq_in[w64 * NQ + 3 + k] = 2.f * o[k];
+    info[w] = flags;
+  }
+}
 static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
 
 }  // namespace nbg1
@@ -99,8 +177,26 @@ long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : 0; }
 int nb_g1_upload(const float* consts, cudaStream_t stream) {
   (void)consts;
   (void)stream;
-  // the model is compiled in; the per-device work is the kernel's shared-memory opt-in (above 48 KB)
-  return (int)cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+  // the model is compiled in; the per-device work is the kernels' shared-memory opt-in (above 48 KB)
+  cudaError_t e = cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_adjoint, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+  return (int)e;
+}
+
+int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
+                  const float* gq_out, const float* gv_out, float* gq_in, float* gv_in, float* gctrl, int* info,
+                  const float* ctrl, float clamp_soft, int clamp_kv, int normal) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3)
+    return (int)cudaErrorInvalidValue;
+  if (nw == 0) return 0;
+  if (!tape || !friction || !com || !gq_out || !gv_out || !gq_in || !gv_in || !gctrl || !info)
+    return (int)cudaErrorInvalidValue;
+  if (clamp_kv == 2 && !ctrl) return (int)cudaErrorInvalidValue;
+  const int blocks = (nw + AWPB - 1) / AWPB;
+  k_adjoint<<<blocks, AWPB * 32, ASMEM, stream>>>(nw, nsub, tape, friction, com, gq_out, gv_out, gq_in, gv_in, gctrl,
+                                                  info, ctrl, clamp_soft, clamp_kv, normal);
+  return (int)cudaGetLastError();
 }
 
 static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
@@ -108,7 +204,6 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
                           float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape,
                           int* stats) {
   if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return (int)cudaErrorInvalidValue;
-  if (tape) return (int)cudaErrorNotSupported;
   if (nw == 0) return 0;
   if (!qpos || !qvel || !warm || !ctrl || !friction || !com || !qpos_out || !qvel_out || !warm_out || !info)
     return (int)cudaErrorInvalidValue;
@@ -120,7 +215,7 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
   const size_t smem = SMEM;
 #endif
   k_forward<<<blocks, WPB * 32, smem, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
-                                                qvel_out, warm_out, info, ocon, stats);
+                                                qvel_out, warm_out, info, ocon, stats, tape);
   return (int)cudaGetLastError();
 }
 

@@ -33,6 +33,17 @@ constexpr int ROWS_PER_LANE = (NEFC + 31) / 32;
 __host__ __device__ constexpr int TRI(int i, int j) { return i * (i + 1) / 2 + j; }  // packed lower triangle, j <= i
 
 enum : int { UNSUPPORTED_PAIR = 1, CONTACT_OVERFLOW = 4, ROW_OVERFLOW = 16 };
+
+// The forward tape: one record of REC_WORDS float32 words per world and substep (record w * nsub + k), what the
+// adjoint reads: the substep's input state, the Newton solution a*, a_adv = (M + h kv)^-1 M a*, the Cholesky factors
+// of the Newton Hessian at the final zones (L_H) and of M + h kv (L_Q) with their inverse diagonals, the contact
+// table (pair | slot << 9, two 16-bit entries per word, contact order), the rows' final zone bits, the actuator
+// clamp mask (dof bits) and a header
+constexpr int T_QPOS = 0, T_QVEL = 36, T_ASTAR = 71, T_AADV = 106, T_DINVH = 141, T_DINVQ = 176, T_LH = 211;
+constexpr int T_LQ = T_LH + NTRI, T_CON = T_LQ + NTRI, T_ZONE = T_CON + MAXCON / 2, T_CLAMP = T_ZONE + NEFC / 32;
+constexpr int T_HDR = T_CLAMP + 2, T_FLAGS = T_HDR + 1, REC_WORDS = ((T_FLAGS + 1 + 3) / 4) * 4;
+static_assert(T_LQ == 841 && REC_WORDS == 1516, "tape layout");
+enum : unsigned { TAPE_REFACT = 1u << 8, TAPE_NONCONV = 1u << 9 };
 enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
 
 // Phase profile (build with -DNB_PROFILE; the product build has none of it): lane 0 of every world adds the clock64
@@ -68,6 +79,7 @@ struct __align__(16) World {
   int ngroup, nls, nfact, pad3_;        // groups; line-search evaluations, factorisations (work counters)
   float ncost;                          // Newton state between iterations: cost, iterations, converged, same zones
   int nit_cur, ndone, nsame;
+  unsigned clamp_lo, clamp_hi;          // actuator force at its limit (dof bits), for the tape
   int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
   int con_pair[MAXCON];
   unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
@@ -321,12 +333,16 @@ __device__ __noinline__ void mass_and_force(World& s, int lane) {
     // bias: the subtree wrench of the dof's body projected on its motion
     const float bias = dot3(w, s.u.sm.wr[b]) + dot3(v, s.u.sm.wr[b] + 3);
     float act = 0.f;
+    bool clamp = false;
     if (i >= 6) {
       act = ld(g1_dof_kp + i) * (s.ctrl[i - 6] - s.qpos[i + 1]) - ld(g1_dof_kv + i) * s.qvel[i];
       const float lim = ld(g1_dof_frclim + i);
       act = fminf(fmaxf(act, -lim), lim);
+      clamp = act <= -lim || act >= lim;
     }
     s.qsm[i] = act - bias;
+    const unsigned bal = __ballot_sync(__activemask(), clamp);
+    if (lane == 0) { if (i < 32) s.clamp_lo = bal; else s.clamp_hi = bal; }
   }
   __syncwarp();
 }
@@ -1272,8 +1288,16 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
 // evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
 // substep_pre: smooth dynamics, qacc_smooth, collision, rows and the Newton start; substep_post: the work counters,
 // implicitfast and the integration. Between them the caller runs newton_iter until the world is done.
-__device__ __noinline__ void substep_pre(World& s, int lane) {
+__device__ __forceinline__ void tape_put(float* dst, const float* src, int n, int lane) {
+  for (int i = lane; i < n; i += 32) __stcs(dst + i, src[i]);
+}
+
+__device__ __noinline__ void substep_pre(World& s, int lane, float* rec) {
   PROF_START(s);
+  if (rec) {
+    tape_put(rec + T_QPOS, s.qpos, NQ, lane);
+    tape_put(rec + T_QVEL, s.qvel, NV, lane);
+  }
   kinematics(s, lane);
   dof_motion(s, lane);
   PROF(s, 0);
@@ -1301,10 +1325,41 @@ __device__ __noinline__ void substep_pre(World& s, int lane) {
 
 // stats: null, or this world's 8 counters of the substep (contacts kept, rows, Newton iterations, line-search
 // evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
-__device__ __noinline__ void substep_post(World& s, int lane, int* stats) {
+__device__ __noinline__ void substep_post(World& s, int lane, int* stats, float* rec) {
   const float h = G1_TIMESTEP;
   PROF_START(s);
   const int it = s.nit_cur;
+  if (rec) {  // the Hessian factor at the final zones (re-assembled when the last step changed a zone or none ran)
+    const bool refact = !s.nsame || it == 0;
+    if (refact) {
+      hessian(s, lane);
+      chol_factor(s.L, s.L, s.dinv, lane);
+    }
+    tape_put(rec + T_LH, s.L, NTRI, lane);
+    tape_put(rec + T_DINVH, s.dinv, NV, lane);
+    tape_put(rec + T_ASTAR, s.qacc, NV, lane);
+    const int ncon = s.ncon, nefc = s.nefc;
+    for (int i = lane; i < MAXCON / 2; i += 32) {
+      const unsigned e0 = 2 * i < ncon ? (unsigned)s.con_pair[2 * i] | (unsigned)s.con_slot[2 * i] << 9 : 0xffffu;
+      const unsigned e1 = 2 * i + 1 < ncon ? (unsigned)s.con_pair[2 * i + 1] | (unsigned)s.con_slot[2 * i + 1] << 9
+                                          : 0xffffu;
+      __stcs(rec + T_CON + i, __uint_as_float(e0 | e1 << 16));
+    }
+    for (int r0 = 0; r0 < NEFC; r0 += 32) {
+      const int r = r0 + lane;
+      const unsigned z = __ballot_sync(FULL, r < nefc && s.efc_jar[r] < 0.f);
+      if (lane == 0) __stcs(rec + T_ZONE + r0 / 32, __uint_as_float(z));
+    }
+    if (lane == 0) {
+      __stcs(rec + T_CLAMP, __uint_as_float(s.clamp_lo));
+      __stcs(rec + T_CLAMP + 1, __uint_as_float(s.clamp_hi));
+      __stcs(rec + T_HDR, __uint_as_float((unsigned)ncon | (unsigned)nefc << 8 | (unsigned)s.nlim << 16));
+      __stcs(rec + T_FLAGS, __uint_as_float((unsigned)s.unsup | (refact ? TAPE_REFACT : 0u) |
+                                            (s.ndone ? 0u : TAPE_NONCONV)));
+      for (int k = T_FLAGS + 1; k < REC_WORDS; k++) __stcs(rec + k, 0.f);
+    }
+    __syncwarp();
+  }
   if (stats && lane == 0) {
     stats[0] = s.ncon; stats[1] = s.nefc; stats[2] = it; stats[3] = s.nls;
     stats[4] = s.nfact; stats[5] = s.ncand; stats[6] = s.ncon_raw; stats[7] = 0;
@@ -1316,6 +1371,11 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats) {
   __syncwarp();
   chol_factor(s.L, s.L, s.dinv, lane);
   chol_solve(s.L, s.dinv, s.tmp, lane);
+  if (rec) {
+    tape_put(rec + T_LQ, s.L, NTRI, lane);
+    tape_put(rec + T_DINVQ, s.dinv, NV, lane);
+    tape_put(rec + T_AADV, s.tmp, NV, lane);
+  }
   for (int i = lane; i < NV; i += 32) s.qvel[i] += h * s.tmp[i];
   __syncwarp();
   if (lane == 0) {

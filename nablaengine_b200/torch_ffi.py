@@ -4,13 +4,20 @@ CUDA kernels of libnabla_g1.so on torch's current stream of the inputs' device.
 
   step(qpos, qvel, warm, ctrl, friction, com, *, iterations=10, substeps=4, clamp_kv=0, normal=3, clamp_soft=None,
        grad_decay=1.0) -> (qpos', qvel', warm')
-  forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=10, substeps=4) -> (qpos', qvel', warm', info)
+  forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=10, substeps=4, tape=False)
+      -> (qpos', qvel', warm', info[, tape])
+  backward(tape, friction, com, g_qpos, g_qvel, *, substeps=4, clamp_kv=0, normal=3, ctrl=None, clamp_soft=None)
+      -> (g_qpos, g_qvel, g_ctrl, info)
+  scale_grad(tree, gamma)
 
 Arguments as the reference: float32 CUDA tensors on one device, contiguous, leading dimension B (the worlds): qpos
 (B, 36), qvel (B, 35), warm (B, 35), ctrl (B, 29), friction (B,), com (B, 3). Other dtypes, devices or shapes raise
-TypeError (nothing is cast or copied implicitly); bad options raise ValueError. The call only launches kernels and
-allocates through torch's caching allocator, so after init(device) it can be captured in a CUDA graph. There is no
-CPU fallback: without the CUDA library the call raises.
+TypeError (nothing is cast or copied implicitly); bad options raise ValueError. step is differentiable
+(torch.autograd): when an input requires grad the forward also writes the tape (B, substeps * REC_WORDS float32) and
+keeps it for the backward, the analytic adjoint (deterministic), which returns d/dqpos (qpos form, 36), d/dqvel and
+d/dctrl and no gradient for warm, friction and com. The calls only launch kernels and allocate through torch's
+caching allocator, so after init(device) they can be captured in a CUDA graph. There is no CPU fallback: without
+the CUDA library the call raises.
 """
 import ctypes
 import math
@@ -71,7 +78,16 @@ def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
-def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps):
+def _rec_words():
+    return int(capi.sizes()[6])
+
+
+def tape_bytes(nworld, substeps=SUBSTEPS, steps=1):
+    """Bytes of the tapes of `steps` differentiated control steps (reference torch_ffi.py:454)."""
+    return 4 * _rec_words() * substeps * nworld * steps
+
+
+def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape=False):
     import torch
     if not isinstance(qpos, torch.Tensor) or qpos.device.type != "cuda":
         _check("qpos", qpos, (getattr(qpos, "shape", (0,))[0], NQ), None)
@@ -88,42 +104,177 @@ def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps):
     kw = dict(dtype=torch.float32, device=qpos.device)
     q1, v1, w1 = torch.empty((B, NQ), **kw), torch.empty((B, NV), **kw), torch.empty((B, NV), **kw)
     info = torch.empty((B, 4), dtype=torch.int32, device=qpos.device)
+    tp = torch.empty((B if tape else 0, substeps * _rec_words()), **kw)
     if B == 0:
-        return q1, v1, w1, info
+        return q1, v1, w1, info, tp
     lib = capi.load()
     nwork = int(lib.nb_g1_work_bytes(B))
     work = torch.empty((nwork,), dtype=torch.uint8, device=qpos.device) if nwork > 0 else None
     with torch.cuda.device(dev):
         st = torch.cuda.current_stream(dev).cuda_stream
         rc = lib.nb_g1_forward(ctypes.c_void_p(st), B, *map(_ptr, (qpos, qvel, warm, ctrl, friction, com)),
-                               int(iterations), int(substeps), _ptr(q1), _ptr(v1), _ptr(w1), _ptr(info), None, None,
-                               _ptr(work))
+                               int(iterations), int(substeps), _ptr(q1), _ptr(v1), _ptr(w1), _ptr(info), None,
+                               _ptr(tp) if tape else None, _ptr(work))
     if rc:
         raise _err(f"the forward launch failed (CUDA error {rc})", RuntimeError)
-    return q1, v1, w1, info
+    return q1, v1, w1, info, tp
 
 
-def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS):
-    """One control step without autograd: (qpos', qvel', warm', info (B, 4) int32), as the reference's forward:
-    info = [Newton iterations of the last substep, its contact count (may exceed 64), its constraint rows, bits
-    1 unsupported pair / 4 contacts beyond 64 / 16 rows beyond 192 over the substeps]."""
-    return _forward_impl(qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps))
+def _soft(clamp_kv, clamp_soft):
+    """The soft clamp's width for clamp_kv 2 (None: CLAMP_SOFT), None for 0 / 1, where it must be None (reference
+    torch_ffi.py:436 _soft)."""
+    if int(clamp_kv) != 2:
+        if clamp_soft is not None:
+            raise _err(f"clamp_soft is the soft clamp's (clamp_kv=2), not clamp_kv={clamp_kv}", ValueError)
+        return None
+    d = float(CLAMP_SOFT if clamp_soft is None else clamp_soft)
+    if not (math.isfinite(d) and d >= 0.0):
+        raise _err(f"clamp_soft must be finite and >= 0, got {clamp_soft}", ValueError)
+    return d
+
+
+def _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv, normal, clamp_soft):
+    import torch
+    if not isinstance(tape, torch.Tensor) or tape.device.type != "cuda" or tape.dim() != 2:
+        _check("tape", tape, (getattr(tape, "shape", (0,))[0], substeps * _rec_words()), None)
+    B, dev = tape.shape[0], tape.device.index
+    for name, x, shape in (("tape", tape, (B, substeps * _rec_words())), ("friction", friction, (B,)),
+                           ("com", com, (B, 3)), ("g_qpos", g_qpos, (B, NQ)), ("g_qvel", g_qvel, (B, NV))):
+        _check(name, x, shape, dev)
+    if int(clamp_kv) not in (0, 1, 2) or int(normal) not in (0, 1, 2, 3):
+        raise _err(f"no adjoint variant clamp_kv={clamp_kv} normal={normal}", ValueError)
+    if (int(clamp_kv) == 2) != (ctrl is not None):
+        raise _err("clamp_kv=2 (the soft clamp) needs the step's ctrl; 0 and 1 take none", ValueError)
+    if ctrl is not None:
+        _check("ctrl", ctrl, (B, NU), dev)
+    if not (1 <= substeps <= 32):
+        raise _err("substeps in 1..32", ValueError)
+    if dev not in _READY:
+        init(dev)
+    kw = dict(dtype=torch.float32, device=tape.device)
+    gq, gv, gu = torch.empty((B, NQ), **kw), torch.empty((B, NV), **kw), torch.empty((B, NU), **kw)
+    info = torch.empty((B,), dtype=torch.int32, device=tape.device)
+    if B == 0:
+        return gq, gv, gu, info
+    lib = capi.load()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.nb_g1_adjoint(ctypes.c_void_p(st), B, int(substeps),
+                               *map(_ptr, (tape, friction, com, g_qpos, g_qvel, gq, gv, gu, info, ctrl)),
+                               ctypes.c_float(clamp_soft), int(clamp_kv), int(normal))
+    if rc:
+        raise _err(f"the adjoint launch failed (CUDA error {rc})", RuntimeError)
+    return gq, gv, gu, info
+
+
+def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, tape=False):
+    """One control step without autograd: (qpos', qvel', warm', info (B, 4) int32[, tape]), as the reference's forward
+    (torch_ffi.py:845): info = [Newton iterations of the last substep, its contact count (may exceed 64), its
+    constraint rows, bits 1 unsupported pair / 4 contacts beyond 64 / 16 rows beyond 192 over the substeps]."""
+    r = _forward_impl(qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape))
+    return r if tape else r[:4]
+
+
+def backward(tape, friction, com, g_qpos, g_qvel, *, substeps=SUBSTEPS, clamp_kv=CLAMP_KV, normal=NORMAL, ctrl=None,
+             clamp_soft=None):
+    """The adjoint of one control step from its tape (reference torch_ffi.py:854): (g_qpos (qpos form), g_qvel,
+    g_ctrl, info (B,) int32, the replay flags)."""
+    soft = _soft(clamp_kv, clamp_soft)
+    if soft is not None and ctrl is None:
+        raise _err("clamp_kv=2 (the soft clamp) needs the step's ctrl", ValueError)
+    return _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl if soft is not None else None, int(substeps),
+                          int(clamp_kv), int(normal), 0.0 if soft is None else soft)
+
+
+def _make_step_fn():
+    import torch
+
+    class _Step(torch.autograd.Function):
+        """Forward with tape; backward = the analytic adjoint (reference torch_ffi.py:747-779)."""
+
+        @staticmethod
+        def forward(ctx, qpos, qvel, warm, ctrl, friction, com, iterations, substeps, clamp_kv, normal, clamp_soft,
+                    grad_decay):
+            q1, v1, w1, _, tp = _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, True)
+            ctx.save_for_backward(tp, friction, com, ctrl)
+            ctx.opts = (substeps, clamp_kv, normal, clamp_soft, grad_decay)
+            ctx.mark_non_differentiable(w1)
+            return q1, v1, w1
+
+        @staticmethod
+        def backward(ctx, g_q1, g_v1, g_w1):
+            tp, friction, com, ctrl = ctx.saved_tensors
+            substeps, clamp_kv, normal, clamp_soft, grad_decay = ctx.opts
+            B = tp.shape[0]
+            g_q1 = tp.new_zeros((B, NQ)) if g_q1 is None else g_q1.contiguous()
+            g_v1 = tp.new_zeros((B, NV)) if g_v1 is None else g_v1.contiguous()
+            gq, gv, gu, _ = _backward_impl(tp, friction, com, g_q1, g_v1, ctrl if clamp_kv == 2 else None, substeps,
+                                           clamp_kv, normal, 0.0 if clamp_soft is None else clamp_soft)
+            if grad_decay != 1.0:  # the state's cotangent through the physics times grad_decay, ctrl's not
+                gq, gv = gq * grad_decay, gv * grad_decay
+            return gq, gv, None, gu, None, None, None, None, None, None, None, None
+
+    return _Step
+
+
+_FNS = {}
+
+
+def _fn(name, make):
+    if name not in _FNS:
+        _FNS[name] = make()
+    return _FNS[name]
 
 
 def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, clamp_kv=CLAMP_KV,
          normal=NORMAL, clamp_soft=None, grad_decay=GRAD_DECAY):
-    """One control step: (qpos', qvel', warm'). The gradient options (clamp_kv, normal, clamp_soft, grad_decay) are
-    validated as the reference does."""
+    """One control step: (qpos', qvel', warm') (reference torch_ffi.py:817). Differentiable in qpos, qvel and ctrl when
+    an input requires grad (the forward then also writes the tape); warm' is not differentiable. clamp_kv, normal,
+    clamp_soft and grad_decay act on the backward only."""
     import torch
     if int(clamp_kv) not in (0, 1, 2) or int(normal) not in (0, 1, 2, 3):
         raise _err("clamp_kv in {0, 1, 2}, normal in 0..3", ValueError)
-    if int(clamp_kv) != 2 and clamp_soft is not None:
-        raise _err(f"clamp_soft is the soft clamp's (clamp_kv=2), not clamp_kv={clamp_kv}", ValueError)
-    if not math.isfinite(float(grad_decay)):
+    soft = _soft(clamp_kv, clamp_soft)
+    gd = float(grad_decay)
+    if not math.isfinite(gd):
         raise _err(f"grad_decay must be finite, got {grad_decay}", ValueError)
     args = (qpos, qvel, warm, ctrl, friction, com)
     if torch.is_grad_enabled() and any(isinstance(x, torch.Tensor) and x.requires_grad for x in args):
-        raise _err("the differentiable step (tape + adjoint) is not in this build yet; call it under "
-                   "torch.no_grad() or with inputs that do not require grad", NotImplementedError)
-    q1, v1, w1, _ = _forward_impl(*args, int(iterations), int(substeps))
+        return _fn("step", _make_step_fn).apply(*args, int(iterations), int(substeps), int(clamp_kv), int(normal),
+                                                soft, gd)
+    q1, v1, w1, _, _ = _forward_impl(*args, int(iterations), int(substeps))
     return q1, v1, w1
+
+
+def _make_scale_fn():
+    import torch
+
+    class _Scale(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, gamma, *xs):
+            ctx.gamma = gamma
+            return tuple(x.view_as(x) for x in xs)
+
+        @staticmethod
+        def backward(ctx, *g):
+            return (None,) + tuple(None if x is None else x * ctx.gamma for x in g)
+
+    return _Scale
+
+
+def scale_grad(tree, gamma):
+    """The identity on a pytree of tensors whose cotangent the backward multiplies by gamma (floating tensors only;
+    others pass through), as the reference's scale_grad (torch_ffi.py:884): applied to the carried state at the top
+    of each rollout step it gives an exact decay^n per step boundary."""
+    import torch
+    from torch.utils import _pytree
+    g = float(gamma)
+    if not math.isfinite(g):
+        raise _err(f"scale_grad's gamma must be finite, got {gamma}", ValueError)
+    leaves, spec = _pytree.tree_flatten(tree)
+    idx = [i for i, x in enumerate(leaves) if isinstance(x, torch.Tensor) and x.is_floating_point()]
+    if idx:
+        out = _fn("scale", _make_scale_fn).apply(g, *(leaves[i] for i in idx))
+        for i, x in zip(idx, out):
+            leaves[i] = x
+    return _pytree.tree_unflatten(leaves, spec)

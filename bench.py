@@ -120,6 +120,50 @@ def cpu_baseline(seconds=12.0):
                       f"x {SUBSTEPS} substeps, {dt:.1f} s; MuJoCo C (the reference's CPU path) is not installed"}
 
 
+def measure_fwd_grad(dev, rank, steps, warmup, flush):
+    """forward + analytic VJP of one step (4096 worlds, 10 % lowered into multi-contact),
+    loss = sum(qvel'^2), exact gradient mode (clamp_kv=1, normal=0), through torch autograd (torch_ffi.step then
+    loss.backward()). Device time per step (CUDA events, L2 flushed between steps); the forward-with-tape and the
+    adjoint kernels also timed alone."""
+    import torch
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("vjp", seed_offset=rank)
+    keys = ("qpos", "qvel", "warm", "ctrl", "friction", "com")
+    x = [torch.from_numpy(s[k]).to(dev) for k in keys]
+    B = x[0].shape[0]
+    leaves = [x[0].clone().requires_grad_(True), x[1].clone().requires_grad_(True), x[3].clone().requires_grad_(True)]
+
+    def one():
+        q, v, u = leaves
+        for t in leaves:
+            t.grad = None
+        q1, v1, w1 = torch_ffi.step(q, v, x[2], u, x[4], x[5], iterations=ITERATIONS, substeps=SUBSTEPS, clamp_kv=1,
+                                    normal=0)
+        (v1 * v1).sum().backward()
+
+    st = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record(st)
+            fn()
+            e1.record(st)
+        torch.cuda.synchronize()
+        return sum(e0.elapsed_time(e1) for e0, e1 in ev) / steps
+
+    ms = timed(one)
+    ms_fwd_tape = timed(lambda: torch_ffi.forward(*x, iterations=ITERATIONS, substeps=SUBSTEPS, tape=True))
+    q1, v1, w1, info, tape = torch_ffi.forward(*x, iterations=ITERATIONS, substeps=SUBSTEPS, tape=True)
+    gq, gv = torch.zeros_like(q1), 2 * v1
+    ms_bwd = timed(lambda: torch_ffi.backward(tape, x[4], x[5], gq, gv, clamp_kv=1, normal=0))
+    return {"B": B, "ms": ms, "ms_fwd_tape": ms_fwd_tape, "ms_adjoint": ms_bwd}
+
+
 def run_reference(a, rank):
     """--impl reference: rank 0 times the reference's CPU path substitute (the float64 oracle port) per step on a
     bounded sample of the configuration-2 workload."""
@@ -215,6 +259,8 @@ def main():
     torch.cuda.synchronize()
     kern_ms = [e0.elapsed_time(e1) for e0, e1 in ev]
     total = torch.tensor([sum(kern_ms)], dtype=torch.float64, device=dev)
+    fg = measure_fwd_grad(dev, rank, a.steps, a.warmup, flush)
+    fg_ms = torch.tensor([fg["ms"], fg["ms_fwd_tape"], fg["ms_adjoint"]], dtype=torch.float64, device=dev)
 
     # end to end through the public API: pinned host inputs in, host outputs back, every step
     host = [t.cpu().pin_memory() for t in x]
@@ -243,6 +289,7 @@ def main():
     if world > 1:
         dist.all_reduce(total, op=dist.ReduceOp.MAX)
         dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+        dist.all_reduce(fg_ms, op=dist.ReduceOp.MAX)
     t_s, e2e_s = total.item() / 1e3, e2e_total.item() / 1e3
     value = world * B * a.steps / t_s
     e2e_value = world * B * a.steps / e2e_s
@@ -281,6 +328,12 @@ def main():
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "world-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": a.steps,
+        "fwd_grad": {"metric": "world-steps/sec fwd+grad at B=4096/GPU (BASELINE configuration 3: loss sum(qvel'^2), "
+                               "VJP w.r.t. qpos, qvel, ctrl, exact mode clamp_kv=1 normal=0, torch autograd)",
+                     "value": world * fg["B"] / (fg_ms[0].item() / 1e3), "unit": "world-steps/s",
+                     "ms_per_step": fg_ms[0].item(), "ms_forward_with_tape": fg_ms[1].item(),
+                     "ms_adjoint": fg_ms[2].item(), "worlds_per_gpu": fg["B"],
+                     "gpu_launches_per_step": 2, "l2": "flushed between timed steps"},
         "kernel_ms": {"median": statistics.median(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
     }
     if world == 1 and not a.no_cpu_baseline:

@@ -83,8 +83,8 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 constexpr size_t SMEM = sizeof(World) * WPB;
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
-constexpr int AWPB = 1;  // worlds per block of k_adjoint
-struct AdjBlock { World s; Adj a; float cw[32][30]; };
+constexpr int AWPB = 2;  // worlds per block of k_adjoint (2 x 21.9 KB: 10 worlds per SM)
+struct AdjBlock { AWorld s; Adj a; };
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
 
 // tape: nw * nsub records; gq_out (B,36) / gv_out (B,35): cotangents of qpos' / qvel'; outputs gq_in (B,36) (qpos
@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
   const int w = blockIdx.x * AWPB + warp;
   if (w >= nw) return;
   AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
-  World& s = blk.s;
+  AWorld& s = blk.s;
   Adj& A = blk.a;
   const size_t w64 = (size_t)w;
   const float h = G1_TIMESTEP;
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
   __syncwarp();
   int flags = 0;
   for (int k = nsub - 1; k >= 0; k--)
-    flags |= adj_substep(s, A, tape + (w64 * nsub + k) * REC_WORDS, clamp_kv, clamp_soft, blk.cw, lane);
+    flags |= adj_substep(s, A, tape + (w64 * nsub + k) * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane);
   // the input qpos gradient in qpos form: (q_lin, 2 xi (0, q_rot), q_hinge), xi the input quaternion
   const float* first = tape + w64 * nsub * REC_WORDS;
   for (int i = lane; i < NV; i += 32) {

@@ -29,6 +29,18 @@ namespace nbg1 {
 
 enum : int { ADJ_REPLAY_MISMATCH = 1 << 13 };
 
+// The world quantities the adjoint replays from the tape (the members of World it uses, same names): ~5.3 KB of
+// shared memory per world instead of World's 22.5 KB
+struct __align__(16) AWorld {
+  float qpos[NQ], qvel[NV], qacc[NV], com[3], fric;
+  float Q[NB][4], X[NB][3];            // body poses
+  float L[NTRI], dinv[NV + 1];         // the tape's factor being solved with
+  struct { struct { float gx[NG][3], gq[NG][4]; } col; } u;  // geom poses
+  int ncon, nefc;
+  int con_pair[MAXCON];
+  unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
+};
+
 struct __align__(16) Adj {
   float lam[NV], y[NV], xa[NV], aadv[NV], vb[NV], qb[NV], ub[NU], qout[NV], tmp2[NV], u[NU];
   float ql[NV];                       // direct tangent cotangents (integrator, limits, actuators)
@@ -37,7 +49,10 @@ struct __align__(16) Adj {
   float dep[NB][24];                  // per body: G_lambda, G_a, G_v (wrenches at the origin), pose wrench
   float up[NB][18];                   // to the parent: its om, alA, aoA, alB, aoB cotangents and the relative-position
                                       // force rbar (applied as -rbar at the parent's origin)
-  float sub[NB][36];                  // subtree sums: W_A, W_B, G_lambda, G_a, G_v, P (6 each)
+  union {
+    float sub[NB][36];                // subtree sums: W_A, W_B, G_lambda, G_a, G_v, P (6 each) (the sweep)
+    float cw[32][30];                 // a batch of 32 contacts' wrenches (the contact phase, before the sweep)
+  };
   float ax[NV][3];                    // dof axes (world)
   unsigned clamp_lo, clamp_hi;
   int nlim_tape, flags, normal, pad_;  // normal: the self-contact normal derivative option (0..3)
@@ -45,7 +60,7 @@ struct __align__(16) Adj {
 
 // ---- replay ---------------------------------------------------------------------------------------------------------
 // poses, the dofs' axes and both channels' velocities / accelerations (lane = body, by depth level)
-__device__ __noinline__ void adj_replay_kin(World& s, Adj& A, int lane) {
+__device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
   const int b = lane;
   const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
   if (lane == 0) {
@@ -123,7 +138,7 @@ __device__ __noinline__ void adj_replay_kin(World& s, Adj& A, int lane) {
 
 // the motion of body b (angular, linear velocity of the world origin) for the generalised vector v: pointer jumping
 // over the ancestor dofs, with the motion vectors s_i = (w_i, X_b x w_i) (root translations: (0, e_k))
-__device__ __noinline__ void adj_motion(const World& s, const Adj& A, const float* v, float (*out)[6], int lane) {
+__device__ __noinline__ void adj_motion(const AWorld& s, const Adj& A, const float* v, float (*out)[6], int lane) {
   float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   int par = 0;
   if (lane == 1) {
@@ -195,7 +210,7 @@ __device__ __forceinline__ void impedance_d(const float* solimp, float pos, floa
 // Contacts (lane = contact): replay the tape's contact (pair, slot) from the geom poses, its rows' forces at the
 // tape's zones, the cotangents of J x for x = lambda, a*, v as forces at the contact point (deposited as wrenches on
 // the two bodies) and the geometry's pose wrenches. Returns the replay mismatch flag of this lane.
-__device__ __noinline__ int adj_contacts(World& s, Adj& A, const float* rec, float (*cw)[30], int c0, int lane) {
+__device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, float (*cw)[30], int c0, int lane) {
   const int ncon = s.ncon;
   const int c = c0 + lane;
   float out[30];
@@ -456,7 +471,7 @@ __device__ __noinline__ int adj_contacts(World& s, Adj& A, const float* rec, flo
 
 // lane = body: adds the batch's contact terms (contacts c0 .. c0 + 31, in contact order): G(x) with sign + on body 2,
 // - on body 1; the pose wrenches of each body's points
-__device__ __noinline__ void adj_contact_deposit(const World& s, Adj& A, const float (*cw)[30], int c0, int lane) {
+__device__ __noinline__ void adj_contact_deposit(const AWorld& s, Adj& A, const float (*cw)[30], int c0, int lane) {
   const int n = min(32, s.ncon - c0);
   if (lane < NB && lane > 0) {
     float acc[24];
@@ -480,7 +495,7 @@ __device__ __noinline__ void adj_contact_deposit(const World& s, Adj& A, const f
 
 // limit rows (lane = dof, dofs 6..NV-1): replay with the forward's test, force at the tape's zone; direct tangent
 // and velocity cotangents of the dof
-__device__ __noinline__ int adj_limits(World& s, Adj& A, const float* rec, int lane) {
+__device__ __noinline__ int adj_limits(AWorld& s, Adj& A, const float* rec, int lane) {
   const float h = G1_TIMESTEP;
   int nlim = 0, mismatch = 0;
   const unsigned below = (1u << lane) - 1u;
@@ -533,7 +548,7 @@ __device__ __forceinline__ float wrench_dot(const float* P, const float* w, cons
 // The leaf-to-root sweep (lane = body, deepest level first): each body's local reverse of both ID channels (its
 // COM acceleration, wrench and inertia), the velocity / acceleration recursion cotangents to its parent, the
 // subtree sums, and its dofs' tangent and velocity cotangents
-__device__ __noinline__ void adj_sweep(World& s, Adj& A, int lane) {
+__device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
   const int b = lane;
   const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
   const int nch = b < NB ? ldi(g1_body_nchild + b) : 0;
@@ -790,7 +805,7 @@ __device__ __noinline__ void adj_sweep(World& s, Adj& A, int lane) {
 
 // one substep of the adjoint: rec = its tape record; A.qout / A.vb in: the cotangents of the substep's output
 // (tangent, velocity); out: of its input (A.qout, A.vb); A.ub accumulates the ctrl gradient
-__device__ __noinline__ int adj_substep(World& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
+__device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
                                         float (*cw)[30], int lane) {
   const float h = G1_TIMESTEP;
   int flags = 0;

@@ -64,6 +64,15 @@ int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, cons
                   const float* gq_out, const float* gv_out, float* gq_in, float* gv_in, float* gctrl, int* info,
                   const float* ctrl, float clamp_soft, int clamp_kv, int normal);
 
+/* The full step Jacobian from a tape: jac (B,71,99) float32, row r = d(output r) / d(inputs) with the outputs
+ * qpos' (36, qpos form) then qvel' (35) and the inputs in the tangent basis: qpos tangent (35: root position, root
+ * rotation vector in the local frame, hinges), qvel (35), ctrl (29); info (B,) int32: the replay flags ORed over the
+ * rows. Arguments otherwise as nb_g1_adjoint; one launch (one warp per world and row). No counterpart in the
+ * reference's ABI: its Jacobian is 71 calls of `<pfx>_adjoint` with unit cotangents plus the qpos-to-tangent map
+ * (scripts/paper_bench/ours.py:99-110, benchmarks/bench/adapters/base.py:254-277); row r here equals that row. */
+int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
+                   float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal);
+
 /* nb_g1_forward plus the per-substep work counters stats (B, nsub, 8) int32: contacts kept, constraint rows, Newton
  * iterations, line-search evaluations, Hessian factorisations, broad-phase candidate pairs, contacts found, 0; the
  * outputs are bitwise those of nb_g1_forward. The counters feed the

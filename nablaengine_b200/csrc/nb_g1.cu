@@ -87,6 +87,52 @@ constexpr int AWPB = 2;  // worlds per block of k_adjoint (2 x 21.9 KB: 10 world
 struct AdjBlock { AWorld s; Adj a; };
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
 
+// One world's adjoint over its nsub records tw (w's first record): the output cotangent is (gq, gv) (qpos form, in
+// any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel') when unit >= 0.
+// Leaves the input cotangents in A.qout (dof tangent), A.vb, A.ub; returns the replay flags.
+__device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int nsub, float fric, const float* comw,
+                                      const float* ctrlw, const float* gq, const float* gv, int unit, int clamp_kv,
+                                      float clamp_soft, int normal, int lane) {
+  const float h = G1_TIMESTEP;
+  if (lane == 0) { s.fric = fric; A.normal = normal; }
+  if (lane < 3) s.com[lane] = comw[lane];
+  auto cq = [&](int i) { return unit >= 0 ? (i == unit ? 1.f : 0.f) : gq[i]; };
+  auto cv = [&](int i) { return unit >= 0 ? (i + NQ == unit ? 1.f : 0.f) : gv[i]; };
+  for (int i = lane; i < NU; i += 32) { A.u[i] = ctrlw ? ctrlw[i] : 0.f; A.ub[i] = 0.f; }
+  for (int i = lane; i < NV; i += 32) A.vb[i] = cv(i);
+  // the output cotangent in the dof tangent: the quaternion part at the output quaternion q' (re-integrated from the
+  // last record): 1/2 Im(q'* gq) / |q'|^2
+  const float* last = tw + (size_t)(nsub - 1) * REC_WORDS;
+  for (int i = lane; i < NV; i += 32)
+    if (i < 3 || i >= 6) A.qout[i] = cq(i < 3 ? i : i + 1);
+  if (lane == 0) {
+    float q[4] = {last[T_QPOS + 3], last[T_QPOS + 4], last[T_QPOS + 5], last[T_QPOS + 6]};
+    const float wv[3] = {last[T_QVEL + 3] + h * last[T_AADV + 3], last[T_QVEL + 4] + h * last[T_AADV + 4],
+                         last[T_QVEL + 5] + h * last[T_AADV + 5]};
+    const float nw = sqrtf(dot3(wv, wv));
+    if (nw > 0.f) {
+      float sa, ca;
+      sincosf(0.5f * h * nw, &sa, &ca);
+      const float dq[4] = {ca, sa * wv[0] / nw, sa * wv[1] / nw, sa * wv[2] / nw};
+      float o[4];
+      qmul(q, dq, o);
+      const float on = sqrtf(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      for (int k = 0; k < 4; k++) q[k] = o[k] / on;
+    }
+    const float g[4] = {cq(3), cq(4), cq(5), cq(6)};
+    const float qc[4] = {q[0], -q[1], -q[2], -q[3]};
+    float m[4];
+    qmul(qc, g, m);
+    const float n2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+    for (int k = 0; k < 3; k++) A.qout[3 + k] = 0.5f * m[1 + k] / n2;
+  }
+  __syncwarp();
+  int flags = 0;
+  for (int k = nsub - 1; k >= 0; k--)
+    flags |= adj_substep(s, A, tw + (size_t)k * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane);
+  return flags;
+}
+
 // tape: nw * nsub records; gq_out (B,36) / gv_out (B,35): cotangents of qpos' / qvel'; outputs gq_in (B,36) (qpos
 // form), gv_in (B,35), gctrl (B,29), info (B,) (replay mismatch bits); ctrl: the step's setpoints (clamp_kv 2 only)
 __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const float* __restrict__ tape,
@@ -104,43 +150,10 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
   AWorld& s = blk.s;
   Adj& A = blk.a;
   const size_t w64 = (size_t)w;
-  const float h = G1_TIMESTEP;
-  if (lane == 0) { s.fric = fric[w]; A.normal = normal; }
-  if (lane < 3) s.com[lane] = com[w64 * 3 + lane];
-  for (int i = lane; i < NU; i += 32) { A.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f; A.ub[i] = 0.f; }
-  for (int i = lane; i < NV; i += 32) A.vb[i] = gv_out[w64 * NV + i];
-  // the output cotangent in the dof tangent: the quaternion part at the output quaternion q' (re-integrated from the
-  // last record): 1/2 Im(q'* gq)
-  const float* last = tape + (w64 * nsub + nsub - 1) * REC_WORDS;
-  for (int i = lane; i < NV; i += 32)
-    if (i < 3 || i >= 6) A.qout[i] = gq_out[w64 * NQ + (i < 3 ? i : i + 1)];
-  if (lane == 0) {
-    float q[4] = {last[T_QPOS + 3], last[T_QPOS + 4], last[T_QPOS + 5], last[T_QPOS + 6]};
-    const float wv[3] = {last[T_QVEL + 3] + h * last[T_AADV + 3], last[T_QVEL + 4] + h * last[T_AADV + 4],
-                         last[T_QVEL + 5] + h * last[T_AADV + 5]};
-    const float nw = sqrtf(dot3(wv, wv));
-    if (nw > 0.f) {
-      float sa, ca;
-      sincosf(0.5f * h * nw, &sa, &ca);
-      const float dq[4] = {ca, sa * wv[0] / nw, sa * wv[1] / nw, sa * wv[2] / nw};
-      float o[4];
-      qmul(q, dq, o);
-      const float on = sqrtf(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
-      for (int k = 0; k < 4; k++) q[k] = o[k] / on;
-    }
-    const float g[4] = {gq_out[w64 * NQ + 3], gq_out[w64 * NQ + 4], gq_out[w64 * NQ + 5], gq_out[w64 * NQ + 6]};
-    const float qc[4] = {q[0], -q[1], -q[2], -q[3]};
-    float m[4];
-    qmul(qc, g, m);
-    const float n2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
-    for (int k = 0; k < 3; k++) A.qout[3 + k] = 0.5f * m[1 + k] / n2;
-  }
-  __syncwarp();
-  int flags = 0;
-  for (int k = nsub - 1; k >= 0; k--)
-    flags |= adj_substep(s, A, tape + (w64 * nsub + k) * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane);
+  const float* tw = tape + w64 * nsub * REC_WORDS;
+  const int flags = adj_world(s, A, tw, nsub, fric[w], com + w64 * 3, ctrl ? ctrl + w64 * NU : nullptr,
+                              gq_out + w64 * NQ, gv_out + w64 * NV, -1, clamp_kv, clamp_soft, normal, lane);
   // the input qpos gradient in qpos form: (q_lin, 2 xi (0, q_rot), q_hinge), xi the input quaternion
-  const float* first = tape + w64 * nsub * REC_WORDS;
   for (int i = lane; i < NV; i += 32) {
     if (i < 3) gq_in[w64 * NQ + i] = A.qout[i];
     else if (i >= 6) gq_in[w64 * NQ + i + 1] = A.qout[i];
@@ -148,13 +161,39 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
   }
   for (int i = lane; i < NU; i += 32) gctrl[w64 * NU + i] = A.ub[i];
   if (lane == 0) {
-    const float xi[4] = {first[T_QPOS + 3], first[T_QPOS + 4], first[T_QPOS + 5], first[T_QPOS + 6]};
+    const float xi[4] = {tw[T_QPOS + 3], tw[T_QPOS + 4], tw[T_QPOS + 5], tw[T_QPOS + 6]};
     const float t[4] = {0.f, A.qout[3], A.qout[4], A.qout[5]};
     float o[4];
     qmul(xi, t, o);
     for (int k = 0; k < 4; k++) gq_in[w64 * NQ + 3 + k] = 2.f * o[k];
     info[w] = flags;
   }
+}
+
+// The step Jacobian (B, 71, 99): row r = the VJP of output r (qpos' in qpos form 0..35, qvel' 36..70) in the
+// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). One warp per (world, row); a block holds AWPB rows of one
+// world (they read the same records). info (B,): the replay flags ORed over the rows (zeroed by the launcher).
+constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU;
+constexpr int JBLK = (JROWS + AWPB - 1) / AWPB;  // blocks per world
+__global__ void __launch_bounds__(AWPB * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
+                                                        const float* __restrict__ fric, const float* __restrict__ com,
+                                                        float* __restrict__ jac, int* __restrict__ info,
+                                                        const float* __restrict__ ctrl, float clamp_soft,
+                                                        int clamp_kv, int normal) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x / JBLK, row = (blockIdx.x % JBLK) * AWPB + warp;
+  if (w >= nw || row >= JROWS) return;
+  AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
+  const size_t w64 = (size_t)w;
+  const int flags = adj_world(blk.s, blk.a, tape + w64 * nsub * REC_WORDS, nsub, fric[w], com + w64 * 3,
+                              ctrl ? ctrl + w64 * NU : nullptr, nullptr, nullptr, row, clamp_kv, clamp_soft, normal,
+                              lane);
+  float* out = jac + (w64 * JROWS + row) * JCOLS;
+  const Adj& A = blk.a;
+  for (int i = lane; i < NV; i += 32) { out[i] = A.qout[i]; out[NV + i] = A.vb[i]; }
+  for (int i = lane; i < NU; i += 32) out[2 * NV + i] = A.ub[i];
+  if (lane == 0 && flags) atomicOr(info + w, flags);
 }
 static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
 
@@ -181,7 +220,23 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_adjoint, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
   return (int)e;
+}
+
+int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
+                   float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3)
+    return (int)cudaErrorInvalidValue;
+  if (nw == 0) return 0;
+  if (!tape || !friction || !com || !jac || !info) return (int)cudaErrorInvalidValue;
+  if (clamp_kv == 2 && !ctrl) return (int)cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(info, 0, sizeof(int) * (size_t)nw, stream);
+  if (e != cudaSuccess) return (int)e;
+  k_jacobian<<<(unsigned)nw * JBLK, AWPB * 32, ASMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
+                                                                 clamp_soft, clamp_kv, normal);
+  return (int)cudaGetLastError();
 }
 
 int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,

@@ -8,6 +8,7 @@ CUDA kernels of libnabla_g1.so on torch's current stream of the inputs' device.
       -> (qpos', qvel', warm', info[, tape])
   backward(tape, friction, com, g_qpos, g_qvel, *, substeps=4, clamp_kv=0, normal=3, ctrl=None, clamp_soft=None)
       -> (g_qpos, g_qvel, g_ctrl, info)
+  jacobian(tape, friction, com, *, substeps=4, clamp_kv=1, normal=0, ctrl=None, clamp_soft=None) -> (J, info)
   scale_grad(tree, gamma)
 
 Arguments as the reference: float32 CUDA tensors on one device, contiguous, leading dimension B (the worlds): qpos
@@ -165,6 +166,42 @@ def _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv
     if rc:
         raise _err(f"the adjoint launch failed (CUDA error {rc})", RuntimeError)
     return gq, gv, gu, info
+
+
+def jacobian(tape, friction, com, *, substeps=SUBSTEPS, clamp_kv=1, normal=0, ctrl=None, clamp_soft=None):
+    """The full step Jacobian from a forward's tape: (J (B, 71, 99) float32, info (B,) int32). Rows: qpos' (36, qpos
+    form) then qvel' (35); columns: qpos tangent (35), qvel (35), ctrl (29), each row the VJP of that output's unit
+    cotangent (the reference's 71-backward Jacobian, scripts/paper_bench/ours.py:99-110, with its tangent map), in one
+    launch. Defaults to the exact gradient mode (clamp_kv=1, normal=0)."""
+    import torch
+    soft = _soft(clamp_kv, clamp_soft)
+    if soft is not None and ctrl is None:
+        raise _err("clamp_kv=2 (the soft clamp) needs the step's ctrl", ValueError)
+    if not isinstance(tape, torch.Tensor) or tape.device.type != "cuda" or tape.dim() != 2:
+        _check("tape", tape, (getattr(tape, "shape", (0,))[0], substeps * _rec_words()), None)
+    B, dev = tape.shape[0], tape.device.index
+    for name, x, shape in (("tape", tape, (B, substeps * _rec_words())), ("friction", friction, (B,)),
+                           ("com", com, (B, 3))):
+        _check(name, x, shape, dev)
+    if int(normal) not in (0, 1, 2, 3) or not (1 <= substeps <= 32):
+        raise _err("normal in 0..3, substeps in 1..32", ValueError)
+    if soft is not None:
+        _check("ctrl", ctrl, (B, NU), dev)
+    if dev not in _READY:
+        init(dev)
+    J = torch.empty((B, NQ + NV, 2 * NV + NU), dtype=torch.float32, device=tape.device)
+    info = torch.empty((B,), dtype=torch.int32, device=tape.device)
+    if B == 0:
+        return J, info
+    lib = capi.load()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.nb_g1_jacobian(ctypes.c_void_p(st), B, int(substeps), _ptr(tape), _ptr(friction), _ptr(com),
+                                _ptr(J), _ptr(info), _ptr(ctrl if soft is not None else None),
+                                ctypes.c_float(0.0 if soft is None else soft), int(clamp_kv), int(normal))
+    if rc:
+        raise _err(f"the Jacobian launch failed (CUDA error {rc})", RuntimeError)
+    return J, info
 
 
 def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, tape=False):

@@ -9,6 +9,10 @@ The outputs are small subsets of the reference's Apache-2.0 benchmark data (benc
                    floor (h = 1e-7) in the tangent basis (qpos tangent 35, qvel 35, ctrl 29), validity bits, groups
   mjw_sample.npz   the first 256 states of mf_s0 with MuJoCo Warp 3.17's one-step outputs (50 iterations, float32)
                    and its per-substep contact / row / iteration counts
+  truth_jac.npz    16 of mf_s0's Jacobian states (the G0 sample): inputs, the MuJoCo C float64 FD Jacobian (71 x 99,
+                   stored float32 by the reference, h = 1e-6, tangent columns), its per-column floor, validity bits
+
+Existing files are kept unless --force is given (each is written once; the tests pin their contents).
 
 Nothing at test time reads the reference; the tests read these files.
 """
@@ -24,9 +28,23 @@ INPUTS = ("qpos", "qvel", "qacc_warmstart", "ctrl", "friction", "com")
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="the reference repository root")
+    ap.add_argument("--force", action="store_true", help="rewrite files that exist")
     a = ap.parse_args()
     ref = Path(a.ref)
     data = ref / "benchmarks" / "data"
+    write = lambda name: a.force or not (HERE / name).exists()  # noqa: E731
+    if write("truth_jac.npz"):
+        c, t = np.load(data / "mf_s0.npz"), np.load(data / "truth" / "mf_s0.npz")
+        n = 16
+        pos = t["jac_index"][:n]  # positions into the gradient states
+        jidx = t["index"][pos]     # corpus states
+        jac = {k: c[k][jidx] for k in INPUTS}
+        jac.update(index=jidx, jacobian=t["jacobian"][:n], jacobian_dcol=t["jacobian_dcol"][:n], bad=t["bad"][pos],
+                   model_flags=t["model_flags"][jidx])
+        np.savez_compressed(HERE / "truth_jac.npz", **jac)
+        print("truth_jac.npz", (HERE / "truth_jac.npz").stat().st_size, "bytes")
+    if not write("truth_check.npz"):
+        return
     out = {k: [] for k in INPUTS + ("check_out", "model_flags", "corpus", "index")}
     for s in range(4):
         c, t = np.load(data / f"mf_s{s}.npz"), np.load(data / "truth" / f"mf_s{s}.npz")

@@ -1,0 +1,107 @@
+"""The full step Jacobian (B, 71, 99) on the GPU (nb_g1_jacobian / torch_ffi.jacobian).
+
+Parity: against the reference's MuJoCo C float64 FD Jacobian (truth_jac.npz, 16 G0 states; the reference's scorer
+benchmarks/bench/accuracy/gradient.py jacobian_errors: Frobenius relative error per input block, floored at the
+truth's per-column floor), against the float64 oracle's central differences on synthetic multi-contact states, and
+row by row against the VJP entry (the reference's Jacobian is 71 backward calls, scripts/paper_bench/ours.py:99-110).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+KEYS = ("qpos", "qvel", "qacc_warmstart", "ctrl", "friction", "com")
+BLOCKS = dict(qpos=slice(0, 35), qvel=slice(35, 70), ctrl=slice(70, 99))
+# Frobenius relative error bounds per block (the gradient check's p99 bounds, scripts/gradient_check.py:53)
+BOUND = dict(qpos=2e-3, qvel=5e-4, ctrl=1e-4)
+
+
+def _cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _frob(J, Jt, floor_cols=None):
+    out = {}
+    for name, sl in BLOCKS.items():
+        e = np.linalg.norm((J[:, :, sl] - Jt[:, :, sl]).reshape(len(J), -1), axis=1)
+        if floor_cols is not None:
+            e = np.maximum(e, np.linalg.norm(floor_cols[:, sl], axis=1))
+        out[name] = e / np.maximum(np.linalg.norm(Jt[:, :, sl].reshape(len(J), -1), axis=1), 1e-9)
+    return out
+
+
+def test_jacobian_matches_mujoco_fd_truth(golden):
+    torch = _cuda()
+    from nablaengine_b200 import torch_ffi
+    d = golden("truth_jac.npz")
+    t = [torch.from_numpy(np.ascontiguousarray(d[k], np.float32)).cuda() for k in KEYS]
+    tape = torch_ffi.forward(*t, iterations=50, tape=True)[4]
+    J, info = torch_ffi.jacobian(tape, t[4], t[5])
+    J = J.cpu().numpy().astype(np.float64)
+    assert np.isfinite(J).all() and (info.cpu().numpy() & (1 << 13)).sum() == 0
+    err = _frob(J, d["jacobian"].astype(np.float64), d["jacobian_dcol"].astype(np.float64))
+    print({k: (float(np.median(v)), float(v.max())) for k, v in err.items()})
+    for name, e in err.items():
+        assert e.max() <= BOUND[name], (name, e)
+
+
+def test_jacobian_matches_oracle_fd_on_synthetic_states():
+    torch = _cuda()
+    import oracle
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("vjp", B=8)
+    s["qpos"][:4, 2] -= 0.1  # multi-contact feet
+    keys = ("qpos", "qvel", "warm", "ctrl", "friction", "com")
+    Jf = oracle.fd_jacobian(*(s[k] for k in keys))
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda() for k in keys]
+    tape = torch_ffi.forward(*t, iterations=50, tape=True)[4]
+    J = torch_ffi.jacobian(tape, t[4], t[5])[0].cpu().numpy().astype(np.float64)
+    err = _frob(J, Jf)
+    print({k: (float(np.median(v)), float(v.max())) for k, v in err.items()})
+    for name, e in err.items():
+        assert np.median(e) <= BOUND[name], (name, e)
+
+
+def test_jacobian_rows_equal_the_vjp_of_unit_cotangents(golden):
+    torch = _cuda()
+    from nablaengine_b200 import torch_ffi
+    d = golden("truth_jac.npz")
+    t = [torch.from_numpy(np.ascontiguousarray(d[k], np.float32)).cuda() for k in KEYS]
+    tape = torch_ffi.forward(*t, tape=True)[4]
+    J = torch_ffi.jacobian(tape, t[4], t[5], clamp_kv=0, normal=3)[0]
+    B = J.shape[0]
+    xi = t[0][:, 3:7].double()
+    for r in (0, 4, 12, 40, 70):
+        cq, cv = torch.zeros(B, 36, device="cuda"), torch.zeros(B, 35, device="cuda")
+        if r < 36:
+            cq[:, r] = 1.0
+        else:
+            cv[:, r - 36] = 1.0
+        gq, gv, gu, _ = torch_ffi.backward(tape, t[4], t[5], cq, cv)
+        assert torch.equal(J[:, r, 35:70], gv) and torch.equal(J[:, r, 70:], gu)
+        # the qpos block: qpos form -> tangent, 1/2 Im(xi* (x) g) / |xi|^2
+        g = gq.double()
+        w, x, y, z = xi.unbind(1)
+        a, b, c, e = g[:, 3:7].unbind(1)
+        rot = 0.5 * torch.stack([w * b - x * a - y * e + z * c, w * c + x * e - y * a - z * b,
+                                 w * e - x * c + y * b - z * a], 1) / (xi * xi).sum(1, keepdim=True)
+        tan = torch.cat([g[:, :3], rot, g[:, 7:]], 1)
+        err = (J[:, r, :35].double() - tan).norm(dim=1) / tan.norm(dim=1).clamp_min(1e-9)
+        assert float(err.max()) < 1e-5, (r, err)
+
+
+def test_jacobian_argument_errors(golden):
+    torch = _cuda()
+    from nablaengine_b200 import torch_ffi
+    d = golden("truth_jac.npz")
+    t = [torch.from_numpy(np.ascontiguousarray(d[k][:2], np.float32)).cuda() for k in KEYS]
+    tape = torch_ffi.forward(*t, tape=True)[4]
+    with pytest.raises(TypeError):
+        torch_ffi.jacobian(tape.double(), t[4], t[5])
+    with pytest.raises(ValueError):
+        torch_ffi.jacobian(tape, t[4], t[5], clamp_kv=2)
+    J, info = torch_ffi.jacobian(tape[:0], t[4][:0], t[5][:0])
+    assert J.shape == (0, 71, 99)

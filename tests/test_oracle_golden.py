@@ -84,3 +84,21 @@ def test_oracle_fd_matches_truth_vjp(golden, h):
             valid = g["bad"][w] == 0
             err = np.abs(vjp - truth)[valid] / (np.abs(truth[valid]) + 1e-3 * np.abs(truth).max())
             assert np.median(err) < 1e-5, (w, c, np.median(err))
+
+
+def test_oracle_fd_jacobian_matches_mujoco_jacobian_truth(golden):
+    """The oracle's central-difference Jacobian (h = 1e-6, converged) against the reference's MuJoCo C float64 FD
+    Jacobian of 16 G0 states (truth_jac.npz): Frobenius relative error per input block, floored at the truth's own
+    per-column floor |J(1e-6) - J(1e-7)| (benchmarks/bench/accuracy/gradient.py jacobian_errors)."""
+    import numpy as np
+    import oracle
+    d = golden("truth_jac.npz")
+    J = oracle.fd_jacobian(d["qpos"], d["qvel"], d["qacc_warmstart"], d["ctrl"], d["friction"], d["com"])
+    Jt = d["jacobian"].astype(np.float64)
+    for sl in (slice(0, 35), slice(35, 70), slice(70, 99)):
+        e = np.linalg.norm((J[:, :, sl] - Jt[:, :, sl]).reshape(len(J), -1), axis=1)
+        nt = np.linalg.norm(Jt[:, :, sl].reshape(len(J), -1), axis=1)
+        floor = np.linalg.norm(d["jacobian_dcol"][:, sl], axis=1)
+        err = np.maximum(e, floor) / nt
+        assert np.median(err) < 1e-5, (sl, err)
+        assert err.max() < 1e-4, (sl, err)

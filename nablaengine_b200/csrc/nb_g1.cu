@@ -3,6 +3,7 @@
 // k_forward: one warp per world, WPB worlds per block, each world's whole control step (nsub substeps) in one
 // launch with its state resident in shared memory (nb_g1_step.cuh), so a step is a single kernel per call.
 #include "../../include/nabla_g1.h"
+#include <cstddef>
 #include "nb_g1_step.cuh"
 #include "nb_g1_adjoint.cuh"
 
@@ -47,15 +48,18 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   for (int k = 0; k < nsub; k++) {
     float* rec = tape && active ? tape + (w64 * nsub + k) * REC_WORDS : nullptr;
     if (active) substep_pre(s, lane, rec);
-    while (true) {
-      const bool done = !active || s.ndone || s.nit_cur >= iterations;
 #if NB_LOCKSTEP
-      if (__syncthreads_and(done)) break;
-#else
-      if (done) break;
-#endif
-      if (!done) newton_iter(s, lane);
+    // rounds of up to NB_LOCKSTEP iterations per world, a block barrier after each round
+    while (true) {
+      for (int q = 0; q < NB_LOCKSTEP; q++) {
+        if (uall(!active || s.ndone || s.nit_cur >= iterations)) break;
+        newton_iter(s, lane);
+      }
+      if (__syncthreads_and(!active || s.ndone || s.nit_cur >= iterations)) break;
     }
+#else
+    while (!uall(!active || s.ndone || s.nit_cur >= iterations)) newton_iter(s, lane);
+#endif
     if (active) substep_post(s, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr, rec);
   }
   if (!active) return;
@@ -196,6 +200,7 @@ __global__ void __launch_bounds__(AWPB * 32) k_jacobian(int nw, int nsub, const 
   if (lane == 0 && flags) atomicOr(info + w, flags);
 }
 static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
+static_assert(offsetof(World, M) % 16 == 0 && offsetof(World, L) % 16 == 0, "float4 copies of the triangles");
 
 }  // namespace nbg1
 

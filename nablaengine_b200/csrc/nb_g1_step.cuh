@@ -28,6 +28,7 @@ constexpr int NQ = G1_NQ, NV = G1_NV, NU = G1_NU, NB = G1_NBODY, NG = G1_NGEOM, 
 constexpr int MAXCON = 64, NEFC = 192, KDOF = 16, MAXD = G1_MAXDEPTH;
 static_assert(G1_NV == G1_NBODY + 4, "dof d >= 6 is the hinge of body d - 4 (one hinge per body after the root)");
 constexpr int NTRI = NV * (NV + 1) / 2;
+constexpr int NTRIP = (NTRI + 3) / 4 * 4;  // the packed triangles' storage in World: whole float4s
 constexpr unsigned FULL = 0xffffffffu;
 constexpr int ROWS_PER_LANE = (NEFC + 31) / 32;
 __host__ __device__ constexpr int TRI(int i, int j) { return i * (i + 1) / 2 + j; }  // packed lower triangle, j <= i
@@ -66,7 +67,7 @@ struct __align__(16) World {
   float Q[NB][4], X[NB][3];            // body poses
   float dw[NV][3], dv[NV][3];          // dof motion about O: angular axis, velocity of the point O
   float BV[NB][6];                     // body spatial motion at O (angular, linear) for a generalised vector
-  float M[NTRI], L[NTRI];              // mass matrix (with armature), factor scratch
+  float M[NTRIP], L[NTRIP];            // mass matrix (with armature), factor scratch (16-byte aligned)
   float qsm[NV], qacc0[NV], Ma[NV], grad[NV], p[NV], Mp[NV], tmp[NV], dinv[NV + 1];
   union {
     struct { float om[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
@@ -126,6 +127,11 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
   return v;
 }
+// Values that are the same on every lane of the warp (a count in shared memory, a warp_sum result; the xor butterfly
+// gives every lane the same bits) made provably uniform for the compiler, so branches on them need no divergence
+// handling around the shuffles they enclose: uni for counts >= 0, uall for conditions
+__device__ __forceinline__ int uni(int x) { return (int)__reduce_max_sync(FULL, (unsigned)x); }
+__device__ __forceinline__ bool uall(bool c) { return __all_sync(FULL, c); }
 __device__ __forceinline__ float ld(const float* p) { return __ldg(p); }
 __device__ __forceinline__ int ldi(const int* p) { return __ldg(p); }
 
@@ -314,7 +320,7 @@ __device__ __forceinline__ void apply_inertia(const float* J, const float* w, co
 
 // mass matrix rows (lane = dof: entries with its ancestor dofs) and qfrc_smooth = clamped actuator force - bias
 __device__ __noinline__ void mass_and_force(World& s, int lane) {
-  for (int e = lane; e < NTRI; e += 32) s.M[e] = 0.f;
+  for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(s.M)[e] = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncwarp();
   for (int i = lane; i < NV; i += 32) {
     const int b = ldi(g1_dof_body + i);
@@ -380,13 +386,29 @@ __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, 
     if (r < NV && k0 > 0) {
       const float* Li = L + TRI(r, 0);
       const float* L0 = L + TRI(k0, 0);
+      // k0 is a multiple of 4: four j at a time, their 20 loads issued together; row k0 + 1 starts k0 + 1 entries
+      // after row k0, row k0 + 2 at 2 k0 + 3, row k0 + 3 at 3 k0 + 6 (rows past NV - 1 are not read)
+      const float* L1 = L0 + (k0 + 1);
+      const float* L2 = L0 + (2 * k0 + 3);
+      const float* L3 = L0 + (3 * k0 + 6);
 #pragma unroll 1
-      for (int j = 0; j < k0; j++) {
-        const float lij = Li[j];
-        S[0] += lij * L0[j];
-        if (nb > 1) S[1] += lij * L0[(k0 + 1) + j];        // row k0 + 1 starts k0 + 1 entries after row k0
-        if (nb > 2) S[2] += lij * L0[(2 * k0 + 3) + j];    // row k0 + 2
-        if (nb > 3) S[3] += lij * L0[(3 * k0 + 6) + j];    // row k0 + 3
+      for (int j = 0; j < k0; j += 4) {
+        float li[4], a0[4], a1[4], a2[4], a3[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          li[q] = Li[j + q];
+          a0[q] = L0[j + q];
+          a1[q] = nb > 1 ? L1[j + q] : 0.f;
+          a2[q] = nb > 2 ? L2[j + q] : 0.f;
+          a3[q] = nb > 3 ? L3[j + q] : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          S[0] += li[q] * a0[q];
+          S[1] += li[q] * a1[q];
+          S[2] += li[q] * a2[q];
+          S[3] += li[q] * a3[q];
+        }
       }
     }
     // phase 2: the block's columns in order; lane l keeps its row's new entries lo[c] (and the second row's, lt[c])
@@ -753,7 +775,7 @@ __device__ __noinline__ void collision(World& s, int lane) {
 // support and the sign of every Jacobian column, so the Hessian and J' f treat a group as one spatial stiffness /
 // one wrench
 __device__ __noinline__ void contact_setup(World& s, int lane) {
-  const int ncon = s.ncon;
+  const int ncon = uni(s.ncon);
   const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
   __syncwarp();
   for (int c = lane; c < ncon; c += 32) {
@@ -915,7 +937,7 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
   // contact rows need J qvel
   body_motion(s, s.qvel, lane);
   contact_jv(s, lane);
-  const int ncon = s.ncon;
+  const int ncon = uni(s.ncon);
   int r0 = nlim;
   for (int c0 = 0; c0 < ncon; c0 += 32) {
     const int c = c0 + lane;
@@ -989,7 +1011,7 @@ __device__ __noinline__ float total_cost(World& s, int lane) {
 // wrench at O from its rows' forces, summed per group (members in contact order), then per dof the groups whose
 // support holds it (sign +1 on body 2's chain, -1 on body 1's) and the dof's limit row
 __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
-  const int ncon = s.ncon, ngroup = s.ngroup;
+  const int ncon = uni(s.ncon), ngroup = uni(s.ngroup);
   for (int c = lane; c < ncon; c += 32) {
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
     float f[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1066,8 +1088,8 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
 // 3 x 6 rows (moment, frame) and S the dofs' motion vectors, so a group of contacts adds S' K S with the 6 x 6
 // spatial stiffness K = sum G' C G, on the group's support with the columns' signs
 __device__ __noinline__ void hessian(World& s, int lane) {
-  const int ncon = s.ncon, ngroup = s.ngroup;
-  for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
+  const int ncon = uni(s.ncon), ngroup = uni(s.ngroup);
+  for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(s.L)[e] = reinterpret_cast<const float4*>(s.M)[e];
   for (int c = lane; c < ncon; c += 32) {
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
     float d[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1083,9 +1105,11 @@ __device__ __noinline__ void hessian(World& s, int lane) {
   for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
     if (s.efc_jar[r] < 0.f) s.L[TRI(s.efc_a[r], s.efc_a[r])] += s.efc_D[r];
   __syncwarp();
+  PROF(s, 21);
   for (int g = 0; g < ngroup; g++) {
     const unsigned long long gm = s.grp_mask[g];
     // K (upper triangle of 6 x 6, entry e = (e1, e2)), lane e < 21, summed over the members in contact order
+    bool any = false;
     if (lane < 21) {
       int e1 = 0, rest = lane;
       while (rest >= 6 - e1) { rest -= 6 - e1; e1++; }
@@ -1111,14 +1135,14 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       s.u.hs.K[lane] = acc;
     }
     __syncwarp();
+    for (int e = 0; e < 21; e++) any |= s.u.hs.K[e] != 0.f;
+    __syncwarp();
+    PROF(s, 22);
     const int lead = __ffsll((long long)gm) - 1;
     unsigned long long m1, m2;
     pair_masks(s.con_pair[lead], &m1, &m2);
     const unsigned long long sup = m1 | m2;
-    bool any = false;
-    for (int e = 0; e < 21; e++) any |= s.u.hs.K[e] != 0.f;
-    __syncwarp();
-    if (!any) continue;  // (uniform) no quadratic row in the group
+    if (uall(!any)) continue;  // no quadratic row in the group
     const int nsup = __popcll(sup);
     // P_k = K s_i for the support dofs i (rank k: the k-th set bit of the support), signed
     {
@@ -1163,6 +1187,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       s.L[TRI(da, db)] += v;
     }
     __syncwarp();
+    PROF(s, 23);
   }
 }
 
@@ -1180,7 +1205,7 @@ __device__ __noinline__ void newton_begin(World& s, int lane) {
   __syncwarp();
   refresh(s, lane);
   const float cost0 = total_cost(s, lane);
-  if (cost0 > cost) {
+  if (uall(cost0 > cost)) {
     for (int i = lane; i < NV; i += 32) { s.qacc[i] = s.tmp[i]; s.Ma[i] = s.p[i]; }
     for (int r = lane; r < s.nefc; r += 32) s.efc_jar[r] = s.efc_jv[r];
     __syncwarp();
@@ -1195,7 +1220,7 @@ __device__ __noinline__ void newton_begin(World& s, int lane) {
 __device__ __noinline__ void newton_iter(World& s, int lane) {
   const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
   const float cost = s.ncost;
-  if (!s.nsame) {  // (no row changed its zone in the last step: H and its factor in s.L are still exact)
+  if (uall(!s.nsame)) {  // (no row changed its zone in the last step: H and its factor in s.L are still exact)
     if (lane == 0) s.nfact++;
     hessian(s, lane);
     PROF(s, 7);
@@ -1213,7 +1238,7 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
   for (int i = lane; i < NV; i += 32) { a1 += (s.Ma[i] - s.qsm[i]) * s.p[i]; a2 += s.p[i] * s.Mp[i]; }
   a1 = warp_sum(a1);
   a2 = warp_sum(a2);
-  const int nefc = s.nefc;
+  const int nefc = uni(s.nefc);
   float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE];
 #pragma unroll
   for (int t = 0; t < ROWS_PER_LANE; t++) {
@@ -1240,8 +1265,8 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
     if (lane == 0) s.nls++;
     fd = warp_sum(fd) + a1 + alpha * a2;
     fdd = warp_sum(fdd) + a2;
-    if (k == 0) { d0 = fd; if (d0 >= 0.f) break; }
-    if (fabsf(fd) <= 1e-7f * fabsf(d0)) break;
+    if (k == 0) { d0 = fd; if (uall(d0 >= 0.f)) break; }
+    if (uall(fabsf(fd) <= 1e-7f * fabsf(d0))) break;
     if (fd < 0.f) lo = alpha; else hi = alpha;
     float nx = alpha - fd / fdd;
     nwt = nx > lo && nx < hi;

@@ -10,7 +10,7 @@
 namespace nbg1 {
 
 #ifndef NB_WPB
-#define NB_WPB 5
+#define NB_WPB 10
 #endif
 #ifndef NB_LOCKSTEP
 #define NB_LOCKSTEP 1
@@ -18,7 +18,9 @@ namespace nbg1 {
 constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // NB_LOCKSTEP: the worlds of a block run their Newton iterations in lockstep (a block barrier per iteration): the
 // warps of an SM then fetch the same instructions at the same time, instead of each streaming the ~50 KB Newton loop
-// from its own position (the kernel is bound by instruction fetch otherwise)
+// from its own position (the kernel is bound by instruction fetch otherwise). WPB = 10: one block of 10 worlds
+// (220 KB of shared memory) per SM, so the whole SM runs one instruction stream (measured: 4.06 ms at B = 4096
+// against 4.27 ms with two blocks of 5).
 constexpr int TAPE_WORDS = REC_WORDS;
 constexpr long long ABI_VERSION = 1;
 
@@ -87,9 +89,12 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 constexpr size_t SMEM = sizeof(World) * WPB;
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
-constexpr int AWPB = 2;  // worlds per block of k_adjoint (2 x 21.9 KB: 10 worlds per SM)
+// worlds per block of k_adjoint (21.9 KB each: 9 per SM) and rows (warps) per block of k_jacobian (10 rows of one
+// world: 10 warps per SM sharing the world's records in L1 and their instruction stream); measured at B = 4096:
+// adjoint 1.04 ms (against 1.12 with 2 worlds per block), Jacobian 12.7 ms per 1024 worlds (14.2 with 2 rows)
+constexpr int AWPB = 1, JWPB = 10;
 struct AdjBlock { AWorld s; Adj a; };
-constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
+constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB, JSMEM = sizeof(AdjBlock) * JWPB;
 
 // One world's adjoint over its nsub records tw (w's first record): the output cotangent is (gq, gv) (qpos form, in
 // any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel') when unit >= 0.
@@ -175,18 +180,18 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
 }
 
 // The step Jacobian (B, 71, 99): row r = the VJP of output r (qpos' in qpos form 0..35, qvel' 36..70) in the
-// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). One warp per (world, row); a block holds AWPB rows of one
+// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). One warp per (world, row); a block holds JWPB rows of one
 // world (they read the same records). info (B,): the replay flags ORed over the rows (zeroed by the launcher).
 constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU;
-constexpr int JBLK = (JROWS + AWPB - 1) / AWPB;  // blocks per world
-__global__ void __launch_bounds__(AWPB * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
+constexpr int JBLK = (JROWS + JWPB - 1) / JWPB;  // blocks per world
+__global__ void __launch_bounds__(JWPB * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
                                                         const float* __restrict__ fric, const float* __restrict__ com,
                                                         float* __restrict__ jac, int* __restrict__ info,
                                                         const float* __restrict__ ctrl, float clamp_soft,
                                                         int clamp_kv, int normal) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w = blockIdx.x / JBLK, row = (blockIdx.x % JBLK) * AWPB + warp;
+  const int w = blockIdx.x / JBLK, row = (blockIdx.x % JBLK) * JWPB + warp;
   if (w >= nw || row >= JROWS) return;
   AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
   const size_t w64 = (size_t)w;
@@ -226,7 +231,7 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_adjoint, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+    e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)JSMEM);
   return (int)e;
 }
 
@@ -239,7 +244,7 @@ int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, con
   if (clamp_kv == 2 && !ctrl) return (int)cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(info, 0, sizeof(int) * (size_t)nw, stream);
   if (e != cudaSuccess) return (int)e;
-  k_jacobian<<<(unsigned)nw * JBLK, AWPB * 32, ASMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
+  k_jacobian<<<(unsigned)nw * JBLK, JWPB * 32, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
                                                                  clamp_soft, clamp_kv, normal);
   return (int)cudaGetLastError();
 }

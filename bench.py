@@ -164,6 +164,35 @@ def measure_fwd_grad(dev, rank, steps, warmup, flush):
     return {"B": B, "ms": ms, "ms_fwd_tape": ms_fwd_tape, "ms_adjoint": ms_bwd}
 
 
+def measure_jacobian(dev, rank, steps, warmup, flush):
+    """the full 71 x 99 step Jacobian of 4096 worlds (forward with tape, then the Jacobian
+    kernel, exact mode), device time per step with the L2 flushed between steps; us per world."""
+    import torch
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("jacobian", seed_offset=rank)
+    x = [torch.from_numpy(s[k]).to(dev) for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    B = x[0].shape[0]
+    st = torch.cuda.current_stream(dev)
+
+    def one():
+        tape = torch_ffi.forward(*x, iterations=ITERATIONS, substeps=SUBSTEPS, tape=True)[4]
+        return torch_ffi.jacobian(tape, x[4], x[5], substeps=SUBSTEPS)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        one()
+        e1.record(st)
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    return {"B": B, "ms": tot / steps}
+
+
 def run_reference(a, rank):
     """--impl reference: rank 0 times the reference's CPU path substitute (the float64 oracle port) per step on a
     bounded sample of the configuration-2 workload."""
@@ -260,7 +289,9 @@ def main():
     kern_ms = [e0.elapsed_time(e1) for e0, e1 in ev]
     total = torch.tensor([sum(kern_ms)], dtype=torch.float64, device=dev)
     fg = measure_fwd_grad(dev, rank, a.steps, a.warmup, flush)
-    fg_ms = torch.tensor([fg["ms"], fg["ms_fwd_tape"], fg["ms_adjoint"]], dtype=torch.float64, device=dev)
+    jac = measure_jacobian(dev, rank, max(1, min(a.steps, 3)), 1, flush)
+    fg_ms = torch.tensor([fg["ms"], fg["ms_fwd_tape"], fg["ms_adjoint"], jac["ms"]], dtype=torch.float64,
+                         device=dev)
 
     # end to end through the public API: pinned host inputs in, host outputs back, every step
     host = [t.cpu().pin_memory() for t in x]
@@ -334,6 +365,11 @@ def main():
                      "ms_per_step": fg_ms[0].item(), "ms_forward_with_tape": fg_ms[1].item(),
                      "ms_adjoint": fg_ms[2].item(), "worlds_per_gpu": fg["B"],
                      "gpu_launches_per_step": 2, "l2": "flushed between timed steps"},
+        "jacobian": {"metric": "full 71 x 99 step Jacobian (forward with tape + Jacobian kernel, exact mode), us per "
+                               "world at B=4096/GPU (BASELINE configuration 4)",
+                     "value": fg_ms[3].item() * 1e3 / jac["B"], "unit": "us/world", "higher_is_better": False,
+                     "ms_per_step": fg_ms[3].item(), "worlds_per_gpu": jac["B"], "gpu_launches_per_step": 2,
+                     "l2": "flushed between timed steps"},
         "kernel_ms": {"median": statistics.median(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
     }
     if world == 1 and not a.no_cpu_baseline:

@@ -73,6 +73,20 @@ int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, cons
 int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
                    float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal);
 
+/* The kinematics outputs of nw states (qpos (B,36), qvel (B,35), com (B,3)): qpos_n (B,36) (the root quaternion
+ * normalised), xpos (B,31,3) and xquat (B,31,4) (body frames, the world body included), cvel (B,31,6) ([angular;
+ * linear] twist of each body at the root's subtree COM), subtree_com (B,31,3). Replaces `<pfx>_kinematics`
+ * (src/nablaengine/jax_ffi.py:281-286; semantics src/nablaengine/g1_engine/kinematics.py:1-47). */
+int nb_g1_kinematics(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* com,
+                     float* qpos_n, float* xpos, float* xquat, float* cvel, float* subtree_com);
+
+/* Their VJP: the cotangents of the five outputs (same layouts) -> gq (B,36) (qpos form) and gv (B,35) of (qpos, qvel);
+ * gq_in / gv_in (may be NULL) are added last (a step's outputs' own cotangents). com gets no gradient. Replaces
+ * `<pfx>_kinematics_vjp` (src/nablaengine/jax_ffi.py:287-292). */
+int nb_g1_kinematics_vjp(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* com,
+                         const float* g_qpos_n, const float* g_xpos, const float* g_xquat, const float* g_cvel,
+                         const float* g_subtree_com, const float* gq_in, const float* gv_in, float* gq, float* gv);
+
 /* nb_g1_forward plus the per-substep work counters stats (B, nsub, 8) int32: contacts kept, constraint rows, Newton
  * iterations, line-search evaluations, Hessian factorisations, broad-phase candidate pairs, contacts found, 0; the
  * outputs are bitwise those of nb_g1_forward. The counters feed the

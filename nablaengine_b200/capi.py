@@ -11,7 +11,7 @@ from . import build as _build
 
 HEADER = Path(__file__).resolve().parents[1] / "include" / "nabla_g1.h"
 EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward", "nb_g1_forward_stats",
-           "nb_g1_adjoint", "nb_g1_jacobian")
+           "nb_g1_adjoint", "nb_g1_jacobian", "nb_g1_kinematics", "nb_g1_kinematics_vjp")
 ABI_VERSION = 1
 NQ, NV, NU, NBODY, MAXCON, NEFC = 36, 35, 29, 31, 64, 192
 
@@ -52,6 +52,8 @@ def load(path=None, build_if_missing=True):
         lib.nb_g1_adjoint.restype = i32
         lib.nb_g1_jacobian.argtypes = [vp, i32, i32] + [vp] * 6 + [ctypes.c_float, i32, i32]
         lib.nb_g1_jacobian.restype = i32
+        lib.nb_g1_kinematics.argtypes, lib.nb_g1_kinematics.restype = [vp, i32] + [vp] * 8, i32
+        lib.nb_g1_kinematics_vjp.argtypes, lib.nb_g1_kinematics_vjp.restype = [vp, i32] + [vp] * 12, i32
         sizes = (ctypes.c_longlong * 8)()
         lib.nb_g1_sizes(sizes)
         want = (NQ, NV, NU, NBODY, MAXCON, NEFC)

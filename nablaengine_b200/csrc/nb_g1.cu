@@ -6,6 +6,7 @@
 #include <cstddef>
 #include "nb_g1_step.cuh"
 #include "nb_g1_adjoint.cuh"
+#include "nb_g1_kin.cuh"
 
 namespace nbg1 {
 
@@ -233,6 +234,27 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)JSMEM);
   return (int)e;
+}
+
+int nb_g1_kinematics(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* com,
+                     float* qpos_n, float* xpos, float* xquat, float* cvel, float* subtree_com) {
+  if (nw < 0) return (int)cudaErrorInvalidValue;
+  if (nw == 0) return 0;
+  if (!qpos || !qvel || !com || !qpos_n || !xpos || !xquat || !cvel || !subtree_com) return (int)cudaErrorInvalidValue;
+  k_kin<<<(nw + KWPB - 1) / KWPB, KWPB * 32, 0, stream>>>(nw, qpos, qvel, com, qpos_n, xpos, xquat, cvel, subtree_com);
+  return (int)cudaGetLastError();
+}
+
+int nb_g1_kinematics_vjp(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* com,
+                         const float* g_qpos_n, const float* g_xpos, const float* g_xquat, const float* g_cvel,
+                         const float* g_subtree_com, const float* gq_in, const float* gv_in, float* gq, float* gv) {
+  if (nw < 0) return (int)cudaErrorInvalidValue;
+  if (nw == 0) return 0;
+  if (!qpos || !qvel || !com || !g_qpos_n || !g_xpos || !g_xquat || !g_cvel || !g_subtree_com || !gq || !gv)
+    return (int)cudaErrorInvalidValue;
+  k_kin_vjp<<<(nw + KWPB - 1) / KWPB, KWPB * 32, 0, stream>>>(nw, qpos, qvel, com, g_qpos_n, g_xpos, g_xquat, g_cvel,
+                                                              g_subtree_com, gq_in, gv_in, gq, gv);
+  return (int)cudaGetLastError();
 }
 
 int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,

@@ -3,9 +3,10 @@
 CUDA kernels of libnabla_g1.so on torch's current stream of the inputs' device.
 
   step(qpos, qvel, warm, ctrl, friction, com, *, iterations=10, substeps=4, clamp_kv=0, normal=3, clamp_soft=None,
-       grad_decay=1.0) -> (qpos', qvel', warm')
-  forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=10, substeps=4, tape=False)
-      -> (qpos', qvel', warm', info[, tape])
+       grad_decay=1.0, kinematics=False) -> (qpos', qvel', warm'[, qpos_n, xpos, xquat, cvel, subtree_com])
+  kinematics(qpos, qvel, com) -> (qpos_n, xpos, xquat, cvel, subtree_com)   (differentiable in qpos, qvel)
+  forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=10, substeps=4, tape=False, kinematics=False)
+      -> (qpos', qvel', warm', info[, tape][, the kinematics outputs])
   backward(tape, friction, com, g_qpos, g_qvel, *, substeps=4, clamp_kv=0, normal=3, ctrl=None, clamp_soft=None)
       -> (g_qpos, g_qvel, g_ctrl, info)
   jacobian(tape, friction, com, *, substeps=4, clamp_kv=1, normal=0, ctrl=None, clamp_soft=None) -> (J, info)
@@ -204,12 +205,98 @@ def jacobian(tape, friction, com, *, substeps=SUBSTEPS, clamp_kv=1, normal=0, ct
     return J, info
 
 
-def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, tape=False):
-    """One control step without autograd: (qpos', qvel', warm', info (B, 4) int32[, tape]), as the reference's forward
-    (torch_ffi.py:845): info = [Newton iterations of the last substep, its contact count (may exceed 64), its
-    constraint rows, bits 1 unsupported pair / 4 contacts beyond 64 / 16 rows beyond 192 over the substeps]."""
+def _kinematics_impl(qpos, qvel, com):
+    import torch
+    if not isinstance(qpos, torch.Tensor) or qpos.device.type != "cuda" or qpos.dim() != 2:
+        _check("qpos", qpos, (getattr(qpos, "shape", (0,))[0], NQ), None)
+    B, dev = qpos.shape[0], qpos.device.index
+    for name, x, shape in (("qpos", qpos, (B, NQ)), ("qvel", qvel, (B, NV)), ("com", com, (B, 3))):
+        _check(name, x, shape, dev)
+    if dev not in _READY:
+        init(dev)
+    kw = dict(dtype=torch.float32, device=qpos.device)
+    out = (torch.empty((B, NQ), **kw), torch.empty((B, NBODY, 3), **kw), torch.empty((B, NBODY, 4), **kw),
+           torch.empty((B, NBODY, 6), **kw), torch.empty((B, NBODY, 3), **kw))
+    if B == 0:
+        return out
+    lib = capi.load()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.nb_g1_kinematics(ctypes.c_void_p(st), B, *map(_ptr, (qpos, qvel, com) + out))
+    if rc:
+        raise _err(f"the kinematics launch failed (CUDA error {rc})", RuntimeError)
+    return out
+
+
+def _kinematics_backward_impl(qpos, qvel, com, cot, gq_in=None, gv_in=None):
+    import torch
+    B, dev = qpos.shape[0], qpos.device.index
+    shapes = ((B, NQ), (B, NBODY, 3), (B, NBODY, 4), (B, NBODY, 6), (B, NBODY, 3))
+    for name, x, shape in zip(("g_qpos_n", "g_xpos", "g_xquat", "g_cvel", "g_subtree_com"), cot, shapes):
+        _check(name, x, shape, dev)
+    kw = dict(dtype=torch.float32, device=qpos.device)
+    gq, gv = torch.empty((B, NQ), **kw), torch.empty((B, NV), **kw)
+    if B == 0:
+        return gq, gv
+    lib = capi.load()
+    with torch.cuda.device(dev):
+        st = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.nb_g1_kinematics_vjp(ctypes.c_void_p(st), B, *map(_ptr, (qpos, qvel, com) + tuple(cot)),
+                                      _ptr(gq_in), _ptr(gv_in), _ptr(gq), _ptr(gv))
+    if rc:
+        raise _err(f"the kinematics VJP launch failed (CUDA error {rc})", RuntimeError)
+    return gq, gv
+
+
+def _make_kin_fn():
+    import torch
+
+    class _Kin(torch.autograd.Function):
+        """The kinematics outputs; backward = their VJP (reference torch_ffi.py:787-808)."""
+
+        @staticmethod
+        def forward(ctx, qpos, qvel, com):
+            out = _kinematics_impl(qpos, qvel, com)
+            ctx.save_for_backward(qpos, qvel, com)
+            return out
+
+        @staticmethod
+        def backward(ctx, *g):
+            qpos, qvel, com = ctx.saved_tensors
+            B = qpos.shape[0]
+            shapes = ((B, NQ), (B, NBODY, 3), (B, NBODY, 4), (B, NBODY, 6), (B, NBODY, 3))
+            cot = tuple(qpos.new_zeros(sh) if x is None else x.contiguous() for x, sh in zip(g, shapes))
+            gq, gv = _kinematics_backward_impl(qpos, qvel, com, cot)
+            return gq, gv, None
+
+    return _Kin
+
+
+def kinematics(qpos, qvel, com):
+    """The kinematics outputs of states (qpos, qvel, com): (qpos_n (B, 36), xpos (B, 31, 3), xquat (B, 31, 4),
+    cvel (B, 31, 6), subtree_com (B, 31, 3)), differentiable in qpos and qvel (none for com), as the reference's
+    kinematics (torch_ffi.py:838; semantics g1_engine/kinematics.py:1-47)."""
+    return _kin_outputs(qpos, qvel, com)
+
+
+def _kin_outputs(qpos, qvel, com):
+    import torch
+    if torch.is_grad_enabled() and any(isinstance(x, torch.Tensor) and x.requires_grad for x in (qpos, qvel, com)):
+        return _fn("kin", _make_kin_fn).apply(qpos, qvel, com)
+    return _kinematics_impl(qpos, qvel, com)
+
+
+def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, tape=False,
+            kinematics=False):
+    """One control step without autograd: (qpos', qvel', warm', info (B, 4) int32[, tape][, the kinematics outputs of
+    (qpos', qvel')]), as the reference's forward (torch_ffi.py:845): info = [Newton iterations of the last substep,
+    its contact count (may exceed 64), its constraint rows, bits 1 unsupported pair / 4 contacts beyond 64 / 16 rows
+    beyond 192 over the substeps]."""
     r = _forward_impl(qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape))
-    return r if tape else r[:4]
+    out = r if tape else r[:4]
+    if kinematics:
+        out = tuple(out) + tuple(_kinematics_impl(r[0], r[1], com))
+    return out
 
 
 def backward(tape, friction, com, g_qpos, g_qvel, *, substeps=SUBSTEPS, clamp_kv=CLAMP_KV, normal=NORMAL, ctrl=None,
@@ -264,7 +351,7 @@ def _fn(name, make):
 
 
 def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, clamp_kv=CLAMP_KV,
-         normal=NORMAL, clamp_soft=None, grad_decay=GRAD_DECAY):
+         normal=NORMAL, clamp_soft=None, grad_decay=GRAD_DECAY, kinematics=False):
     """One control step: (qpos', qvel', warm') (reference torch_ffi.py:817). Differentiable in qpos, qvel and ctrl when
     an input requires grad (the forward then also writes the tape); warm' is not differentiable. clamp_kv, normal,
     clamp_soft and grad_decay act on the backward only."""
@@ -277,9 +364,12 @@ def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, subste
         raise _err(f"grad_decay must be finite, got {grad_decay}", ValueError)
     args = (qpos, qvel, warm, ctrl, friction, com)
     if torch.is_grad_enabled() and any(isinstance(x, torch.Tensor) and x.requires_grad for x in args):
-        return _fn("step", _make_step_fn).apply(*args, int(iterations), int(substeps), int(clamp_kv), int(normal),
-                                                soft, gd)
-    q1, v1, w1, _, _ = _forward_impl(*args, int(iterations), int(substeps))
+        q1, v1, w1 = _fn("step", _make_step_fn).apply(*args, int(iterations), int(substeps), int(clamp_kv),
+                                                      int(normal), soft, gd)
+    else:
+        q1, v1, w1, _, _ = _forward_impl(*args, int(iterations), int(substeps))
+    if kinematics:  # the output state's kinematics; through autograd their cotangents add to (qpos', qvel')'s
+        return (q1, v1, w1) + tuple(_kin_outputs(q1, v1, com))
     return q1, v1, w1
 
 

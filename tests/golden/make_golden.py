@@ -9,6 +9,8 @@ The outputs are small subsets of the reference's Apache-2.0 benchmark data (benc
                    floor (h = 1e-7) in the tangent basis (qpos tangent 35, qvel 35, ctrl 29), validity bits, groups
   mjw_sample.npz   the first 256 states of mf_s0 with MuJoCo Warp 3.17's one-step outputs (50 iterations, float32)
                    and its per-substep contact / row / iteration counts
+  mjw_contacts.npz the first 64 states of mf_s0 with MuJoCo Warp 3.17's contacts at the input state (pair, dist,
+                   pos[3], normal[3]): pins the body poses of the kinematics outputs
   truth_jac.npz    16 of mf_s0's Jacobian states (the G0 sample): inputs, the MuJoCo C float64 FD Jacobian (71 x 99,
                    stored float32 by the reference, h = 1e-6, tangent columns), its per-column floor, validity bits
 
@@ -43,6 +45,14 @@ def main():
                    model_flags=t["model_flags"][jidx])
         np.savez_compressed(HERE / "truth_jac.npz", **jac)
         print("truth_jac.npz", (HERE / "truth_jac.npz").stat().st_size, "bytes")
+    if write("mjw_contacts.npz"):
+        c = np.load(data / "mf_s0.npz")
+        m = np.load(ref / "fixtures" / "mjlab" / "mjw317_mf_s0.npz")
+        n = 64
+        w = {k: c[k][:n] for k in INPUTS}
+        w.update(con=m["con"][:n], con_count=m["con_count"][:n])
+        np.savez_compressed(HERE / "mjw_contacts.npz", **w)
+        print("mjw_contacts.npz", (HERE / "mjw_contacts.npz").stat().st_size, "bytes")
     if not write("truth_check.npz"):
         return
     out = {k: [] for k in INPUTS + ("check_out", "model_flags", "corpus", "index")}

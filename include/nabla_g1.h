@@ -87,6 +87,20 @@ int nb_g1_kinematics_vjp(cudaStream_t stream, int nw, const float* qpos, const f
                          const float* g_qpos_n, const float* g_xpos, const float* g_xquat, const float* g_cvel,
                          const float* g_subtree_com, const float* gq_in, const float* gv_in, float* gq, float* gv);
 
+/* Diagnostics: device counters (unsigned long long, nb_g1_diag_count() of them, the caller's zero-initialised array,
+ * added to by every call): forward calls, worlds, worlds with unsupported / overflow bits, worlds at the iteration
+ * limit, tape records, records refactored / not converged / with a clamped pivot; backward calls, rows, rows with a
+ * non-finite gradient (all / qpos / qvel / ctrl), rows with a non-finite cotangent, worlds with a replay mismatch; then
+ * contact-overflow and row-overflow worlds. nb_g1_diag_backward also ORs the non-finite bits (1 qpos, 2 qvel, 4 ctrl,
+ * 8 cotangent) << 16 into the backward's info. One small kernel each, stream-ordered after the call it counts.
+ * Replaces the reference's counter kernels `k_diag_fwd` / `k_diag_bwd` (src/nablaengine/jax_ffi.py:334-425,
+ * src/nablaengine/torch_ffi.py:101-157). */
+long long nb_g1_diag_count(void);
+int nb_g1_diag_forward(cudaStream_t stream, unsigned long long* counters, int nw, int nsub, int iterations,
+                       const int* info, const float* tape);
+int nb_g1_diag_backward(cudaStream_t stream, unsigned long long* counters, int nw, const float* gq, const float* gv,
+                        const float* gctrl, const float* gq_out, const float* gv_out, int* info);
+
 /* nb_g1_forward plus the per-substep work counters stats (B, nsub, 8) int32: contacts kept, constraint rows, Newton
  * iterations, line-search evaluations, Hessian factorisations, broad-phase candidate pairs, contacts found, 0; the
  * outputs are bitwise those of nb_g1_forward. The counters feed the

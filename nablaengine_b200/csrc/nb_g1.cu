@@ -3,6 +3,7 @@
 // k_forward: one warp per world, WPB worlds per block, each world's whole control step (nsub substeps) in one
 // launch with its state resident in shared memory (nb_g1_step.cuh), so a step is a single kernel per call.
 #include "../../include/nabla_g1.h"
+#include <algorithm>
 #include <cstddef>
 #include "nb_g1_step.cuh"
 #include "nb_g1_adjoint.cuh"
@@ -205,6 +206,96 @@ __global__ void __launch_bounds__(JWPB * 32) k_jacobian(int nw, int nsub, const 
   for (int i = lane; i < NU; i += 32) out[2 * NV + i] = A.ub[i];
   if (lane == 0 && flags) atomicOr(info + w, flags);
 }
+// ---- diagnostics: device counters (uint64, DIAG order of the Python layer) added by one small kernel per call ------
+enum : int {
+  D_FWD_CALLS, D_FWD_WORLDS, D_FWD_UNSUPPORTED, D_FWD_ITER_LIMIT, D_TAPE_RECORDS, D_REFACT_RECORDS, D_NONCONV_RECORDS,
+  D_SINGULAR_RECORDS, D_BWD_CALLS, D_BWD_ROWS, D_NONFINITE_ROWS, D_NONFINITE_QPOS, D_NONFINITE_QVEL, D_NONFINITE_CTRL,
+  D_NONFINITE_COT, D_REPLAY_MISMATCH, D_FWD_CONTACT_OVERFLOW, D_FWD_ROW_OVERFLOW, NDIAG
+};
+enum : int { NONFINITE_QPOS = 1, NONFINITE_QVEL = 2, NONFINITE_CTRL = 4, NONFINITE_COT = 8, NONFINITE_SHIFT = 16 };
+
+// a warp's count into counter k (exact integer sums: the totals do not depend on the order)
+__device__ __forceinline__ void diag_add(unsigned long long* d, int k, unsigned v) {
+  v = __reduce_add_sync(FULL, v);
+  if ((threadIdx.x & 31) == 0 && v) atomicAdd(&d[k], (unsigned long long)v);
+}
+__device__ __forceinline__ bool finite_row(const float* x, int n) {
+  bool ok = true;
+  for (int i = 0; i < n; i++) ok &= isfinite(x[i]);
+  return ok;
+}
+
+__global__ void k_diag_fwd(unsigned long long* d, int nw, int nsub, int iterations, const int* info,
+                           const float* tape) {
+  unsigned unsup = 0, lim = 0, oc = 0, orow = 0, refact = 0, nonconv = 0, sing = 0;
+  const int stride = gridDim.x * blockDim.x;
+  for (int w0 = blockIdx.x * blockDim.x; w0 < nw; w0 += stride) {  // whole warps stay in the loop
+    const int w = w0 + threadIdx.x;
+    if (w < nw) {
+      const int bits = info[4 * w + 3];
+      unsup += bits != 0;
+      oc += (bits & CONTACT_OVERFLOW) != 0;
+      orow += (bits & ROW_OVERFLOW) != 0;
+      lim += info[4 * w] >= iterations;
+      if (tape)
+        for (int k = 0; k < nsub; k++) {
+          const unsigned f = __float_as_uint(tape[((size_t)w * nsub + k) * REC_WORDS + T_FLAGS]);
+          refact += (f & TAPE_REFACT) != 0;
+          nonconv += (f & TAPE_NONCONV) != 0;
+          sing += (f & TAPE_SINGULAR) != 0;
+        }
+    }
+  }
+  diag_add(d, D_FWD_UNSUPPORTED, unsup);
+  diag_add(d, D_FWD_ITER_LIMIT, lim);
+  diag_add(d, D_FWD_CONTACT_OVERFLOW, oc);
+  diag_add(d, D_FWD_ROW_OVERFLOW, orow);
+  diag_add(d, D_REFACT_RECORDS, refact);
+  diag_add(d, D_NONCONV_RECORDS, nonconv);
+  diag_add(d, D_SINGULAR_RECORDS, sing);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    atomicAdd(&d[D_FWD_CALLS], 1ull);
+    atomicAdd(&d[D_FWD_WORLDS], (unsigned long long)nw);
+    if (tape) atomicAdd(&d[D_TAPE_RECORDS], (unsigned long long)nw * nsub);
+  }
+}
+
+// the backward's counters; the non-finite bits go into info (bits NONFINITE_* << NONFINITE_SHIFT)
+__global__ void k_diag_bwd(unsigned long long* d, int nw, const float* gq, const float* gv, const float* gu,
+                           const float* cq, const float* cv, int* info) {
+  unsigned rows = 0, rq = 0, rv = 0, ru = 0, rc = 0, rm = 0;
+  const int stride = gridDim.x * blockDim.x;
+  for (int w0 = blockIdx.x * blockDim.x; w0 < nw; w0 += stride) {
+    const int w = w0 + threadIdx.x;
+    if (w < nw) {
+      const size_t ww = (size_t)w;
+      const unsigned b = (finite_row(gq + ww * NQ, NQ) ? 0u : (unsigned)NONFINITE_QPOS) |
+                         (finite_row(gv + ww * NV, NV) ? 0u : (unsigned)NONFINITE_QVEL) |
+                         (finite_row(gu + ww * NU, NU) ? 0u : (unsigned)NONFINITE_CTRL) |
+                         (finite_row(cq + ww * NQ, NQ) && finite_row(cv + ww * NV, NV) ? 0u : (unsigned)NONFINITE_COT);
+      const int f = info[w];
+      info[w] = f | (int)(b << NONFINITE_SHIFT);
+      rows += (b & 7u) != 0;
+      rq += (b & NONFINITE_QPOS) != 0;
+      rv += (b & NONFINITE_QVEL) != 0;
+      ru += (b & NONFINITE_CTRL) != 0;
+      rc += (b & NONFINITE_COT) != 0;
+      rm += (f & ADJ_REPLAY_MISMATCH) != 0;
+    }
+  }
+  diag_add(d, D_NONFINITE_ROWS, rows);
+  diag_add(d, D_NONFINITE_QPOS, rq);
+  diag_add(d, D_NONFINITE_QVEL, rv);
+  diag_add(d, D_NONFINITE_CTRL, ru);
+  diag_add(d, D_NONFINITE_COT, rc);
+  diag_add(d, D_REPLAY_MISMATCH, rm);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    atomicAdd(&d[D_BWD_CALLS], 1ull);
+    atomicAdd(&d[D_BWD_ROWS], (unsigned long long)nw);
+  }
+}
+static unsigned diag_grid(int nw) { return (unsigned)std::max(1, std::min(148, (nw + 255) / 256)); }
+
 static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
 static_assert(offsetof(World, M) % 16 == 0 && offsetof(World, L) % 16 == 0, "float4 copies of the triangles");
 
@@ -235,6 +326,24 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
     e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)JSMEM);
   return (int)e;
 }
+
+int nb_g1_diag_forward(cudaStream_t stream, unsigned long long* counters, int nw, int nsub, int iterations,
+                       const int* info, const float* tape) {
+  if (nw < 0 || nsub < 1 || nsub > 32) return (int)cudaErrorInvalidValue;
+  if (!counters || (nw > 0 && !info)) return (int)cudaErrorInvalidValue;
+  k_diag_fwd<<<diag_grid(nw), 256, 0, stream>>>(counters, nw, nsub, iterations, info, tape);
+  return (int)cudaGetLastError();
+}
+
+int nb_g1_diag_backward(cudaStream_t stream, unsigned long long* counters, int nw, const float* gq, const float* gv,
+                        const float* gctrl, const float* gq_out, const float* gv_out, int* info) {
+  if (nw < 0 || !counters) return (int)cudaErrorInvalidValue;
+  if (nw > 0 && (!gq || !gv || !gctrl || !gq_out || !gv_out || !info)) return (int)cudaErrorInvalidValue;
+  k_diag_bwd<<<diag_grid(nw), 256, 0, stream>>>(counters, nw, gq, gv, gctrl, gq_out, gv_out, info);
+  return (int)cudaGetLastError();
+}
+
+long long nb_g1_diag_count(void) { return NDIAG; }
 
 int nb_g1_kinematics(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* com,
                      float* qpos_n, float* xpos, float* xquat, float* cvel, float* subtree_com) {

@@ -44,7 +44,8 @@ constexpr int T_QPOS = 0, T_QVEL = 36, T_ASTAR = 71, T_AADV = 106, T_DINVH = 141
 constexpr int T_LQ = T_LH + NTRI, T_CON = T_LQ + NTRI, T_ZONE = T_CON + MAXCON / 2, T_CLAMP = T_ZONE + NEFC / 32;
 constexpr int T_HDR = T_CLAMP + 2, T_FLAGS = T_HDR + 1, REC_WORDS = ((T_FLAGS + 1 + 3) / 4) * 4;
 static_assert(T_LQ == 841 && REC_WORDS == 1516, "tape layout");
-enum : unsigned { TAPE_REFACT = 1u << 8, TAPE_NONCONV = 1u << 9 };
+// TAPE_SINGULAR: a pivot of the recorded Hessian factor was clamped (at 1e-30: not positive definite in float32)
+enum : unsigned { TAPE_REFACT = 1u << 8, TAPE_NONCONV = 1u << 9, TAPE_SINGULAR = 1u << 12 };
 enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
 
 // Phase profile (build with -DNB_PROFILE; the product build has none of it): lane 0 of every world adds the clock64
@@ -1362,6 +1363,9 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
     }
     tape_put(rec + T_LH, s.L, NTRI, lane);
     tape_put(rec + T_DINVH, s.dinv, NV, lane);
+    bool sing = false;
+    for (int i = lane; i < NV; i += 32) sing |= !(s.dinv[i] < 1e14f);
+    sing = __any_sync(FULL, sing);
     tape_put(rec + T_ASTAR, s.qacc, NV, lane);
     const int ncon = s.ncon, nefc = s.nefc;
     for (int i = lane; i < MAXCON / 2; i += 32) {
@@ -1380,7 +1384,7 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
       __stcs(rec + T_CLAMP + 1, __uint_as_float(s.clamp_hi));
       __stcs(rec + T_HDR, __uint_as_float((unsigned)ncon | (unsigned)nefc << 8 | (unsigned)s.nlim << 16));
       __stcs(rec + T_FLAGS, __uint_as_float((unsigned)s.unsup | (refact ? TAPE_REFACT : 0u) |
-                                            (s.ndone ? 0u : TAPE_NONCONV)));
+                                            (s.ndone ? 0u : TAPE_NONCONV) | (sing ? TAPE_SINGULAR : 0u)));
       for (int k = T_FLAGS + 1; k < REC_WORDS; k++) __stcs(rec + k, 0.f);
     }
     __syncwarp();

@@ -21,8 +21,10 @@ d/dctrl and no gradient for warm, friction and com. The calls only launch kernel
 caching allocator, so after init(device) they can be captured in a CUDA graph. There is no CPU fallback: without
 the CUDA library the call raises.
 """
+import atexit
 import ctypes
 import math
+import os
 import threading
 
 from . import capi
@@ -31,11 +33,18 @@ ITERATIONS, SUBSTEPS, CLAMP_KV, NORMAL = 10, 4, 0, 3
 CLAMP_SOFT, GRAD_DECAY = 0.2, 1.0
 OVERFLOW_CONTACTS, OVERFLOW_ROWS, UNSUPPORTED = 4, 16, 1
 NQ, NV, NU, NBODY, MAXCON = capi.NQ, capi.NV, capi.NU, capi.NBODY, capi.MAXCON
-DIAG = ("fwd_calls", "fwd_worlds", "fwd_unsupported_worlds", "fwd_iteration_limit_worlds",
-        "fwd_contact_overflow_worlds", "fwd_row_overflow_worlds")
+# the device counters (nb_g1_diag_forward / _backward), in the library's order (the reference's DIAG names)
+DIAG = ("fwd_calls", "fwd_worlds", "fwd_unsupported_worlds", "fwd_iteration_limit_worlds", "tape_records",
+        "refact_records", "nonconv_records", "singular_records", "bwd_calls", "bwd_rows", "nonfinite_rows",
+        "nonfinite_qpos_rows", "nonfinite_qvel_rows", "nonfinite_ctrl_rows", "nonfinite_cotangent_rows",
+        "replay_mismatch_worlds", "fwd_contact_overflow_worlds", "fwd_row_overflow_worlds")
+NONFINITE_QPOS, NONFINITE_QVEL, NONFINITE_CTRL, NONFINITE_COT, NONFINITE_SHIFT = 1, 2, 4, 8, 16
 
 _LOCK = threading.Lock()
 _READY = set()
+_DIAG = {}                     # device -> int64 (len(DIAG),) counters
+_DIAG_ON = [True]
+_OVERFLOW_WARN = [os.environ.get("NB_OVERFLOW_WARN", "0") not in ("", "0")]
 
 
 def _err(msg, exc=TypeError):
@@ -60,6 +69,10 @@ def init(device=None):
                 rc = lib.nb_g1_upload(None, ctypes.c_void_p(st.cuda_stream))
                 if rc:
                     raise _err(f"nb_g1_upload on cuda:{dev} failed (CUDA error {rc})", RuntimeError)
+                if int(lib.nb_g1_diag_count()) != len(DIAG):
+                    raise _err("the library's diagnostic counters do not match DIAG", RuntimeError)
+                import torch as _t
+                _DIAG[dev] = _t.zeros((len(DIAG),), dtype=_t.int64, device=f"cuda:{dev}")
                 st.synchronize()
             _READY.add(dev)
     return {"library": str(capi._build.LIB), "nq": NQ, "nv": NV, "nu": NU, "nbody": NBODY, "maxcon": MAXCON}
@@ -119,6 +132,12 @@ def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, t
                                _ptr(tp) if tape else None, _ptr(work))
     if rc:
         raise _err(f"the forward launch failed (CUDA error {rc})", RuntimeError)
+    if _DIAG_ON[0]:
+        with torch.cuda.device(dev):
+            rc = lib.nb_g1_diag_forward(ctypes.c_void_p(st), _ptr(_DIAG[dev]), B, int(substeps), int(iterations),
+                                        _ptr(info), _ptr(tp) if tape else None)
+        if rc:
+            raise _err(f"the forward diagnostics launch failed (CUDA error {rc})", RuntimeError)
     return q1, v1, w1, info, tp
 
 
@@ -166,6 +185,12 @@ def _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv
                                ctypes.c_float(clamp_soft), int(clamp_kv), int(normal))
     if rc:
         raise _err(f"the adjoint launch failed (CUDA error {rc})", RuntimeError)
+    if _DIAG_ON[0]:
+        with torch.cuda.device(dev):
+            rc = lib.nb_g1_diag_backward(ctypes.c_void_p(st), _ptr(_DIAG[dev]), B,
+                                         *map(_ptr, (gq, gv, gu, g_qpos, g_qvel, info)))
+        if rc:
+            raise _err(f"the backward diagnostics launch failed (CUDA error {rc})", RuntimeError)
     return gq, gv, gu, info
 
 
@@ -371,6 +396,74 @@ def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, subste
     if kinematics:  # the output state's kinematics; through autograd their cotangents add to (qpos', qvel')'s
         return (q1, v1, w1) + tuple(_kin_outputs(q1, v1, com))
     return q1, v1, w1
+
+
+# ---- diagnostics (device counters; reference torch_ffi.py:679-745) -------------------------------------------------
+
+def set_diagnostics(enabled):
+    """Switch the device counters and the backward's non-finite info bits on (the default) or off; returns the previous
+    setting. They are one small kernel per forward and per backward; outputs and gradients are the same either way."""
+    prev = _DIAG_ON[0]
+    _DIAG_ON[0] = bool(enabled)
+    return prev
+
+
+def diagnostics(device=None):
+    """The device's counters: an int64 (len(DIAG),) CUDA tensor in DIAG order, added to by every call since init or
+    the last reset; not copied or synchronised."""
+    import torch
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    if dev is None:
+        dev = torch.cuda.current_device()
+    if dev not in _READY:
+        init(dev)
+    return _DIAG[dev]
+
+
+def read_diagnostics(device=None, reset=True):
+    """The device's counters as {name: int} (synchronises); reset=True zeroes them afterwards. With
+    set_overflow_warnings(True) it warns when worlds exceeded the contact or constraint-row capacity."""
+    d = diagnostics(device)
+    out = dict(zip(DIAG, (int(x) for x in d.cpu())))
+    if reset:
+        d.zero_()
+    if _OVERFLOW_WARN[0]:
+        warn_overflow(out)
+    return out
+
+
+def warn_overflow(d, where="nablaengine_b200"):
+    """A RuntimeWarning when the counters d count worlds whose contacts or rows exceeded the per-world capacity (64
+    contacts, 192 rows: the excess is dropped, so those worlds miss support and friction forces); returns the count.
+    The worlds of one call: info[:, 3] & OVERFLOW_CONTACTS / OVERFLOW_ROWS of forward()."""
+    import warnings
+    nc, nr = d.get("fwd_contact_overflow_worlds", 0), d.get("fwd_row_overflow_worlds", 0)
+    if nc or nr:
+        warnings.warn(f"{where}: {nc} world-steps exceeded the contact capacity (64 per world) and {nr} the "
+                      f"constraint-row capacity (192); their extra contacts / rows were dropped, so those worlds miss "
+                      f"support and friction forces", RuntimeWarning, stacklevel=3)
+    return nc + nr
+
+
+def set_overflow_warnings(enabled):
+    """Switch the capacity-overflow warnings on or off (default off, or $NB_OVERFLOW_WARN=1): when on,
+    read_diagnostics warns, and counts nobody read are reported once more at exit. Returns the previous setting."""
+    prev = _OVERFLOW_WARN[0]
+    _OVERFLOW_WARN[0] = bool(enabled)
+    return prev
+
+
+def _exit_report():
+    try:
+        if not (_DIAG_ON[0] and _OVERFLOW_WARN[0]):
+            return
+        for dev in sorted(_DIAG):
+            warn_overflow(dict(zip(DIAG, (int(x) for x in _DIAG[dev].cpu()))), where=f"nablaengine_b200 (cuda:{dev})")
+    except Exception:  # noqa: BLE001  (the interpreter or CUDA shutting down)
+        pass
+
+
+atexit.register(_exit_report)
 
 
 def _make_scale_fn():

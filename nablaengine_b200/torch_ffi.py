@@ -281,7 +281,7 @@ def _make_kin_fn():
 
         @staticmethod
         def forward(ctx, qpos, qvel, com):
-            out = _kinematics_impl(qpos, qvel, com)
+            out = tuple(_ops()["kinematics"](qpos, qvel, com))
             ctx.save_for_backward(qpos, qvel, com)
             return out
 
@@ -291,7 +291,7 @@ def _make_kin_fn():
             B = qpos.shape[0]
             shapes = ((B, NQ), (B, NBODY, 3), (B, NBODY, 4), (B, NBODY, 6), (B, NBODY, 3))
             cot = tuple(qpos.new_zeros(sh) if x is None else x.contiguous() for x, sh in zip(g, shapes))
-            gq, gv = _kinematics_backward_impl(qpos, qvel, com, cot)
+            gq, gv = _ops()["kinematics_backward"](qpos, qvel, com, *cot)
             return gq, gv, None
 
     return _Kin
@@ -308,7 +308,72 @@ def _kin_outputs(qpos, qvel, com):
     import torch
     if torch.is_grad_enabled() and any(isinstance(x, torch.Tensor) and x.requires_grad for x in (qpos, qvel, com)):
         return _fn("kin", _make_kin_fn).apply(qpos, qvel, com)
-    return _kinematics_impl(qpos, qvel, com)
+    return tuple(_ops()["kinematics"](qpos, qvel, com))
+
+
+# ---- custom ops (torch.library): the library calls as opaque nodes for torch.compile ---------------------------------
+# (reference torch_ffi.py:595-657: nablaengine::forward / backward / kinematics / kinematics_backward with fake impls)
+_OPS = {}
+
+
+def _ops():
+    if _OPS:  # (registered: no lock, so torch.compile traces through this lookup)
+        return _OPS
+    with _LOCK:
+        if _OPS:
+            return _OPS
+        import torch
+        from typing import List, Optional
+        T = torch.Tensor
+
+        @torch.library.custom_op("nabla_b200::forward", mutates_args=())
+        def forward_op(qpos: T, qvel: T, warm: T, ctrl: T, friction: T, com: T, iterations: int, substeps: int,
+                       tape: bool) -> List[T]:
+            return list(_forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape))
+
+        @forward_op.register_fake
+        def _(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape):
+            B = qpos.shape[0]
+            return [qpos.new_empty((B, NQ)), qpos.new_empty((B, NV)), qpos.new_empty((B, NV)),
+                    qpos.new_empty((B, 4), dtype=torch.int32),
+                    qpos.new_empty((B if tape else 0, substeps * _rec_words()))]
+
+        @torch.library.custom_op("nabla_b200::backward", mutates_args=())
+        def backward_op(tape: T, friction: T, com: T, g_qpos: T, g_qvel: T, ctrl: Optional[T], substeps: int,
+                        clamp_kv: int, normal: int, clamp_soft: float) -> List[T]:
+            return list(_backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv, normal,
+                                       clamp_soft))
+
+        @backward_op.register_fake
+        def _(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv, normal, clamp_soft):
+            B = tape.shape[0]
+            return [tape.new_empty((B, NQ)), tape.new_empty((B, NV)), tape.new_empty((B, NU)),
+                    tape.new_empty((B,), dtype=torch.int32)]
+
+        @torch.library.custom_op("nabla_b200::kinematics", mutates_args=())
+        def kinematics_op(qpos: T, qvel: T, com: T) -> List[T]:
+            return list(_kinematics_impl(qpos, qvel, com))
+
+        @kinematics_op.register_fake
+        def _(qpos, qvel, com):
+            B = qpos.shape[0]
+            return [qpos.new_empty((B, NQ)), qpos.new_empty((B, NBODY, 3)), qpos.new_empty((B, NBODY, 4)),
+                    qpos.new_empty((B, NBODY, 6)), qpos.new_empty((B, NBODY, 3))]
+
+        @torch.library.custom_op("nabla_b200::kinematics_backward", mutates_args=())
+        def kinematics_backward_op(qpos: T, qvel: T, com: T, g_qpos_n: T, g_xpos: T, g_xquat: T, g_cvel: T,
+                                   g_subtree_com: T) -> List[T]:
+            return list(_kinematics_backward_impl(qpos, qvel, com, (g_qpos_n, g_xpos, g_xquat, g_cvel,
+                                                                    g_subtree_com)))
+
+        @kinematics_backward_op.register_fake
+        def _(qpos, qvel, com, g_qpos_n, g_xpos, g_xquat, g_cvel, g_subtree_com):
+            B = qpos.shape[0]
+            return [qpos.new_empty((B, NQ)), qpos.new_empty((B, NV))]
+
+        _OPS.update(forward=forward_op, backward=backward_op, kinematics=kinematics_op,
+                    kinematics_backward=kinematics_backward_op)
+        return _OPS
 
 
 def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, tape=False,
@@ -317,22 +382,30 @@ def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, sub
     (qpos', qvel')]), as the reference's forward (torch_ffi.py:845): info = [Newton iterations of the last substep,
     its contact count (may exceed 64), its constraint rows, bits 1 unsupported pair / 4 contacts beyond 64 / 16 rows
     beyond 192 over the substeps]."""
-    r = _forward_impl(qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape))
-    out = r if tape else r[:4]
+    r = _ops()["forward"](qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape))
+    out = tuple(r) if tape else tuple(r[:4])
     if kinematics:
-        out = tuple(out) + tuple(_kinematics_impl(r[0], r[1], com))
+        out = out + tuple(_ops()["kinematics"](r[0], r[1], com))
     return out
 
 
 def backward(tape, friction, com, g_qpos, g_qvel, *, substeps=SUBSTEPS, clamp_kv=CLAMP_KV, normal=NORMAL, ctrl=None,
-             clamp_soft=None):
+             clamp_soft=None, kinematics=None):
     """The adjoint of one control step from its tape (reference torch_ffi.py:854): (g_qpos (qpos form), g_qvel,
-    g_ctrl, info (B,) int32, the replay flags)."""
+    g_ctrl, info (B,) int32: the replay flags, non-finite bits << 16). kinematics: None, or (qpos', qvel', g_qpos_n,
+    g_xpos, g_xquat, g_cvel, g_subtree_com): the output state's kinematics cotangents, pulled back onto (qpos',
+    qvel') and added to g_qpos, g_qvel first."""
     soft = _soft(clamp_kv, clamp_soft)
     if soft is not None and ctrl is None:
         raise _err("clamp_kv=2 (the soft clamp) needs the step's ctrl", ValueError)
-    return _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl if soft is not None else None, int(substeps),
-                          int(clamp_kv), int(normal), 0.0 if soft is None else soft)
+    if kinematics is not None:
+        if len(kinematics) != 7:
+            raise _err("kinematics = (qpos', qvel', g_qpos_n, g_xpos, g_xquat, g_cvel, g_subtree_com)", ValueError)
+        q1, v1 = kinematics[:2]
+        _check("qpos'", q1, (q1.shape[0] if hasattr(q1, "shape") else 0, NQ), None)
+        g_qpos, g_qvel = _kinematics_backward_impl(q1, v1, com, tuple(kinematics[2:]), gq_in=g_qpos, gv_in=g_qvel)
+    return tuple(_ops()["backward"](tape, friction, com, g_qpos, g_qvel, ctrl if soft is not None else None,
+                                    int(substeps), int(clamp_kv), int(normal), 0.0 if soft is None else soft))
 
 
 def _make_step_fn():
@@ -344,7 +417,7 @@ def _make_step_fn():
         @staticmethod
         def forward(ctx, qpos, qvel, warm, ctrl, friction, com, iterations, substeps, clamp_kv, normal, clamp_soft,
                     grad_decay):
-            q1, v1, w1, _, tp = _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, True)
+            q1, v1, w1, _, tp = _ops()["forward"](qpos, qvel, warm, ctrl, friction, com, iterations, substeps, True)
             ctx.save_for_backward(tp, friction, com, ctrl)
             ctx.opts = (substeps, clamp_kv, normal, clamp_soft, grad_decay)
             ctx.mark_non_differentiable(w1)
@@ -357,8 +430,8 @@ def _make_step_fn():
             B = tp.shape[0]
             g_q1 = tp.new_zeros((B, NQ)) if g_q1 is None else g_q1.contiguous()
             g_v1 = tp.new_zeros((B, NV)) if g_v1 is None else g_v1.contiguous()
-            gq, gv, gu, _ = _backward_impl(tp, friction, com, g_q1, g_v1, ctrl if clamp_kv == 2 else None, substeps,
-                                           clamp_kv, normal, 0.0 if clamp_soft is None else clamp_soft)
+            gq, gv, gu, _ = _ops()["backward"](tp, friction, com, g_q1, g_v1, ctrl if clamp_kv == 2 else None,
+                                               substeps, clamp_kv, normal, 0.0 if clamp_soft is None else clamp_soft)
             if grad_decay != 1.0:  # the state's cotangent through the physics times grad_decay, ctrl's not
                 gq, gv = gq * grad_decay, gv * grad_decay
             return gq, gv, None, gu, None, None, None, None, None, None, None, None
@@ -392,7 +465,7 @@ def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, subste
         q1, v1, w1 = _fn("step", _make_step_fn).apply(*args, int(iterations), int(substeps), int(clamp_kv),
                                                       int(normal), soft, gd)
     else:
-        q1, v1, w1, _, _ = _forward_impl(*args, int(iterations), int(substeps))
+        q1, v1, w1 = _ops()["forward"](*args, int(iterations), int(substeps), False)[:3]
     if kinematics:  # the output state's kinematics; through autograd their cotangents add to (qpos', qvel')'s
         return (q1, v1, w1) + tuple(_kin_outputs(q1, v1, com))
     return q1, v1, w1

@@ -91,19 +91,22 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 constexpr size_t SMEM = sizeof(World) * WPB;
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
-// worlds per block of k_adjoint (21.9 KB each: 9 per SM) and rows (warps) per block of k_jacobian (10 rows of one
-// world: 10 warps per SM sharing the world's records in L1 and their instruction stream); measured at B = 4096:
-// adjoint 1.04 ms (against 1.12 with 2 worlds per block), Jacobian 12.7 ms per 1024 worlds (14.2 with 2 rows)
-constexpr int AWPB = 1, JWPB = 10;
+// worlds per block of k_adjoint and rows (warps) per block of k_jacobian: 10 x 21.9 KB, one block per SM. The
+// adjoint's worlds meet at a block barrier before every substep, so the SM's warps run the same code together (one
+// instruction stream; measured at B = 4096: 1.06 ms against 1.14 ms with one world per block and no barrier); the
+// Jacobian's 10 rows of one world share its records in L1 and stay together without one (12.7 ms per 1024 worlds
+// against 14.2 with 2 rows per block)
+constexpr int AWPB = 10, JWPB = 10;
 struct AdjBlock { AWorld s; Adj a; };
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB, JSMEM = sizeof(AdjBlock) * JWPB;
 
 // One world's adjoint over its nsub records tw (w's first record): the output cotangent is (gq, gv) (qpos form, in
 // any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel') when unit >= 0.
-// Leaves the input cotangents in A.qout (dof tangent), A.vb, A.ub; returns the replay flags.
+// Leaves the input cotangents in A.qout (dof tangent), A.vb, A.ub; returns the replay flags. block_sync: a block
+// barrier before every substep (every warp of the block calls this with the same nsub).
 __device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int nsub, float fric, const float* comw,
                                       const float* ctrlw, const float* gq, const float* gv, int unit, int clamp_kv,
-                                      float clamp_soft, int normal, int lane) {
+                                      float clamp_soft, int normal, int lane, bool block_sync) {
   const float h = G1_TIMESTEP;
   if (lane == 0) { s.fric = fric; A.normal = normal; }
   if (lane < 3) s.com[lane] = comw[lane];
@@ -139,8 +142,10 @@ __device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int ns
   }
   __syncwarp();
   int flags = 0;
-  for (int k = nsub - 1; k >= 0; k--)
+  for (int k = nsub - 1; k >= 0; k--) {
+    if (block_sync) __syncthreads();  // (the same value on every thread of the block)
     flags |= adj_substep(s, A, tw + (size_t)k * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane);
+  }
   return flags;
 }
 
@@ -155,15 +160,17 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
                                                        float clamp_soft, int clamp_kv, int normal) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w = blockIdx.x * AWPB + warp;
-  if (w >= nw) return;
+  int w = blockIdx.x * AWPB + warp;
+  const bool active = w < nw;  // inactive warps replay world 0 for the barriers and write nothing
+  if (!active) w = 0;
   AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
   AWorld& s = blk.s;
   Adj& A = blk.a;
   const size_t w64 = (size_t)w;
   const float* tw = tape + w64 * nsub * REC_WORDS;
   const int flags = adj_world(s, A, tw, nsub, fric[w], com + w64 * 3, ctrl ? ctrl + w64 * NU : nullptr,
-                              gq_out + w64 * NQ, gv_out + w64 * NV, -1, clamp_kv, clamp_soft, normal, lane);
+                              gq_out + w64 * NQ, gv_out + w64 * NV, -1, clamp_kv, clamp_soft, normal, lane, true);
+  if (!active) return;
   // the input qpos gradient in qpos form: (q_lin, 2 xi (0, q_rot), q_hinge), xi the input quaternion
   for (int i = lane; i < NV; i += 32) {
     if (i < 3) gq_in[w64 * NQ + i] = A.qout[i];
@@ -199,7 +206,7 @@ __global__ void __launch_bounds__(JWPB * 32) k_jacobian(int nw, int nsub, const 
   const size_t w64 = (size_t)w;
   const int flags = adj_world(blk.s, blk.a, tape + w64 * nsub * REC_WORDS, nsub, fric[w], com + w64 * 3,
                               ctrl ? ctrl + w64 * NU : nullptr, nullptr, nullptr, row, clamp_kv, clamp_soft, normal,
-                              lane);
+                              lane, false);
   float* out = jac + (w64 * JROWS + row) * JCOLS;
   const Adj& A = blk.a;
   for (int i = lane; i < NV; i += 32) { out[i] = A.qout[i]; out[NV + i] = A.vb[i]; }

@@ -17,6 +17,7 @@ namespace nbg1 {
 #ifndef NB_LOCKSTEP
 #define NB_LOCKSTEP 1
 #endif
+
 constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // NB_LOCKSTEP: the worlds of a block run their Newton iterations in lockstep (a block barrier per iteration): the
 // warps of an SM then fetch the same instructions at the same time, instead of each streaming the ~50 KB Newton loop
@@ -144,7 +145,7 @@ __device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int ns
   int flags = 0;
   for (int k = nsub - 1; k >= 0; k--) {
     if (block_sync) __syncthreads();  // (the same value on every thread of the block)
-    flags |= adj_substep(s, A, tw + (size_t)k * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane);
+    flags |= adj_substep(s, A, tw + (size_t)k * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane, block_sync);
   }
   return flags;
 }

@@ -55,7 +55,11 @@ struct __align__(16) Adj {
   };
   float ax[NV][3];                    // dof axes (world)
   unsigned clamp_lo, clamp_hi;
+  unsigned zone[NEFC / 32];           // the record's zone bits (row r quadratic: bit r & 31 of word r / 32)
   int nlim_tape, flags, normal, pad_;  // normal: the self-contact normal derivative option (0..3)
+#ifdef NB_PROFILE
+  long long prof_t;
+#endif
 };
 
 // ---- replay ---------------------------------------------------------------------------------------------------------
@@ -323,7 +327,6 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
     const float R = fmaxf(1e-15f, iw * (1.f - imp) / imp), D = 1.f / R;
     const float dD = R > 1e-15f ? D * D * iw / (imp * imp) : 0.f;  // dD / dimp = 1 / (iw (1 - imp)^2)
     // relative point velocities u(x) = dV_lin + dW x pos for x = lambda, a*, v; jd_d(x) = fr_d . u(x)
-    const float* V[3] = {nullptr, nullptr, nullptr};
     float u[3][3], jd[3][3];
     for (int m = 0; m < 3; m++) {
       const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? A.VA : A.VV);
@@ -332,7 +335,6 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
       cross(dV, pos, t);
       for (int k = 0; k < 3; k++) u[m][k] = dV[3 + k] + t[k];
       for (int dd = 0; dd < 3; dd++) jd[m][dd] = dot3(fr + 3 * dd, u[m]);
-      (void)V;
     }
     // psi_c = -D sum_t (J_t lambda) (J_t a + b J_t v + k imp dist) over the tape's quadratic rows
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
@@ -341,7 +343,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
     const float kterm = kk * imp * dist;
     for (int t = 0; t < nr; t++) {
       const int r = r0 + t;
-      if (!((__float_as_uint(rec[T_ZONE + r / 32]) >> (r & 31)) & 1u)) continue;
+      if (!((A.zone[r >> 5] >> (r & 31)) & 1u)) continue;
       const float sg = (t & 1) ? -1.f : 1.f;
       const int kd = 1 + (t >> 1);
       const float w1 = dim == 3 ? sg * mu : 0.f;
@@ -511,7 +513,7 @@ __device__ __noinline__ int adj_limits(AWorld& s, Adj& A, const float* rec, int 
     const unsigned bal = __ballot_sync(FULL, on);
     if (on) {
       const int r = nlim + __popc(bal & below);
-      const bool active = (__float_as_uint(rec[T_ZONE + r / 32]) >> (r & 31)) & 1u;
+      const bool active = (A.zone[r >> 5] >> (r & 31)) & 1u;
       if (active) {
         const float pos = fminf(dlo, dhi), sg = dlo < dhi ? 1.f : -1.f;
         const float sr[2] = {ld(g1_jnt_solref), ld(g1_jnt_solref + 1)};
@@ -552,22 +554,150 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
   const int b = lane;
   const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
   const int nch = b < NB ? ldi(g1_body_nchild + b) : 0;
+  // each body's own terms first, all bodies at once (they need only the replay), kept in registers: its channels'
+  // own wrenches (Sown), the velocity / acceleration cotangents it causes, its rotation and COM-point cotangents;
+  // the level-by-level sweep then only adds the children's and does the recursion
+  float Q[4], X[3], om[3], alA[3], aoA[3], alB[3], aoB[3];
+  float omb[3] = {0.f, 0.f, 0.f}, alAb[3] = {0.f, 0.f, 0.f}, aoAb[3] = {0.f, 0.f, 0.f};
+  float alBb[3] = {0.f, 0.f, 0.f}, aoBb[3] = {0.f, 0.f, 0.f};
+  float S[36], P[6];
+  float rho[3] = {0.f, 0.f, 0.f};  // rotation cotangent (a pure moment)
+  float cwb[3] = {0.f, 0.f, 0.f};  // cotangent of the COM point
+  for (int k = 0; k < 36; k++) S[k] = 0.f;
+  for (int k = 0; k < 6; k++) P[k] = 0.f;
+  if (b >= 1 && b < NB) {
+    for (int k = 0; k < 4; k++) Q[k] = s.Q[b][k];
+    for (int k = 0; k < 3; k++) {
+      X[k] = s.X[b][k]; om[k] = A.om[b][k]; alA[k] = A.alA[b][k]; aoA[k] = A.aoA[b][k];
+      alB[k] = A.alB[b][k]; aoB[k] = A.aoB[b][k];
+    }
+    // this body's own terms
+    {
+      float ip[3] = {ld(g1_body_ipos + 3 * b), ld(g1_body_ipos + 3 * b + 1), ld(g1_body_ipos + 3 * b + 2)};
+      if (b == G1_TORSO)
+        for (int k = 0; k < 3; k++) ip[k] += s.com[k];
+      float c[3], cw[3];
+      qrot(Q, ip, c);
+      for (int k = 0; k < 3; k++) cw[k] = X[k] + c[k];
+      const float iq[4] = {ld(g1_body_iquat + 4 * b), ld(g1_body_iquat + 4 * b + 1), ld(g1_body_iquat + 4 * b + 2),
+                           ld(g1_body_iquat + 4 * b + 3)};
+      float qi[4], Rm[3][3];
+      qmul(Q, iq, qi);
+      for (int k = 0; k < 3; k++) {
+        float e[3] = {0.f, 0.f, 0.f}, col[3];
+        e[k] = 1.f;
+        qrot(qi, e, col);
+        for (int r = 0; r < 3; r++) Rm[r][k] = col[r];
+      }
+      const float In[3] = {ld(g1_body_inertia + 3 * b), ld(g1_body_inertia + 3 * b + 1),
+                           ld(g1_body_inertia + 3 * b + 2)};
+      float I[3][3];
+      for (int r = 0; r < 3; r++)
+        for (int q = 0; q < 3; q++) I[r][q] = Rm[r][0] * In[0] * Rm[q][0] + Rm[r][1] * In[1] * Rm[q][1] + Rm[r][2] * In[2] * Rm[q][2];
+      auto Iv = [&](const float* x, float* o) {
+        for (int r = 0; r < 3; r++) o[r] = I[r][0] * x[0] + I[r][1] * x[1] + I[r][2] * x[2];
+      };
+      const float m = ld(g1_body_mass + b);
+      // ---- channel A: weight -1, motion of lambda
+      {
+        const float* V = A.VL[b];
+        float u1[3], u2[3], u3[3], ac[3], F[3], Iom[3], Ial[3], N[3], t[3];
+        cross(alA, c, u1);
+        cross(om, c, u2);
+        cross(om, u2, u3);
+        for (int k = 0; k < 3; k++) { ac[k] = aoA[k] + u1[k] + u3[k]; F[k] = m * ac[k]; }
+        Iv(om, Iom);
+        Iv(alA, Ial);
+        cross(om, Iom, t);
+        for (int k = 0; k < 3; k++) N[k] = Ial[k] + t[k];
+        // own wrench at the origin into the subtree sum: (N + cw x F, F)
+        cross(cw, F, t);
+        for (int k = 0; k < 3; k++) { S[k] += N[k] + t[k]; S[3 + k] += F[k]; }
+        // cotangents: Fbar = -(V_lin + W x cw), Nbar = -W, cw gets W x F ... (psi_A = -<W_b, V^lambda_b>)
+        float Fb[3], Nb[3];
+        cross(V, cw, t);
+        for (int k = 0; k < 3; k++) { Fb[k] = -(V[3 + k] + t[k]); Nb[k] = -V[k]; }
+        cross(V, F, t);
+        for (int k = 0; k < 3; k++) cwb[k] += t[k];
+        // N = I al + om x (I om)
+        float n2[3], Inb[3], In2[3], t2[3];
+        Iv(Nb, Inb);
+        for (int k = 0; k < 3; k++) alAb[k] += Inb[k];
+        cross(Nb, om, n2);  // n . (om x I om) = (n x om) . I om
+        Iv(n2, In2);
+        cross(Iom, Nb, t);
+        cross(Nb, om, t2);
+        float Int2[3];
+        Iv(t2, Int2);
+        for (int k = 0; k < 3; k++) omb[k] += t[k] + Int2[k];
+        // rotation of the inertia: n . (I x) -> (I x) x n + (I n) x x
+        cross(Ial, Nb, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+        cross(Inb, alA, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+        cross(Iom, n2, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+        cross(In2, om, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+        // F = m ac, ac = ao + al x c + om x (om x c)
+        float acb[3], cb[3], z[3], zb[3];
+        for (int k = 0; k < 3; k++) { acb[k] = m * Fb[k]; aoAb[k] += acb[k]; }
+        cross(c, acb, t);
+        for (int k = 0; k < 3; k++) alAb[k] += t[k];
+        cross(acb, alA, cb);
+        cross(om, c, z);
+        cross(acb, om, zb);
+        cross(z, acb, t);
+        for (int k = 0; k < 3; k++) omb[k] += t[k];
+        cross(c, zb, t);
+        for (int k = 0; k < 3; k++) omb[k] += t[k];
+        cross(zb, om, t);
+        for (int k = 0; k < 3; k++) cb[k] += t[k];
+        cross(c, cb, t);  // c = R ip (relative): a rotation moment
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+      }
+      // ---- channel B: weight +1, motion of y, om = 0
+      {
+        const float* V = A.VY[b];
+        float u1[3], ac[3], F[3], N[3], t[3];
+        cross(alB, c, u1);
+        for (int k = 0; k < 3; k++) { ac[k] = aoB[k] + u1[k]; F[k] = m * ac[k]; }
+        Iv(alB, N);
+        cross(cw, F, t);
+        for (int k = 0; k < 3; k++) { S[6 + k] += N[k] + t[k]; S[9 + k] += F[k]; }
+        float Fb[3], Nb[3];
+        cross(V, cw, t);
+        for (int k = 0; k < 3; k++) { Fb[k] = V[3 + k] + t[k]; Nb[k] = V[k]; }
+        cross(F, V, t);  // cw gets Fbar-side term: Nbar_O . (cw x F) with Nbar_O = W: d/dcw = F x W
+        for (int k = 0; k < 3; k++) cwb[k] += t[k];
+        float Inb[3];
+        Iv(Nb, Inb);
+        for (int k = 0; k < 3; k++) alBb[k] += Inb[k];
+        cross(N, Nb, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+        cross(Inb, alB, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+        float acb[3], cb[3];
+        for (int k = 0; k < 3; k++) { acb[k] = m * Fb[k]; aoBb[k] += acb[k]; }
+        cross(c, acb, t);
+        for (int k = 0; k < 3; k++) alBb[k] += t[k];
+        cross(acb, alB, cb);
+        cross(c, cb, t);
+        for (int k = 0; k < 3; k++) rho[k] += t[k];
+      }
+      // the COM point's cotangent as a force at cw
+      float t[3];
+      cross(cw, cwb, t);
+      for (int k = 0; k < 3; k++) { P[k] += t[k]; P[3 + k] += cwb[k]; }
+    }
+  }
   for (int L = MAXD; L >= 1; L--) {
     if (depth == L) {
       const int d = b + 4;  // hinge dof (b >= 2)
-      float Q[4], X[3], om[3], alA[3], aoA[3], alB[3], aoB[3];
-      for (int k = 0; k < 4; k++) Q[k] = s.Q[b][k];
-      for (int k = 0; k < 3; k++) {
-        X[k] = s.X[b][k]; om[k] = A.om[b][k]; alA[k] = A.alA[b][k]; aoA[k] = A.aoA[b][k];
-        alB[k] = A.alB[b][k]; aoB[k] = A.aoB[b][k];
-      }
-      // inflow from the children: velocity / acceleration cotangents, relative-position forces, subtree sums
-      float omb[3] = {0.f, 0.f, 0.f}, alAb[3] = {0.f, 0.f, 0.f}, aoAb[3] = {0.f, 0.f, 0.f};
-      float alBb[3] = {0.f, 0.f, 0.f}, aoBb[3] = {0.f, 0.f, 0.f};
-      float S[36], P[6];
+      // the deposits, then the inflow from the children: velocity / acceleration cotangents, relative-position
+      // forces, subtree sums
       for (int k = 0; k < 18; k++) S[12 + k] = A.dep[b][k];
-      for (int k = 0; k < 12; k++) S[k] = 0.f;
-      for (int k = 0; k < 6; k++) { S[30 + k] = 0.f; P[k] = A.dep[b][18 + k]; }
+      for (int k = 0; k < 6; k++) P[k] += A.dep[b][18 + k];
       for (int ci = 0; ci < nch; ci++) {
         const int ch = ldi(g1_body_child + 3 * b + ci);
         for (int k = 0; k < 3; k++) {
@@ -579,127 +709,6 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
         cross(X, rb, t);
         for (int k = 0; k < 3; k++) { P[k] -= t[k]; P[3 + k] -= rb[k]; }
         for (int k = 0; k < 36; k++) S[k] += A.sub[ch][k];
-      }
-      // this body's own terms
-      float rho[3] = {0.f, 0.f, 0.f};  // rotation cotangent (a pure moment)
-      float cwb[3] = {0.f, 0.f, 0.f};  // cotangent of the COM point
-      {
-        float ip[3] = {ld(g1_body_ipos + 3 * b), ld(g1_body_ipos + 3 * b + 1), ld(g1_body_ipos + 3 * b + 2)};
-        if (b == G1_TORSO)
-          for (int k = 0; k < 3; k++) ip[k] += s.com[k];
-        float c[3], cw[3];
-        qrot(Q, ip, c);
-        for (int k = 0; k < 3; k++) cw[k] = X[k] + c[k];
-        const float iq[4] = {ld(g1_body_iquat + 4 * b), ld(g1_body_iquat + 4 * b + 1), ld(g1_body_iquat + 4 * b + 2),
-                             ld(g1_body_iquat + 4 * b + 3)};
-        float qi[4], Rm[3][3];
-        qmul(Q, iq, qi);
-        for (int k = 0; k < 3; k++) {
-          float e[3] = {0.f, 0.f, 0.f}, col[3];
-          e[k] = 1.f;
-          qrot(qi, e, col);
-          for (int r = 0; r < 3; r++) Rm[r][k] = col[r];
-        }
-        const float In[3] = {ld(g1_body_inertia + 3 * b), ld(g1_body_inertia + 3 * b + 1),
-                             ld(g1_body_inertia + 3 * b + 2)};
-        float I[3][3];
-        for (int r = 0; r < 3; r++)
-          for (int q = 0; q < 3; q++) I[r][q] = Rm[r][0] * In[0] * Rm[q][0] + Rm[r][1] * In[1] * Rm[q][1] + Rm[r][2] * In[2] * Rm[q][2];
-        auto Iv = [&](const float* x, float* o) {
-          for (int r = 0; r < 3; r++) o[r] = I[r][0] * x[0] + I[r][1] * x[1] + I[r][2] * x[2];
-        };
-        const float m = ld(g1_body_mass + b);
-        // ---- channel A: weight -1, motion of lambda
-        {
-          const float* V = A.VL[b];
-          float u1[3], u2[3], u3[3], ac[3], F[3], Iom[3], Ial[3], N[3], t[3];
-          cross(alA, c, u1);
-          cross(om, c, u2);
-          cross(om, u2, u3);
-          for (int k = 0; k < 3; k++) { ac[k] = aoA[k] + u1[k] + u3[k]; F[k] = m * ac[k]; }
-          Iv(om, Iom);
-          Iv(alA, Ial);
-          cross(om, Iom, t);
-          for (int k = 0; k < 3; k++) N[k] = Ial[k] + t[k];
-          // own wrench at the origin into the subtree sum: (N + cw x F, F)
-          cross(cw, F, t);
-          for (int k = 0; k < 3; k++) { S[k] += N[k] + t[k]; S[3 + k] += F[k]; }
-          // cotangents: Fbar = -(V_lin + W x cw), Nbar = -W, cw gets W x F ... (psi_A = -<W_b, V^lambda_b>)
-          float Fb[3], Nb[3];
-          cross(V, cw, t);
-          for (int k = 0; k < 3; k++) { Fb[k] = -(V[3 + k] + t[k]); Nb[k] = -V[k]; }
-          cross(V, F, t);
-          for (int k = 0; k < 3; k++) cwb[k] += t[k];
-          // N = I al + om x (I om)
-          float n2[3], Inb[3], In2[3], t2[3];
-          Iv(Nb, Inb);
-          for (int k = 0; k < 3; k++) alAb[k] += Inb[k];
-          cross(Nb, om, n2);  // n . (om x I om) = (n x om) . I om
-          Iv(n2, In2);
-          cross(Iom, Nb, t);
-          cross(Nb, om, t2);
-          float Int2[3];
-          Iv(t2, Int2);
-          for (int k = 0; k < 3; k++) omb[k] += t[k] + Int2[k];
-          // rotation of the inertia: n . (I x) -> (I x) x n + (I n) x x
-          cross(Ial, Nb, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-          cross(Inb, alA, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-          cross(Iom, n2, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-          cross(In2, om, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-          // F = m ac, ac = ao + al x c + om x (om x c)
-          float acb[3], cb[3], z[3], zb[3];
-          for (int k = 0; k < 3; k++) { acb[k] = m * Fb[k]; aoAb[k] += acb[k]; }
-          cross(c, acb, t);
-          for (int k = 0; k < 3; k++) alAb[k] += t[k];
-          cross(acb, alA, cb);
-          cross(om, c, z);
-          cross(acb, om, zb);
-          cross(z, acb, t);
-          for (int k = 0; k < 3; k++) omb[k] += t[k];
-          cross(c, zb, t);
-          for (int k = 0; k < 3; k++) omb[k] += t[k];
-          cross(zb, om, t);
-          for (int k = 0; k < 3; k++) cb[k] += t[k];
-          cross(c, cb, t);  // c = R ip (relative): a rotation moment
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-        }
-        // ---- channel B: weight +1, motion of y, om = 0
-        {
-          const float* V = A.VY[b];
-          float u1[3], ac[3], F[3], N[3], t[3];
-          cross(alB, c, u1);
-          for (int k = 0; k < 3; k++) { ac[k] = aoB[k] + u1[k]; F[k] = m * ac[k]; }
-          Iv(alB, N);
-          cross(cw, F, t);
-          for (int k = 0; k < 3; k++) { S[6 + k] += N[k] + t[k]; S[9 + k] += F[k]; }
-          float Fb[3], Nb[3];
-          cross(V, cw, t);
-          for (int k = 0; k < 3; k++) { Fb[k] = V[3 + k] + t[k]; Nb[k] = V[k]; }
-          cross(F, V, t);  // cw gets Fbar-side term: Nbar_O . (cw x F) with Nbar_O = W: d/dcw = F x W
-          for (int k = 0; k < 3; k++) cwb[k] += t[k];
-          float Inb[3];
-          Iv(Nb, Inb);
-          for (int k = 0; k < 3; k++) alBb[k] += Inb[k];
-          cross(N, Nb, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-          cross(Inb, alB, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-          float acb[3], cb[3];
-          for (int k = 0; k < 3; k++) { acb[k] = m * Fb[k]; aoBb[k] += acb[k]; }
-          cross(c, acb, t);
-          for (int k = 0; k < 3; k++) alBb[k] += t[k];
-          cross(acb, alB, cb);
-          cross(c, cb, t);
-          for (int k = 0; k < 3; k++) rho[k] += t[k];
-        }
-        // the COM point's cotangent as a force at cw
-        float t[3];
-        cross(cw, cwb, t);
-        for (int k = 0; k < 3; k++) { P[k] += t[k]; P[3 + k] += cwb[k]; }
       }
       // the velocity / acceleration recursion to the parent (hinge bodies), the dof's terms
       float up[18];
@@ -807,6 +816,18 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
 // (tangent, velocity); out: of its input (A.qout, A.vb); A.ub accumulates the ctrl gradient
 // block_sync: every warp of the block calls this together; a block barrier before the limit rows and the sweep
 // re-aligns the worlds after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
+// dst[0..NTRI) <- src (a factor from the tape): each lane's 20 loads issued before its first store, so the copy
+// waits for one memory round trip instead of one per element
+__device__ __forceinline__ void copy_factor(float* dst, const float* src, int lane) {
+  constexpr int R = (NTRI + 31) / 32;
+  float v[R];
+#pragma unroll
+  for (int q = 0; q < R; q++) v[q] = lane + 32 * q < NTRI ? __ldg(src + lane + 32 * q) : 0.f;
+#pragma unroll
+  for (int q = 0; q < R; q++)
+    if (lane + 32 * q < NTRI) dst[lane + 32 * q] = v[q];
+}
+
 __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
                                         float (*cw)[30], int lane, bool block_sync = false) {
   const float h = G1_TIMESTEP;
@@ -826,6 +847,7 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
     s.nefc = (hdr >> 8) & 255u;
     A.nlim_tape = (hdr >> 16) & 255u;
     A.clamp_lo = __float_as_uint(rec[T_CLAMP]);
+    for (int k = 0; k < NEFC / 32; k++) A.zone[k] = __float_as_uint(rec[T_ZONE + k]);
     A.clamp_hi = __float_as_uint(rec[T_CLAMP + 1]);
   }
   for (int c = lane; c < MAXCON; c += 32) {
@@ -834,6 +856,7 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
     s.con_slot[c] = (unsigned char)(e >> 9);
   }
   __syncwarp();
+  PROF_START(A);
   // A1: the integrator. v' = v + h a_adv; root rotation: q' = q exp(h w' / 2)
   {
     for (int i = lane; i < NV; i += 32) {
@@ -874,8 +897,9 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
     }
     __syncwarp();
   }
+  PROF(A, 0);
   // y = (M + h kv)^-1 abar_adv with L_Q; abar* = abar_adv - h kv y
-  for (int e = lane; e < NTRI; e += 32) s.L[e] = rec[T_LQ + e];
+  copy_factor(s.L, rec + T_LQ, lane);
   for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVQ + i];
   __syncwarp();
   for (int i = lane; i < NV; i += 32) A.lam[i] = A.y[i];
@@ -883,10 +907,11 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
   chol_solve(s.L, s.dinv, A.y, lane);
   for (int i = lane; i < NV; i += 32) A.lam[i] -= h * ld(g1_dof_kv + i) * A.y[i];
   // A2: lambda = H^-1 abar* with L_H
-  for (int e = lane; e < NTRI; e += 32) s.L[e] = rec[T_LH + e];
+  copy_factor(s.L, rec + T_LH, lane);
   for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVH + i];
   __syncwarp();
   chol_solve(s.L, s.dinv, A.lam, lane);
+  PROF(A, 1);
   // A3: replay poses and both channels; the motions of lambda, y, a*, v
   adj_replay_kin(s, A, lane);
   adj_motion(s, A, A.lam, A.VL, lane);
@@ -895,6 +920,7 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
   adj_motion(s, A, s.qvel, A.VV, lane);
   for (int b = lane; b < NB; b += 32)
     for (int k = 0; k < 24; k++) A.dep[b][k] = 0.f;
+  PROF(A, 2);
   // A5: the contacts (geom poses, rows as in the forward), in batches of 32
   for (int g = lane; g < NG; g += 32) {
     const int b = ldi(g1_geom_body + g);
@@ -927,12 +953,14 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
     }
   }
   __syncwarp();
+  PROF(A, 3);
   int mism = 0;
   for (int c0 = 0; c0 < s.ncon; c0 += 32) {
     mism |= adj_contacts(s, A, rec, cw, c0, lane);
     adj_contact_deposit(s, A, cw, c0, lane);
   }
   if (__any_sync(FULL, mism)) flags |= ADJ_REPLAY_MISMATCH;
+  PROF(A, 4);
   // A6: the limit rows; actuators
   if (block_sync) __syncthreads();
   if (adj_limits(s, A, rec, lane)) flags |= ADJ_REPLAY_MISMATCH;
@@ -954,7 +982,9 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
   // A7: the sweep
   for (int i = lane; i < NV; i += 32) A.qb[i] = 0.f;
   __syncwarp();
+  PROF(A, 5);
   adj_sweep(s, A, lane);
+  PROF(A, 6);
   // A8: the input state's tangent cotangent
   for (int i = lane; i < NV; i += 32) A.qout[i] = A.qb[i] + A.ql[i];
   __syncwarp();

@@ -51,7 +51,10 @@ struct __align__(16) Adj {
                                       // force rbar (applied as -rbar at the parent's origin)
   union {
     float sub[NB][36];                // subtree sums: W_A, W_B, G_lambda, G_a, G_v, P (6 each) (the sweep)
-    float cw[32][30];                 // a batch of 32 contacts' wrenches (the contact phase, before the sweep)
+    struct {
+      float cw[32][30];               // a batch of 32 contacts' wrenches (the contact phase, before the sweep)
+      int cbody[32];                  // their bodies: b1 | b2 << 8
+    };
   };
   float ax[NV][3];                    // dof axes (world)
   unsigned clamp_lo, clamp_hi;
@@ -467,6 +470,10 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
     }
   }
   for (int k = 0; k < 30; k++) cw[lane][k] = out[k];
+  if (c < ncon) {
+    const int pr = s.con_pair[c];
+    A.cbody[lane] = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)) | ldi(g1_geom_body + ldi(g1_pair_g2 + pr)) << 8;
+  }
   __syncwarp();
   return mismatch;
 }
@@ -479,8 +486,7 @@ __device__ __noinline__ void adj_contact_deposit(const AWorld& s, Adj& A, const 
     float acc[24];
     for (int k = 0; k < 24; k++) acc[k] = A.dep[lane][k];
     for (int i = 0; i < n; i++) {
-      const int pr = s.con_pair[c0 + i];
-      const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+      const int pb = A.cbody[i], b1 = pb & 255, b2 = pb >> 8;
       if (b2 == lane) {
         for (int k = 0; k < 18; k++) acc[k] += cw[i][k];
         for (int k = 0; k < 6; k++) acc[18 + k] += cw[i][18 + k];

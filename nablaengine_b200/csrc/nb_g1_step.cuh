@@ -85,6 +85,7 @@ struct __align__(16) World {
   int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
   int con_pair[MAXCON];
   unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
+  unsigned short con_bb[MAXCON];       // the contact's bodies b1 | b2 << 8 (contact_setup on)
   float con_dist[MAXCON], con_mu[MAXCON];
   float con_fr[MAXCON][9];             // frame rows: normal, tangent 1, tangent 2
   float con_pos[MAXCON][3];
@@ -539,9 +540,8 @@ __device__ __noinline__ void matvec(const float* A, const float* v, float* out, 
 }
 
 // the dofs that move only body 1 (m1, Jacobian sign -1) / only body 2 (m2, sign +1) of contact pair pr
-__device__ __forceinline__ void pair_masks(int pr, unsigned long long* m1, unsigned long long* m2) {
-  const unsigned long long a = g1_body_dofmask[ldi(g1_geom_body + ldi(g1_pair_g1 + pr))];
-  const unsigned long long b = g1_body_dofmask[ldi(g1_geom_body + ldi(g1_pair_g2 + pr))];
+__device__ __forceinline__ void body_masks(unsigned bb, unsigned long long* m1, unsigned long long* m2) {
+  const unsigned long long a = __ldg(g1_body_dofmask + (bb & 255u)), b = __ldg(g1_body_dofmask + (bb >> 8));
   *m1 = a & ~b;
   *m2 = b & ~a;
 }
@@ -793,7 +793,9 @@ __device__ __noinline__ void contact_setup(World& s, int lane) {
     int key = -1 - lane, lead = c;
     if (c < ncon) {
       const int pr = s.con_pair[c];
-      key = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)) * 32 + ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+      const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+      s.con_bb[c] = (unsigned short)(b1 | b2 << 8);
+      key = b1 * 32 + b2;
       for (int e = 0; e < c0; e++)  // an earlier chunk (only past 32 contacts)
         if (__float_as_int(s.cs.C[e][0]) == key) { lead = e; break; }
     }
@@ -856,8 +858,7 @@ __device__ __noinline__ void body_motion(World& s, const float* v, int lane) {
 __device__ __noinline__ void contact_jv(World& s, int lane) {
   const int ncon = s.ncon;
   for (int c = lane; c < ncon; c += 32) {
-    const int pr = s.con_pair[c];
-    const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+    const int bb = s.con_bb[c], b1 = bb & 255, b2 = bb >> 8;
     float dV[6], u[3];
     for (int k = 0; k < 6; k++) dV[k] = s.BV[b2][k] - s.BV[b1][k];
     // the relative velocity at the contact point: v_O + w x (pos - O); frame row d: row . that
@@ -958,7 +959,7 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
       s.con_row0[c] = (unsigned char)min(first, 255);
       s.con_nrow[c] = (unsigned char)nr;
       const float mu = s.con_mu[c];
-      const int b1 = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)), b2 = ldi(g1_geom_body + ldi(g1_pair_g2 + pr));
+      const int bb = s.con_bb[c], b1 = bb & 255, b2 = bb >> 8;
       float iw = ld(g1_body_invweight0 + b1) + ld(g1_body_invweight0 + b2);
       if (dim == 3) iw = (mu * mu * iw + iw) * 2.f * mu * mu / (float)G1_IMPRATIO;
       const float sr[2] = {ld(g1_pair_solref), ld(g1_pair_solref + 1)};
@@ -1060,7 +1061,7 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   for (int g = 0; g < ngroup; g++) {
     const int c = __ffsll((long long)s.grp_mask[g]) - 1;
     unsigned long long m1, m2;
-    pair_masks(s.con_pair[c], &m1, &m2);
+    body_masks(s.con_bb[c], &m1, &m2);
     const float* W = s.cs.wr[c];
     const float sg = (m2 & bit) ? 1.f : ((m1 & bit) ? -1.f : 0.f);
     if (sg != 0.f) jtf += sg * (dot3(w, W) + dot3(v, W + 3));
@@ -1141,7 +1142,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     PROF(s, 22);
     const int lead = __ffsll((long long)gm) - 1;
     unsigned long long m1, m2;
-    pair_masks(s.con_pair[lead], &m1, &m2);
+    body_masks(s.con_bb[lead], &m1, &m2);
     const unsigned long long sup = m1 | m2;
     if (uall(!any)) continue;  // no quadratic row in the group
     const int nsup = __popcll(sup);

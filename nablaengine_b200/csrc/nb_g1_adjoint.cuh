@@ -68,79 +68,118 @@ struct __align__(16) Adj {
 // ---- replay ---------------------------------------------------------------------------------------------------------
 // poses, the dofs' axes and both channels' velocities / accelerations (lane = body, by depth level)
 __device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
+  // lane = body. Poses by pointer jumping over the ancestors (a rigid transform composes associatively: 4 rounds
+  // for depths up to 15), then the velocities and both channels' accelerations as path sums of per-body increments
+  // (each increment needs only its parent's already-summed quantities), 4 rounds each: 16 dependent rounds
+  // instead of 11 levels of the whole recursion
+  static_assert(MAXD < 16, "4 pointer-jumping rounds");
   const int b = lane;
-  const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
-  if (lane == 0) {
-    s.Q[0][0] = 1.f; s.Q[0][1] = s.Q[0][2] = s.Q[0][3] = 0.f;
+  const bool body = b >= 1 && b < NB;
+  const int p = b >= 2 && b < NB ? ldi(g1_body_parent + b) : 0, d = b + 4;
+  float Q[4] = {1.f, 0.f, 0.f, 0.f}, X[3] = {0.f, 0.f, 0.f}, axl[3] = {0.f, 0.f, 0.f};
+  if (b == 1) {
+    const float q[4] = {s.qpos[3], s.qpos[4], s.qpos[5], s.qpos[6]};
+    const float n = sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
+    for (int k = 0; k < 4; k++) Q[k] = q[k] / n;
+    for (int k = 0; k < 3; k++) X[k] = s.qpos[k];
+  } else if (body) {  // the transform relative to the parent: body_pos, body_quat (x) axis-angle(hinge)
+    const float bq[4] = {ld(g1_body_quat + 4 * b), ld(g1_body_quat + 4 * b + 1), ld(g1_body_quat + 4 * b + 2),
+                         ld(g1_body_quat + 4 * b + 3)};
+    for (int k = 0; k < 3; k++) { X[k] = ld(g1_body_pos + 3 * b + k); axl[k] = ld(g1_body_axis + 3 * b + k); }
+    float sn, cs;
+    sincosf(0.5f * s.qpos[d + 1], &sn, &cs);
+    const float ha[4] = {cs, sn * axl[0], sn * axl[1], sn * axl[2]};
+    qmul(bq, ha, Q);
+  }
+  int par = p;
+#pragma unroll
+  for (int round = 0; round < 4; round++) {
+    float Qa[4], Xa[3], Qn[4], t[3];
+#pragma unroll
+    for (int k = 0; k < 4; k++) Qa[k] = __shfl_sync(FULL, Q[k], par);
+#pragma unroll
+    for (int k = 0; k < 3; k++) Xa[k] = __shfl_sync(FULL, X[k], par);
+    qmul(Qa, Q, Qn);
+    qrot(Qa, X, t);
+    for (int k = 0; k < 4; k++) Q[k] = Qn[k];
+    for (int k = 0; k < 3; k++) X[k] = Xa[k] + t[k];
+    par = __shfl_sync(FULL, par, par);
+  }
+  // the dof axes (world), the parent's pose and this body's lever arm r = X - X_parent
+  float w[3] = {0.f, 0.f, 0.f}, r[3];
+  if (b >= 2 && b < NB) qrot(Q, axl, w);
+  float Xp[3];
+  for (int k = 0; k < 3; k++) { Xp[k] = __shfl_sync(FULL, X[k], p); r[k] = X[k] - Xp[k]; }
+  const float vd = b >= 2 && b < NB ? s.qvel[d] : 0.f, ad = b >= 2 && b < NB ? s.qacc[d] : 0.f;
+  const float xd = b >= 2 && b < NB ? A.xa[d] : 0.f;
+  // path sums: om (increment w vd; the root R w_local)
+  auto path_sum = [&](float* a) {
+    int pp = p;
+#pragma unroll
+    for (int round = 0; round < 4; round++) {
+#pragma unroll
+      for (int k = 0; k < 3; k++) a[k] += __shfl_sync(FULL, a[k], pp);
+      pp = __shfl_sync(FULL, pp, pp);
+    }
+  };
+  float om[3] = {0.f, 0.f, 0.f}, alA[3] = {0.f, 0.f, 0.f}, alB[3] = {0.f, 0.f, 0.f};
+  if (b == 1) {
+    const float wl[3] = {s.qvel[3], s.qvel[4], s.qvel[5]};
+    const float al[3] = {s.qacc[3], s.qacc[4], s.qacc[5]}, xl[3] = {A.xa[3], A.xa[4], A.xa[5]};
+    qrot(Q, wl, om);
+    qrot(Q, al, alA);
+    qrot(Q, xl, alB);
+  } else if (body) {
+    for (int k = 0; k < 3; k++) om[k] = w[k] * vd;
+  }
+  path_sum(om);
+  // angular accelerations: increments om_p x (w vd) + w ad (channel A), w xd (channel B)
+  float omp[3];
+  for (int k = 0; k < 3; k++) omp[k] = __shfl_sync(FULL, om[k], p);
+  if (b >= 2 && b < NB) {
+    const float wv[3] = {w[0] * vd, w[1] * vd, w[2] * vd};
+    float u[3];
+    cross(omp, wv, u);
+    for (int k = 0; k < 3; k++) { alA[k] = u[k] + w[k] * ad; alB[k] = w[k] * xd; }
+  }
+  path_sum(alA);
+  path_sum(alB);
+  // origin accelerations: increments alA_p x r + om_p x (om_p x r), alB_p x r; the root's (a_lin - g, xa_lin)
+  float aoA[3] = {0.f, 0.f, 0.f}, aoB[3] = {0.f, 0.f, 0.f};
+  {
+    float alAp[3], alBp[3];
+    for (int k = 0; k < 3; k++) { alAp[k] = __shfl_sync(FULL, alA[k], p); alBp[k] = __shfl_sync(FULL, alB[k], p); }
+    if (b == 1) {
+      for (int k = 0; k < 3; k++) { aoA[k] = s.qacc[k]; aoB[k] = A.xa[k]; }
+      aoA[2] -= G1_GRAVITY_Z;
+    } else if (body) {
+      float u2[3], u3[3], u4[3], u5[3];
+      cross(alAp, r, u2);
+      cross(omp, r, u3);
+      cross(omp, u3, u4);
+      cross(alBp, r, u5);
+      for (int k = 0; k < 3; k++) { aoA[k] = u2[k] + u4[k]; aoB[k] = u5[k]; }
+    }
+  }
+  path_sum(aoA);
+  path_sum(aoB);
+  if (b < NB) {
+    for (int k = 0; k < 4; k++) s.Q[b][k] = Q[k];
     for (int k = 0; k < 3; k++) {
-      s.X[0][k] = 0.f; A.om[0][k] = 0.f; A.alA[0][k] = 0.f; A.aoA[0][k] = 0.f; A.alB[0][k] = 0.f; A.aoB[0][k] = 0.f;
+      s.X[b][k] = X[k];
+      A.om[b][k] = om[k]; A.alA[b][k] = alA[k]; A.aoA[b][k] = aoA[k]; A.alB[b][k] = alB[k]; A.aoB[b][k] = aoB[k];
     }
-  }
-  for (int L = 1; L <= MAXD; L++) {
-    if (depth == L) {
-      if (b == 1) {
-        const float q[4] = {s.qpos[3], s.qpos[4], s.qpos[5], s.qpos[6]};
-        const float n = sqrtf(q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]);
-        for (int k = 0; k < 4; k++) s.Q[1][k] = q[k] / n;
-        const float wl[3] = {s.qvel[3], s.qvel[4], s.qvel[5]};
-        const float al[3] = {s.qacc[3], s.qacc[4], s.qacc[5]}, xl[3] = {A.xa[3], A.xa[4], A.xa[5]};
-        float om[3], alA[3], alB[3];
-        qrot(s.Q[1], wl, om);
-        qrot(s.Q[1], al, alA);
-        qrot(s.Q[1], xl, alB);
-        for (int k = 0; k < 3; k++) {
-          s.X[1][k] = s.qpos[k];
-          A.om[1][k] = om[k]; A.alA[1][k] = alA[k]; A.alB[1][k] = alB[k];
-          A.aoA[1][k] = s.qacc[k]; A.aoB[1][k] = A.xa[k];
-          const float e[3] = {k == 0 ? 1.f : 0.f, k == 1 ? 1.f : 0.f, k == 2 ? 1.f : 0.f};
-          float w[3];
-          qrot(s.Q[1], e, w);
-          for (int t = 0; t < 3; t++) { A.ax[3 + k][t] = w[t]; A.ax[k][t] = e[t]; }
-        }
-        A.aoA[1][2] -= G1_GRAVITY_Z;
-      } else {
-        const int p = ldi(g1_body_parent + b), d = b + 4;
-        float Qp[4], Xp[3], omp[3], alAp[3], aoAp[3], alBp[3], aoBp[3];
-        for (int k = 0; k < 4; k++) Qp[k] = s.Q[p][k];
-        for (int k = 0; k < 3; k++) {
-          Xp[k] = s.X[p][k]; omp[k] = A.om[p][k]; alAp[k] = A.alA[p][k]; aoAp[k] = A.aoA[p][k];
-          alBp[k] = A.alB[p][k]; aoBp[k] = A.aoB[p][k];
-        }
-        const float bq[4] = {ld(g1_body_quat + 4 * b), ld(g1_body_quat + 4 * b + 1), ld(g1_body_quat + 4 * b + 2),
-                             ld(g1_body_quat + 4 * b + 3)};
-        const float bp[3] = {ld(g1_body_pos + 3 * b), ld(g1_body_pos + 3 * b + 1), ld(g1_body_pos + 3 * b + 2)};
-        const float axl[3] = {ld(g1_body_axis + 3 * b), ld(g1_body_axis + 3 * b + 1), ld(g1_body_axis + 3 * b + 2)};
-        float q0[4], sn, cs, t[3], X[3], Q[4], w[3], r[3];
-        qmul(Qp, bq, q0);
-        qrot(Qp, bp, t);
-        for (int k = 0; k < 3; k++) X[k] = Xp[k] + t[k];
-        sincosf(0.5f * s.qpos[d + 1], &sn, &cs);
-        const float ha[4] = {cs, sn * axl[0], sn * axl[1], sn * axl[2]};
-        qmul(q0, ha, Q);
-        qrot(Q, axl, w);
-        for (int k = 0; k < 3; k++) r[k] = X[k] - Xp[k];
-        const float vd = s.qvel[d], ad = s.qacc[d], xd = A.xa[d];
-        float wv[3], u1[3], u2[3], u3[3], u4[3], u5[3];
-        for (int k = 0; k < 3; k++) wv[k] = w[k] * vd;
-        cross(omp, wv, u1);
-        cross(alAp, r, u2);
-        cross(omp, r, u3);
-        cross(omp, u3, u4);
-        cross(alBp, r, u5);
-        for (int k = 0; k < 4; k++) s.Q[b][k] = Q[k];
-        for (int k = 0; k < 3; k++) {
-          s.X[b][k] = X[k];
-          A.ax[d][k] = w[k];
-          A.om[b][k] = omp[k] + wv[k];
-          A.alA[b][k] = alAp[k] + u1[k] + w[k] * ad;
-          A.aoA[b][k] = aoAp[k] + u2[k] + u4[k];
-          A.alB[b][k] = alBp[k] + w[k] * xd;
-          A.aoB[b][k] = aoBp[k] + u5[k];
-        }
+    if (b >= 2)
+      for (int k = 0; k < 3; k++) A.ax[d][k] = w[k];
+    if (b == 1)
+      for (int k = 0; k < 3; k++) {
+        const float e[3] = {k == 0 ? 1.f : 0.f, k == 1 ? 1.f : 0.f, k == 2 ? 1.f : 0.f};
+        float wk[3];
+        qrot(Q, e, wk);
+        for (int t = 0; t < 3; t++) { A.ax[3 + k][t] = wk[t]; A.ax[k][t] = e[t]; }
       }
-    }
-    __syncwarp();
   }
+  __syncwarp();
 }
 
 // the motion of body b (angular, linear velocity of the world origin) for the generalised vector v: pointer jumping

@@ -1107,7 +1107,6 @@ __device__ __noinline__ void hessian(World& s, int lane) {
   for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
     if (s.efc_jar[r] < 0.f) s.L[TRI(s.efc_a[r], s.efc_a[r])] += s.efc_D[r];
   __syncwarp();
-  PROF(s, 21);
   for (int g = 0; g < ngroup; g++) {
     const unsigned long long gm = s.grp_mask[g];
     // K (upper triangle of 6 x 6, entry e = (e1, e2)), lane e < 21, summed over the members in contact order
@@ -1139,7 +1138,6 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     __syncwarp();
     for (int e = 0; e < 21; e++) any |= s.u.hs.K[e] != 0.f;
     __syncwarp();
-    PROF(s, 22);
     const int lead = __ffsll((long long)gm) - 1;
     unsigned long long m1, m2;
     body_masks(s.con_bb[lead], &m1, &m2);
@@ -1189,7 +1187,6 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       s.L[TRI(da, db)] += v;
     }
     __syncwarp();
-    PROF(s, 23);
   }
 }
 
@@ -1285,15 +1282,29 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
     cpart += 0.5f * (ma - s.qsm[i]) * (qa - s.qacc0[i]);
   }
   bool chg = false;
+#ifdef NB_PROFILE
+  int nchg = 0;  // rows changing zone (profile builds: a histogram of them)
+#endif
 #pragma unroll
   for (int t = 0; t < ROWS_PER_LANE; t++) {
     const int r = lane + 32 * t;
     const float xn = rx[t] + alpha * rj[t];
     chg |= (xn < 0.f) != (rx[t] < 0.f);
+#ifdef NB_PROFILE
+    nchg += r < nefc && (xn < 0.f) != (rx[t] < 0.f);
+#endif
     if (xn < 0.f) cpart += 0.5f * rD[t] * xn * xn;
     if (r < nefc) s.efc_jar[r] = xn;
   }
   const bool same_zones = !__any_sync(FULL, chg);
+#ifdef NB_PROFILE
+  {
+    const int n = (int)__reduce_add_sync(FULL, (unsigned)nchg);
+    const int slot = n == 0 ? 12 : (n <= 2 ? 13 : (n <= 4 ? 14 : (n <= 8 ? 15 : (n <= 16 ? 21 : 22))));
+    if (slot != 12) PROF_COUNT(slot, 1);
+    PROF_COUNT(23, n);
+  }
+#endif
   __syncwarp();
   PROF(s, 10);
   const float2 gc = newton_grad(s, lane, cpart);

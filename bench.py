@@ -358,7 +358,7 @@ def main():
                      "hbm_peak_gbs": peaks.get("hbm_gbs")},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "world-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": a.steps,
+        "gpu_launches": a.steps * (2 if torch_ffi._DIAG_ON[0] else 1),  # k_forward (+ its diagnostics kernel)
         "fwd_grad": {"metric": "world-steps/sec fwd+grad at B=4096/GPU (BASELINE configuration 3: loss sum(qvel'^2), "
                                "VJP w.r.t. qpos, qvel, ctrl, exact mode clamp_kv=1 normal=0, torch autograd)",
                      "value": world * fg["B"] / (fg_ms[0].item() / 1e3), "unit": "world-steps/s",

@@ -66,3 +66,36 @@ def test_backward_with_kinematics_cotangents():
     b = torch_ffi.backward(tape, x[4], x[5], cq, cv)
     for u, w in zip(a[:3], b[:3]):
         assert torch.equal(u, w)
+
+
+def test_cuda_graph_of_forward_backward_jacobian_kinematics():
+    """A whole differentiated step (forward with tape, adjoint, Jacobian, kinematics and its VJP, the diagnostics
+    kernels) captured in one CUDA graph and replayed equals the eager calls bitwise."""
+    torch = _cuda()
+    from nablaengine_b200 import torch_ffi
+    x = _x(64)
+    torch_ffi.init()
+    z = lambda *sh: torch.zeros(sh, device="cuda")  # noqa: E731
+
+    def run():
+        q1, v1, w1, info, tape = torch_ffi.forward(*x, tape=True)
+        g = torch_ffi.backward(tape, x[4], x[5], z(64, 36), 2 * v1)
+        J, _ = torch_ffi.jacobian(tape, x[4], x[5])
+        k = torch_ffi.kinematics(q1, v1, x[5])
+        kg = torch_ffi._kinematics_backward_impl(q1, v1, x[5], (z(64, 36), k[1], z(64, 31, 4), z(64, 31, 6),
+                                                                z(64, 31, 3)))
+        return (q1, v1, w1, info) + tuple(g) + (J,) + tuple(k) + tuple(kg)
+
+    ref = run()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = run()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(ref, out):
+        assert torch.equal(a, b)

@@ -223,3 +223,45 @@ def test_backward_argument_errors(truth):
         torch_ffi.backward(tape, t[4], t[5], z36, z35, clamp_soft=0.1)
     gq, gv, gu, info = torch_ffi.backward(tape, t[4], t[5], z36, z35, clamp_kv=2, ctrl=t[3])
     assert float(gq.abs().max()) == 0.0 and float(gu.abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("substeps", [1, 2])
+def test_vjp_other_substep_counts_match_oracle_fd(substeps):
+    """The adjoint of a control step of 1 or 2 substeps (the tape's records chained in reverse) against the float64
+    oracle's central differences of the same step (exact mode, converged forward)."""
+    torch = _cuda()
+    import oracle
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("vjp", B=6)
+    s["qpos"][:3, 2] -= 0.08
+    keys = ("qpos", "qvel", "warm", "ctrl", "friction", "com")
+    J = oracle.fd_jacobian(*(s[k] for k in keys), substeps=substeps)
+    rng = np.random.default_rng(11)
+    cq, cv = rng.standard_normal((6, 36)), rng.standard_normal((6, 35))
+    cq[:, 3:7] = 0.0
+    fd = np.einsum("bi,bij->bj", np.concatenate([cq, cv], 1), J)
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda() for k in keys]
+    tape = torch_ffi.forward(*t, iterations=50, substeps=substeps, tape=True)[4]
+    gq, gv, gu, info = torch_ffi.backward(tape, t[4], t[5], torch.from_numpy(cq.astype(np.float32)).cuda(),
+                                          torch.from_numpy(cv.astype(np.float32)).cuda(), substeps=substeps,
+                                          clamp_kv=1, normal=0)
+    g = np.concatenate([qpos_tangent(gq.cpu().numpy(), s["qpos"]), gv.cpu().numpy(), gu.cpu().numpy()], 1)
+    for name, sl in BLOCKS.items():
+        e = np.linalg.norm(g[:, sl] - fd[:, sl], axis=1) / np.maximum(np.linalg.norm(fd[:, sl], axis=1), 1e-9)
+        assert np.median(e) < 1e-3, (name, substeps, e)
+
+
+def test_nonfinite_inputs_are_flagged_not_fatal():
+    """A NaN state propagates to that world's outputs and gradients only, and the diagnostics count it."""
+    torch = _cuda()
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("forward", B=8)
+    t = [torch.from_numpy(s[k]).cuda() for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    t[1][2, 5] = float("nan")
+    torch_ffi.read_diagnostics(reset=True)
+    q1, v1, w1, info, tape = torch_ffi.forward(*t, tape=True)
+    gq, gv, gu, binfo = torch_ffi.backward(tape, t[4], t[5], torch.zeros_like(q1), torch.ones_like(v1))
+    ok = [i for i in range(8) if i != 2]
+    assert torch.isfinite(v1[ok]).all() and torch.isfinite(gq[ok]).all()
+    d = torch_ffi.read_diagnostics(reset=True)
+    assert d["nonfinite_rows"] >= 1 and (int(binfo[2].item()) >> 16) & 7

@@ -51,7 +51,7 @@ enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
 // Phase profile (build with -DNB_PROFILE; the product build has none of it): lane 0 of every world adds the clock64
 // cycles since the previous mark to g_prof[phase]; counters from phase 16 on count events.
 #ifdef NB_PROFILE
-constexpr int NPROF = 24;
+constexpr int NPROF = 32;
 __device__ unsigned long long g_prof[NPROF];
 #define PROF_START(s) do { __syncwarp(); if (lane == 0) (s).prof_t = clock64(); } while (0)
 #define PROF(s, k) do { __syncwarp(); if (lane == 0) { long long t_ = clock64(); \
@@ -92,7 +92,7 @@ struct __align__(16) World {
   union {  // per-contact scratch, each consumed by the phase that writes it
     float jd[MAXCON][3];  // J_d v per frame row
     float wr[MAXCON][6];  // the contact wrench at O (moment, force)
-    float C[MAXCON][5];   // Hessian coefficients of the contact's rows: nn, n1, 11, n2, 22 (and the group key)
+    float C[MAXCON][5];   // contact_setup: the group key in C[c][0]
   } cs;
   float efc_D[NEFC], efc_aref[NEFC], efc_jar[NEFC], efc_jv[NEFC];
   short efc_a[NEFC];                   // dof (limit row) or contact
@@ -138,6 +138,14 @@ __device__ __forceinline__ float ld(const float* p) { return __ldg(p); }
 __device__ __forceinline__ int ldi(const int* p) { return __ldg(p); }
 
 // M(i, j) of a symmetric matrix stored as its packed lower triangle
+// index of the (k + 1)-th set bit of m, or -1
+__device__ __forceinline__ int nth_bit(unsigned long long m, int k) {
+  const unsigned lo = (unsigned)m, hi = (unsigned)(m >> 32);
+  const int nlo = __popc(lo);
+  if (k < nlo) return (int)__fns(lo, 0, k + 1);
+  k -= nlo;
+  return k < __popc(hi) ? 32 + (int)__fns(hi, 0, k + 1) : -1;
+}
 __device__ __forceinline__ float sym(const float* A, int i, int j) { return j <= i ? A[TRI(i, j)] : A[TRI(j, i)]; }
 
 // ---- smooth dynamics ---------------------------------------------------------------------------------------------
@@ -1085,64 +1093,67 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   return make_float2(sqrtf(gn), extra);
 }
 
-// H = M + J' D J over the quadratic rows, into s.L (lower triangle). A contact's rows add J_f' C J_f with J_f its
-// frame rows and C the 3 x 3 sum of D u u' over its quadratic pyramid rows u = n +- mu t_k; J_f = G S with G the
-// 3 x 6 rows (moment, frame) and S the dofs' motion vectors, so a group of contacts adds S' K S with the 6 x 6
-// spatial stiffness K = sum G' C G, on the group's support with the columns' signs
+// H = M + J' D J over the quadratic rows, into s.L (lower triangle). A contact row with direction u (n +- mu t_k)
+// at the point pos has J_r = a' S with a = ((pos - O) x u, u) and S the dofs' motion vectors about O, so a group of
+// contacts (one body pair) adds S' K S with the 6 x 6 spatial stiffness K = sum D a a' over its quadratic rows, on
+// the group's support with the columns' signs
 __device__ __noinline__ void hessian(World& s, int lane) {
-  const int ncon = uni(s.ncon), ngroup = uni(s.ngroup);
+  const int ngroup = uni(s.ngroup);
   for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(s.L)[e] = reinterpret_cast<const float4*>(s.M)[e];
-  for (int c = lane; c < ncon; c += 32) {
-    const int r0 = s.con_row0[c], nr = s.con_nrow[c];
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int t = 0; t < nr; t++) d[t] = s.efc_jar[r0 + t] < 0.f ? s.efc_D[r0 + t] : 0.f;
-    const float mu = s.con_mu[c];
-    s.cs.C[c][0] = d[0] + d[1] + d[2] + d[3];
-    s.cs.C[c][1] = mu * (d[0] - d[1]);
-    s.cs.C[c][2] = mu * mu * (d[0] + d[1]);
-    s.cs.C[c][3] = mu * (d[2] - d[3]);
-    s.cs.C[c][4] = mu * mu * (d[2] + d[3]);
-  }
   __syncwarp();
   for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
     if (s.efc_jar[r] < 0.f) s.L[TRI(s.efc_a[r], s.efc_a[r])] += s.efc_D[r];
   __syncwarp();
+  PROF(s, 26);
   for (int g = 0; g < ngroup; g++) {
     const unsigned long long gm = s.grp_mask[g];
-    // K (upper triangle of 6 x 6, entry e = (e1, e2)), lane e < 21, summed over the members in contact order
+    // K = sum of D a a' over the group's quadratic rows, a = ((pos - O) x u, u) with u = n +- mu t_k the row's
+    // direction: lane 4 m + t holds the 21 products (upper triangle of 6 x 6, row order) of row t of the group's
+    // member m (eight members at a time), and a transposing reduction leaves entry e on lane e
+    float v[32];
+#pragma unroll
+    for (int e = 0; e < 32; e++) v[e] = 0.f;
     bool any = false;
-    if (lane < 21) {
-      int e1 = 0, rest = lane;
-      while (rest >= 6 - e1) { rest -= 6 - e1; e1++; }
-      const int e2 = e1 + rest;
-      float acc = 0.f;
-      unsigned long long m = gm;
-      while (m) {
-        const int c = __ffsll((long long)m) - 1;
-        m &= m - 1ull;
-        const float* C = s.cs.C[c];
-        if (C[0] == 0.f) continue;
-        // G rows (moment (pos - O) x row, row) at components e1 and e2
-        const float* r = s.con_pos[c];
-        float x[3], y[3];
-        for (int dd = 0; dd < 3; dd++) {
-          const float* f = s.con_fr[c] + 3 * dd;
-          x[dd] = e1 < 3 ? r[(e1 + 1) % 3] * f[(e1 + 2) % 3] - r[(e1 + 2) % 3] * f[(e1 + 1) % 3] : f[e1 - 3];
-          y[dd] = e2 < 3 ? r[(e2 + 1) % 3] * f[(e2 + 2) % 3] - r[(e2 + 2) % 3] * f[(e2 + 1) % 3] : f[e2 - 3];
-        }
-        acc += C[0] * x[0] * y[0] + C[1] * (x[0] * y[1] + x[1] * y[0]) + C[2] * x[1] * y[1]
-               + C[3] * (x[0] * y[2] + x[2] * y[0]) + C[4] * x[2] * y[2];
+    const int nmem = __popcll(gm);
+#pragma unroll 1
+    for (int base = 0; base < nmem; base += 8) {
+      const int c = nth_bit(gm, base + (lane >> 2)), t = lane & 3;
+      if (c < 0 || t >= s.con_nrow[c]) continue;
+      const int r = s.con_row0[c] + t;
+      if (!(s.efc_jar[r] < 0.f)) continue;
+      const float D = s.efc_D[r], mu = ((t & 1) ? -1.f : 1.f) * s.con_mu[c];
+      const float* f = s.con_fr[c];
+      const int k = 3 + 3 * (t >> 1);
+      const float u[3] = {f[0] + mu * f[k], f[1] + mu * f[k + 1], f[2] + mu * f[k + 2]};
+      float a[6];
+      cross(s.con_pos[c], u, a);
+      a[3] = u[0]; a[4] = u[1]; a[5] = u[2];
+      int e = 0;
+#pragma unroll
+      for (int e1 = 0; e1 < 6; e1++) {
+        const float da = D * a[e1];
+#pragma unroll
+        for (int e2 = e1; e2 < 6; e2++) v[e++] += da * a[e2];
       }
-      s.u.hs.K[lane] = acc;
+      any = true;
     }
-    __syncwarp();
-    for (int e = 0; e < 21; e++) any |= s.u.hs.K[e] != 0.f;
+    if (!__any_sync(FULL, any)) { PROF(s, 27); continue; }  // no quadratic row in the group
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1) {  // lanes with bit w keep the upper half of the entries, send the lower
+      const bool up = lane & w;
+#pragma unroll
+      for (int i = 0; i < w; i++) {
+        const float keep = up ? v[i + w] : v[i], send = up ? v[i] : v[i + w];
+        v[i] = keep + __shfl_xor_sync(FULL, send, w);
+      }
+    }
+    if (lane < 21) s.u.hs.K[lane] = v[0];
     __syncwarp();
     const int lead = __ffsll((long long)gm) - 1;
     unsigned long long m1, m2;
     body_masks(s.con_bb[lead], &m1, &m2);
     const unsigned long long sup = m1 | m2;
-    if (uall(!any)) continue;  // no quadratic row in the group
+    PROF(s, 27);
     const int nsup = __popcll(sup);
     // P_k = K s_i for the support dofs i (rank k: the k-th set bit of the support), signed
     {
@@ -1172,8 +1183,11 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       }
     }
     __syncwarp();
+    PROF(s, 28);
     // H(dof a, dof b) += (sign_a s_a) . P_b for the support pairs a >= b
     const int npair = nsup * (nsup + 1) / 2;
+    PROF_COUNT(30, 1);
+    PROF_COUNT(31, npair);
     for (int e = lane; e < npair; e += 32) {
       int a = (int)((sqrtf(8.f * e + 1.f) - 1.f) * 0.5f);
       if (TRI(a + 1, 0) <= e) a++;
@@ -1187,6 +1201,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       s.L[TRI(da, db)] += v;
     }
     __syncwarp();
+    PROF(s, 29);
   }
 }
 
@@ -1219,6 +1234,7 @@ __device__ __noinline__ void newton_begin(World& s, int lane) {
 __device__ __noinline__ void newton_iter(World& s, int lane) {
   const float scale = 1.f / ((float)G1_MEANINERTIA * NV), tol = (float)G1_TOLERANCE;
   const float cost = s.ncost;
+  PROF(s, 24);  // (profile builds: the wait at the block barrier before this iteration)
   if (uall(!s.nsame)) {  // (no row changed its zone in the last step: H and its factor in s.L are still exact)
     if (lane == 0) s.nfact++;
     hessian(s, lane);
@@ -1365,7 +1381,7 @@ __device__ __noinline__ void substep_pre(World& s, int lane, float* rec) {
 // evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
 __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float* rec) {
   const float h = G1_TIMESTEP;
-  PROF_START(s);
+  PROF(s, 25);  // (profile builds: the wait at the block barriers after this world's last iteration)
   const int it = s.nit_cur;
   if (rec) {  // the Hessian factor at the final zones (re-assembled when the last step changed a zone or none ran)
     const bool refact = !s.nsame || it == 0;

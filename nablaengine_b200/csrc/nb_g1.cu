@@ -20,10 +20,12 @@ namespace nbg1 {
 
 constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // NB_LOCKSTEP: the worlds of a block run their Newton iterations in lockstep (a block barrier per iteration): the
-// warps of an SM then fetch the same instructions at the same time, instead of each streaming the ~50 KB Newton loop
+// warps of an SM then fetch the same instructions at the same time, instead of each streaming the ~60 KB Newton loop
 // from its own position (the kernel is bound by instruction fetch otherwise). WPB = 10: one block of 10 worlds
 // (220 KB of shared memory) per SM, so the whole SM runs one instruction stream (measured: 4.06 ms at B = 4096
-// against 4.27 ms with two blocks of 5).
+// against 4.27 ms with two blocks of 5). NB_LOCKSTEP = -1 keeps one barrier per substep only (the substep
+// transitions in step, each world's Newton iterations on their own): 3.81 ms against 3.84 at the same code, and
+// it needs the Newton loop to fit the instruction cache (~40 KB measured for 10 warps on separate paths).
 constexpr int TAPE_WORDS = REC_WORDS;
 constexpr long long ABI_VERSION = 1;
 
@@ -53,7 +55,11 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   for (int k = 0; k < nsub; k++) {
     float* rec = tape && active ? tape + (w64 * nsub + k) * REC_WORDS : nullptr;
     if (active) substep_pre(s, lane, rec);
-#if NB_LOCKSTEP
+#if NB_LOCKSTEP < 0
+    // each world iterates on its own; the block meets once, after every world's last iteration
+    while (!uall(!active || s.ndone || s.nit_cur >= iterations)) newton_iter(s, lane);
+    __syncthreads();
+#elif NB_LOCKSTEP
     // rounds of up to NB_LOCKSTEP iterations per world, a block barrier after each round
     while (true) {
       for (int q = 0; q < NB_LOCKSTEP; q++) {

@@ -1022,11 +1022,13 @@ __device__ __noinline__ float total_cost(World& s, int lane) {
 // support holds it (sign +1 on body 2's chain, -1 on body 1's) and the dof's limit row
 __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   const int ncon = uni(s.ncon), ngroup = uni(s.ngroup);
+#pragma unroll 1
   for (int c = lane; c < ncon; c += 32) {
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
-    float f[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int t = 0; t < nr; t++) {
-      const float x = s.efc_jar[r0 + t];
+    float f[4];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const float x = t < nr ? s.efc_jar[r0 + t] : 0.f;
       f[t] = x < 0.f ? -s.efc_D[r0 + t] * x : 0.f;
     }
     const float mu = s.con_mu[c];
@@ -1039,6 +1041,7 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   }
   __syncwarp();
   // group sums into the leader's slot: lane (g mod 5, entry) sums, then writes after a fence
+#pragma unroll 1
   for (int g0 = 0; g0 < ngroup; g0 += 5) {
     const int g = g0 + lane / 6, e = lane % 6;
     float acc = 0.f;
@@ -1066,6 +1069,7 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   }
   const float w[3] = {s.dw[i][0], s.dw[i][1], s.dw[i][2]}, v[3] = {s.dv[i][0], s.dv[i][1], s.dv[i][2]};
   const unsigned long long bit = 1ull << i;
+#pragma unroll 1
   for (int g = 0; g < ngroup; g++) {
     const int c = __ffsll((long long)s.grp_mask[g]) - 1;
     unsigned long long m1, m2;

@@ -51,7 +51,7 @@ enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
 // Phase profile (build with -DNB_PROFILE; the product build has none of it): lane 0 of every world adds the clock64
 // cycles since the previous mark to g_prof[phase]; counters from phase 16 on count events.
 #ifdef NB_PROFILE
-constexpr int NPROF = 32;
+constexpr int NPROF = 40;
 __device__ unsigned long long g_prof[NPROF];
 #define PROF_START(s) do { __syncwarp(); if (lane == 0) (s).prof_t = clock64(); } while (0)
 #define PROF(s, k) do { __syncwarp(); if (lane == 0) { long long t_ = clock64(); \
@@ -1109,6 +1109,9 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     if (s.efc_jar[r] < 0.f) s.L[TRI(s.efc_a[r], s.efc_a[r])] += s.efc_D[r];
   __syncwarp();
   PROF(s, 26);
+#ifdef NB_PROFILE
+  bool xbranch = false;  // a group on two branches of the tree (H fills outside M's pattern)
+#endif
   for (int g = 0; g < ngroup; g++) {
     const unsigned long long gm = s.grp_mask[g];
     // K = sum of D a a' over the group's quadratic rows, a = ((pos - O) x u, u) with u = n +- mu t_k the row's
@@ -1158,6 +1161,9 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     body_masks(s.con_bb[lead], &m1, &m2);
     const unsigned long long sup = m1 | m2;
     PROF(s, 27);
+#ifdef NB_PROFILE
+    xbranch |= m1 != 0ull && m2 != 0ull;
+#endif
     const int nsup = __popcll(sup);
     // P_k = K s_i for the support dofs i (rank k: the k-th set bit of the support), signed
     {
@@ -1207,6 +1213,10 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     __syncwarp();
     PROF(s, 29);
   }
+#ifdef NB_PROFILE
+  PROF_COUNT(32, xbranch ? 1 : 0);
+  PROF_COUNT(33, 1);
+#endif
 }
 
 // Newton from the warm start (or qacc_smooth when that costs less): newton_begin picks the start and forms the

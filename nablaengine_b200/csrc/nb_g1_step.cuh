@@ -450,74 +450,82 @@ __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, 
   }
 }
 
-// b <- (L L')^-1 b with the factor L and dinv = 1 / diag(L) in shared memory; lane l keeps entries l and l + 32 in
-// registers. Both substitutions go in blocks of 4: the block's 4 unknowns are solved redundantly on every lane from
-// the block's diagonal entries (broadcast loads) and their current values (shuffles), then every other entry is
-// updated with the block's 4 columns (forward: L(i, block), backward: L(block, i), read as rows)
+// b <- (L L')^-1 b with the factor L and dinv = 1 / diag(L) in shared memory. Lane l keeps entry l (rows 0..31, the
+// leading block, in blocks of 4: the block's 4 unknowns are solved redundantly on every lane from the block's
+// diagonal entries (broadcast loads) and their current values (shuffles), then every other entry is updated with the
+// block's 4 columns (forward: L(i, block), backward: L(block, i), read as rows); every lane keeps the NT tail rows
+// 32..NV-1, solved after the leading block going forward (their sums over it by warp reductions) and before it going
+// backward (their columns applied to every lane's entry)
 __device__ __noinline__ void chol_solve(const float* L, const float* dinv, float* b, int lane) {
-  float y0 = b[lane], y1 = lane + 32 < NV ? b[lane + 32] : 0.f;
+  static_assert(NV - NT == 32, "the leading block is one entry per lane");
+  float y = b[lane], t[NT];
+#pragma unroll
+  for (int m = 0; m < NT; m++) t[m] = b[32 + m];
   __syncwarp();
 #pragma unroll 1
-  for (int k0 = 0; k0 < NV; k0 += CB) {
-    const int nb = min(CB, NV - k0);
+  for (int k0 = 0; k0 < 32; k0 += CB) {
     float x[CB];
 #pragma unroll
-    for (int c = 0; c < CB; c++) {
-      const int r = k0 + c;
-      x[c] = c < nb ? __shfl_sync(FULL, r < 32 ? y0 : y1, r & 31) : 0.f;
-    }
+    for (int c = 0; c < CB; c++) x[c] = __shfl_sync(FULL, y, k0 + c);
 #pragma unroll
     for (int c = 0; c < CB; c++) {
-      if (c >= nb) break;
-      const int r = k0 + c;
       float v = x[c];
 #pragma unroll
-      for (int m = 0; m < CB; m++)
-        if (m < c) v -= L[TRI(r, k0 + m)] * x[m];
-      x[c] = v * dinv[r];
+      for (int m = 0; m < c; m++) v -= L[TRI(k0 + c, k0 + m)] * x[m];
+      x[c] = v * dinv[k0 + c];
     }
 #pragma unroll
     for (int c = 0; c < CB; c++) {
-      if (c >= nb) break;
-      const int r = k0 + c;
-      if (lane == r) y0 = x[c];
-      if (lane + 32 == r) y1 = x[c];
-      if (lane > k0 + nb - 1) y0 -= L[TRI(lane, r)] * x[c];
-      if (lane + 32 < NV && lane + 32 > k0 + nb - 1) y1 -= L[TRI(lane + 32, r)] * x[c];
+      if (lane == k0 + c) y = x[c];
+      if (lane >= k0 + CB) y -= L[TRI(lane, k0 + c)] * x[c];
     }
   }
-  const int last = ((NV - 1) / CB) * CB;
+  // tail rows: t_m -= sum_{j<32} L(32 + m, j) y_j, then the NT x NT forward and backward substitutions
+  float d[NT];
+#pragma unroll
+  for (int m = 0; m < NT; m++) d[m] = L[TRI(32 + m, lane)] * y;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int m = 0; m < NT; m++) d[m] += __shfl_xor_sync(FULL, d[m], o);
+#pragma unroll
+  for (int m = 0; m < NT; m++) {
+    float v = t[m] - d[m];
+#pragma unroll
+    for (int q = 0; q < m; q++) v -= L[TRI(32 + m, 32 + q)] * t[q];
+    t[m] = v * dinv[32 + m];
+  }
+#pragma unroll
+  for (int m = NT - 1; m >= 0; m--) {
+    float v = t[m];
+#pragma unroll
+    for (int q = m + 1; q < NT; q++) v -= L[TRI(32 + q, 32 + m)] * t[q];
+    t[m] = v * dinv[32 + m];
+  }
+#pragma unroll
+  for (int m = 0; m < NT; m++) y -= L[TRI(32 + m, lane)] * t[m];
 #pragma unroll 1
-  for (int k0 = last; k0 >= 0; k0 -= CB) {
-    const int nb = min(CB, NV - k0);
+  for (int k0 = 32 - CB; k0 >= 0; k0 -= CB) {
     float x[CB];
 #pragma unroll
-    for (int c = 0; c < CB; c++) {
-      const int r = k0 + c;
-      x[c] = c < nb ? __shfl_sync(FULL, r < 32 ? y0 : y1, r & 31) : 0.f;
-    }
+    for (int c = 0; c < CB; c++) x[c] = __shfl_sync(FULL, y, k0 + c);
 #pragma unroll
     for (int c = CB - 1; c >= 0; c--) {
-      if (c >= nb) continue;
-      const int r = k0 + c;
       float v = x[c];
 #pragma unroll
-      for (int m = 0; m < CB; m++)
-        if (m > c && m < nb) v -= L[TRI(k0 + m, r)] * x[m];
-      x[c] = v * dinv[r];
+      for (int m = c + 1; m < CB; m++) v -= L[TRI(k0 + m, k0 + c)] * x[m];
+      x[c] = v * dinv[k0 + c];
     }
 #pragma unroll
     for (int c = 0; c < CB; c++) {
-      if (c >= nb) break;
-      const int r = k0 + c;
-      if (lane == r) y0 = x[c];
-      if (lane + 32 == r) y1 = x[c];
-      if (lane < k0) y0 -= L[TRI(r, lane)] * x[c];
-      if (lane + 32 < k0) y1 -= L[TRI(r, lane + 32)] * x[c];
+      if (lane == k0 + c) y = x[c];
+      if (lane < k0) y -= L[TRI(k0 + c, lane)] * x[c];
     }
   }
-  b[lane] = y0;
-  if (lane + 32 < NV) b[lane + 32] = y1;
+  b[lane] = y;
+#pragma unroll
+  for (int m = 0; m < NT; m++)
+    if (lane == m) b[32 + m] = t[m];
   __syncwarp();
 }
 

@@ -367,12 +367,12 @@ __device__ __noinline__ void mass_and_force(World& s, int lane) {
 // chol_factor: A = L L' (then chol_solve: b <- A^-1 b), left-looking (Crout) in blocks of 4 columns, in shared
 // memory, with compact code (rolled loops: a fully unrolled register factorisation is ~100 KB of instructions,
 // beyond the instruction cache). Block k0: phase 1 forms for every row i >= k0 the dot products
-// S_i^c = sum_{j<k0} L(i, j) L(c, j) for the block's columns c (lane l owns row l: its own row read once per j for
-// all four columns, rows c as broadcasts; the tail rows 32..34 split their sums over the lanes, j = lane, and reduce
-// with shuffles); phase 2 finishes the block's columns one after another with the in-block terms (row c's entries
-// from its lane by shuffle), the pivot from row c's lane, and L(i, c) = t_i / sqrt(pivot) (rsqrt refined by one
-// Newton step; the inverse also goes to dinv for the solves). A may alias L: A(i, c) is read by the lane owning row i
-// when column c is finished, just before L(i, c) replaces it.
+// S_i^c = sum_{j<k0} L(i, j) L(c, j) for the block's columns c (lane l owns row k0 + l: its own row read once per j
+// for all four columns, rows c as broadcasts); phase 2 finishes the block's columns one after another with the
+// in-block terms (row c's entries from its lane by shuffle), the pivot from row c's lane, and L(i, c) =
+// t_i / sqrt(pivot) (rsqrt refined by one Newton step; the inverse also goes to dinv for the solves). Block 0 covers
+// rows 0..31; the tail rows 32..NV-1 get their block-0 entries right after it, one row per lane. A may alias L: A(i, c)
+// is read by the lane owning row i when column c is finished, just before L(i, c) replaces it.
 __device__ __forceinline__ float rsqrt_nr(float x) {
   float r = rsqrtf(x);
   return r * (1.5f - 0.5f * x * r * r);
@@ -382,15 +382,12 @@ constexpr int CB = 4;  // column block
 constexpr int NT = NV - 32;  // tail rows 32 .. NV - 1, finished on lanes 0 .. NT - 1
 
 __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, int lane) {
-  static_assert(NV > 32 && NT <= CB, "block 0 holds every row beyond 32");
-  // Block k0 (columns k0 .. k0 + 3): lane l owns row r = k0 + l (rows k0 .. NV - 1 fit 32 lanes for k0 >= NT);
-  // in block 0 the rows 32 .. 34 are a second row of lanes 0 .. NT - 1 (block 0 has no phase 1)
+  static_assert(NV > 32 && NT <= CB, "block 1 holds every row beyond 32");
+  // Block k0 (columns k0 .. k0 + 3): lane l owns row r = k0 + l (rows k0 .. NV - 1 fit 32 lanes for k0 >= NT)
 #pragma unroll 1
   for (int k0 = 0; k0 < NV; k0 += CB) {
     const int nb = min(CB, NV - k0);
-    const int r = k0 + lane;        // this lane's row (valid when < NV)
-    const int r2 = 32 + lane;       // block 0 only: the second row (lanes < NT)
-    const bool has2 = k0 == 0 && lane < NT;
+    const int r = k0 + lane;  // this lane's row (valid when < NV)
     // phase 1: S[c] = sum_{j<k0} L(r, j) L(k0 + c, j)
     float S[CB] = {0.f, 0.f, 0.f, 0.f};
     if (r < NV && k0 > 0) {
@@ -421,32 +418,37 @@ __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, 
         }
       }
     }
-    // phase 2: the block's columns in order; lane l keeps its row's new entries lo[c] (and the second row's, lt[c])
-    float lo[CB] = {0.f, 0.f, 0.f, 0.f}, lt[CB] = {0.f, 0.f, 0.f, 0.f};
+    // phase 2: the block's columns in order; lane l keeps its row's new entries lo[c]
+    float lo[CB] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < CB; c++) {
       if (c >= nb) break;
       const int col = k0 + c;
-      float t0 = 0.f, t1 = 0.f;
+      float t0 = 0.f;
       if (r >= col && r < NV) t0 = A[TRI(r, col)] - S[c];
-      if (has2) t1 = A[TRI(r2, col)];
 #pragma unroll
-      for (int m = 0; m < CB; m++) {
-        if (m >= c) break;
-        // L(col, k0 + m): row col is lane col - k0's own row, except the block-0 rows beyond 32
-        const float lcm = (col - k0) < 32 ? __shfl_sync(FULL, lo[m], col - k0) : __shfl_sync(FULL, lt[m], col - 32);
-        t0 -= lo[m] * lcm;
-        t1 -= lt[m] * lcm;
-      }
-      const float tkk = __shfl_sync(FULL, t0, c);  // row col is lane c (col - k0 < 32 always: col <= k0 + 3)
+      for (int m = 0; m < c; m++) t0 -= lo[m] * __shfl_sync(FULL, lo[m], c);  // L(col, k0 + m): row col is lane c
+      const float tkk = __shfl_sync(FULL, t0, c);
       const float inv = rsqrt_nr(fmaxf(tkk, 1e-30f));
       lo[c] = r > col ? t0 * inv : (r == col ? tkk * inv : 0.f);
-      lt[c] = has2 ? t1 * inv : 0.f;
       if (r >= col && r < NV) L[TRI(r, col)] = lo[c];
-      if (has2) L[TRI(r2, col)] = lt[c];
       if (lane == 0) dinv[col] = inv;
     }
     __syncwarp();
+    if (k0 == 0) {  // the tail rows' entries in block 0's columns: (A(32 + l, c) - sum_{q<c} L(32 + l, q) L(c, q)) / L(c, c)
+      if (lane < NT) {
+        float e[CB];
+#pragma unroll
+        for (int c = 0; c < CB; c++) {
+          float v = A[TRI(32 + lane, c)];
+#pragma unroll
+          for (int q = 0; q < c; q++) v -= e[q] * L[TRI(c, q)];
+          e[c] = v * dinv[c];
+          L[TRI(32 + lane, c)] = e[c];
+        }
+      }
+      __syncwarp();
+    }
   }
 }
 

@@ -1107,12 +1107,54 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   return make_float2(sqrtf(gn), extra);
 }
 
+// One level of the transposing reduction of N values per lane across the warp: lanes with bit W of their index keep
+// the upper M = ceil(N / 2) values (moved down), the others the lower M, each adding its partner's copy; after the
+// levels W = 16, 8, 4, 2, 1 of 21 values (23 shuffles) lane l holds the warp sum of entry kred_slot(l) (or none: -1)
+template <int N, int W>
+__device__ __forceinline__ void kred_level(float* v, int lane) {
+  constexpr int M = (N + 1) / 2;
+  const bool up = lane & W;
+#pragma unroll
+  for (int i = 0; i < M; i++) {
+    const float hi = M + i < N ? v[M + i] : 0.f;
+    const float keep = up ? hi : v[i], send = up ? v[i] : hi;
+    v[i] = keep + __shfl_xor_sync(FULL, send, W);
+  }
+}
+__host__ __device__ constexpr int kred_slot(int l) {
+  int base = 0, cnt = 21, n = 21;
+  for (int w = 16; w >= 1; w >>= 1) {
+    const int m = (n + 1) / 2;
+    if (l & w) { base += m; cnt = cnt > m ? cnt - m : 0; } else { cnt = cnt < m ? cnt : m; }
+    n = m;
+  }
+  return cnt >= 1 ? base : -1;
+}
+struct KSlotTable { signed char slot[32]; };
+constexpr KSlotTable make_kslot_table() {
+  KSlotTable t{};
+  for (int l = 0; l < 32; l++) t.slot[l] = (signed char)kred_slot(l);
+  return t;
+}
+static __device__ const KSlotTable g_kslot = make_kslot_table();
+// support pair e (packed lower triangle of the support ranks) -> a | b << 8
+struct PairTable { unsigned short ab[KDOF * (KDOF + 1) / 2]; };
+constexpr PairTable make_pair_table() {
+  PairTable t{};
+  int e = 0;
+  for (int a = 0; a < KDOF; a++)
+    for (int b = 0; b <= a; b++) t.ab[e++] = (unsigned short)(a | b << 8);
+  return t;
+}
+static __device__ const PairTable g_pair_ab = make_pair_table();
+
 // H = M + J' D J over the quadratic rows, into s.L (lower triangle). A contact row with direction u (n +- mu t_k)
 // at the point pos has J_r = a' S with a = ((pos - O) x u, u) and S the dofs' motion vectors about O, so a group of
 // contacts (one body pair) adds S' K S with the 6 x 6 spatial stiffness K = sum D a a' over its quadratic rows, on
 // the group's support with the columns' signs
 __device__ __noinline__ void hessian(World& s, int lane) {
   const int ngroup = uni(s.ngroup);
+  const int kslot = __ldg(g_kslot.slot + lane);
   for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(s.L)[e] = reinterpret_cast<const float4*>(s.M)[e];
   __syncwarp();
   for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
@@ -1126,10 +1168,10 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     const unsigned long long gm = s.grp_mask[g];
     // K = sum of D a a' over the group's quadratic rows, a = ((pos - O) x u, u) with u = n +- mu t_k the row's
     // direction: lane 4 m + t holds the 21 products (upper triangle of 6 x 6, row order) of row t of the group's
-    // member m (eight members at a time), and a transposing reduction leaves entry e on lane e
-    float v[32];
+    // member m (eight members at a time), and a transposing reduction leaves entry kslot on each lane
+    float v[21];
 #pragma unroll
-    for (int e = 0; e < 32; e++) v[e] = 0.f;
+    for (int e = 0; e < 21; e++) v[e] = 0.f;
     bool any = false;
     const int nmem = __popcll(gm);
 #pragma unroll 1
@@ -1155,16 +1197,12 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       any = true;
     }
     if (!__any_sync(FULL, any)) { PROF(s, 27); continue; }  // no quadratic row in the group
-#pragma unroll
-    for (int w = 16; w >= 1; w >>= 1) {  // lanes with bit w keep the upper half of the entries, send the lower
-      const bool up = lane & w;
-#pragma unroll
-      for (int i = 0; i < w; i++) {
-        const float keep = up ? v[i + w] : v[i], send = up ? v[i] : v[i + w];
-        v[i] = keep + __shfl_xor_sync(FULL, send, w);
-      }
-    }
-    if (lane < 21) s.u.hs.K[lane] = v[0];
+    kred_level<21, 16>(v, lane);
+    kred_level<11, 8>(v, lane);
+    kred_level<6, 4>(v, lane);
+    kred_level<3, 2>(v, lane);
+    kred_level<2, 1>(v, lane);
+    if (kslot >= 0) s.u.hs.K[kslot] = v[0];
     __syncwarp();
     const int lead = __ffsll((long long)gm) - 1;
     unsigned long long m1, m2;
@@ -1208,11 +1246,10 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     const int npair = nsup * (nsup + 1) / 2;
     PROF_COUNT(30, 1);
     PROF_COUNT(31, npair);
+#pragma unroll 1
     for (int e = lane; e < npair; e += 32) {
-      int a = (int)((sqrtf(8.f * e + 1.f) - 1.f) * 0.5f);
-      if (TRI(a + 1, 0) <= e) a++;
-      if (TRI(a, 0) > e) a--;
-      const int b = e - TRI(a, 0);
+      const unsigned ab = __ldg(g_pair_ab.ab + e);
+      const int a = ab & 255u, b = ab >> 8;
       const int da = s.u.hs.dof[a], db = s.u.hs.dof[b];
       const float sa = ((m2 >> da) & 1ull) ? 1.f : -1.f;
       const float* P = s.u.hs.P[b];

@@ -1315,7 +1315,8 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
   a1 = warp_sum(a1);
   a2 = warp_sum(a2);
   const int nefc = uni(s.nefc);
-  float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE];
+  // per row: jar, J p, D J p and D (J p)^2 (the row's slope and curvature factors along p)
+  float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE], rdj[ROWS_PER_LANE], rdjj[ROWS_PER_LANE];
 #pragma unroll
   for (int t = 0; t < ROWS_PER_LANE; t++) {
     const int r = lane + 32 * t;
@@ -1323,10 +1324,13 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
     rx[t] = v ? s.efc_jar[r] : 0.f;
     rj[t] = v ? s.efc_jv[r] : 0.f;
     rD[t] = v ? s.efc_D[r] : 0.f;
+    rdj[t] = rD[t] * rj[t];
+    rdjj[t] = rdj[t] * rj[t];
   }
   float alpha = 0.f, lo = 0.f, hi = 1e30f, d0 = 0.f;
   unsigned zprev = 0u;
   bool nwt = false;
+  int nls = 0;
   for (int k = 0; k <= 40; k++) {
     PROF_COUNT(17, 1);
     float fd = 0.f, fdd = 0.f;
@@ -1334,11 +1338,11 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
 #pragma unroll
     for (int t = 0; t < ROWS_PER_LANE; t++) {
       const float x = rx[t] + alpha * rj[t];
-      if (x < 0.f) { z |= 1u << t; fd += rD[t] * x * rj[t]; fdd += rD[t] * rj[t] * rj[t]; }
+      if (x < 0.f) { z |= 1u << t; fd += rdj[t] * x; fdd += rdjj[t]; }
     }
     if (__all_sync(FULL, nwt && z == zprev)) break;  // the Newton step kept every row on its piece: exact minimum
     if (k == 40) break;
-    if (lane == 0) s.nls++;
+    nls++;
     fd = warp_sum(fd) + a1 + alpha * a2;
     fdd = warp_sum(fdd) + a2;
     if (k == 0) { d0 = fd; if (uall(d0 >= 0.f)) break; }
@@ -1350,6 +1354,7 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
     zprev = z;
     alpha = nx;
   }
+  if (lane == 0) s.nls += nls;
   // move along p; the new cost (0.5 (Ma - qsm)(qacc - qacc_smooth) + the rows' costs) is summed with |grad|
   float cpart = 0.f;
   for (int i = lane; i < NV; i += 32) {

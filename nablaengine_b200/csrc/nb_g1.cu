@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   for (int i = lane; i < NV; i += 32) { s.qvel[i] = qvel[w64 * NV + i]; s.qacc[i] = warm[w64 * NV + i]; }
   for (int i = lane; i < NU; i += 32) s.ctrl[i] = ctrl[w64 * NU + i];
   if (lane < 3) s.com[lane] = com[w64 * 3 + lane];
-  if (lane == 0) { s.fric = fric[w]; s.unsup = 0; s.nit = 0; }
+  if (lane == 0) { s.fric = fric[w64]; s.unsup = 0; s.nit = 0; }  // (w64: world 0 for an inactive warp)
   __syncwarp();
   for (int k = 0; k < nsub; k++) {
     float* rec = tape && active ? tape + (w64 * nsub + k) * REC_WORDS : nullptr;

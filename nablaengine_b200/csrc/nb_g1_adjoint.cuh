@@ -6,7 +6,8 @@
 // hinges; vbar'):
 //  1. integrator: q' = q (+) h v' (root quaternion q' = q exp(h w' / 2)): vbar'_tot = vbar' + h J^T qbar' (J_r(h w')
 //     the right Jacobian of SO(3) for the rotation), the input tangent gets qbar' (rotation: R(h w') qbar'_rot);
-//  2. v' = v + h a_adv, (M + h kv) a_adv = M a*: y = (M + h kv)^-1 (h vbar'_tot) with L_Q, abar* = h vbar'_tot - h kv y;
+//  2. v' = v + h a_adv, (M + h kv) a_adv = M a*: y = (M + h kv)^-1 (h vbar'_tot) with L_Q,
+//     abar* = h vbar'_tot - h kv y;
 //  3. IFT at the Newton solution g(a*) = ID(q, v, a*) - act(q, v, u) - J' f = 0: lambda = H^-1 abar* with L_H;
 //  4. the gradient of one scalar, psi = -lambda' ID(q, v, a*) + y' M(q) (a* - a_adv) + lambda' act + sum_r (J_r
 //     lambda) f_r, with respect to q (tangent), v and u. Every pose dependence is collected as a wrench at the world
@@ -18,8 +19,9 @@
 //     x = lambda, a*, v: their cotangents are the wrench of a force at the contact point, deposited on the two bodies,
 //     and enter through the motion vectors (sbar_i) and the velocity (vbar_i = s_i . wrench).
 // Self contacts (sphere / capsule pairs) are differentiated through their free (unclamped) closest-point parameters
-// (held where both capsule parameters are free on axes within ~2 degrees and normal != 0); the normal derivative kappa(d) (I - n n') of the centre distance d follows the
-// reference's option `normal` (0 exact, 1 frozen, 2 1/max(d, 1e-3), 3 (default) frozen below 1e-3 m).
+// (held where both capsule parameters are free on axes within ~2 degrees and normal != 0); the normal derivative
+// kappa(d) (I - n n') of the centre distance d follows the reference's option `normal` (0 exact, 1 frozen,
+// 2 1/max(d, 1e-3), 3 (default) frozen below 1e-3 m).
 // clamp_kv: 0 keeps the actuator damping term on clamped dofs (MuJoCo Warp's adjoint, the API default), 1 drops it
 // (exact), 2 the soft clamp surrogate with width clamp_soft.
 #pragma once
@@ -450,7 +452,8 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
       // kappa(dd) of the normal derivative kappa (I - n n'): 0 exact 1/dd, 1 frozen frame, 2 1/max(dd, eps),
       // 3 frozen below eps (strict <), eps = 1e-3 m
       const int nopt = A.normal;
-      const float kap = nopt == 1 ? 0.f : (nopt == 2 ? 1.f / fmaxf(dd, 1e-3f) : (nopt == 3 && dd < 1e-3f ? 0.f : 1.f / dd));
+      const float kap =
+          nopt == 1 ? 0.f : (nopt == 2 ? 1.f / fmaxf(dd, 1e-3f) : (nopt == 3 && dd < 1e-3f ? 0.f : 1.f / dd));
       const float nnb = dot3(nrm, nb);
       for (int k = 0; k < 3; k++) dirb[k] = nrm[k] * distb2 + kap * (nb[k] - nrm[k] * nnb);
       for (int k = 0; k < 3; k++) { v1b[k] = pb[k] - dirb[k]; v2b[k] = dirb[k]; }
@@ -638,7 +641,8 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
                            ld(g1_body_inertia + 3 * b + 2)};
       float I[3][3];
       for (int r = 0; r < 3; r++)
-        for (int q = 0; q < 3; q++) I[r][q] = Rm[r][0] * In[0] * Rm[q][0] + Rm[r][1] * In[1] * Rm[q][1] + Rm[r][2] * In[2] * Rm[q][2];
+        for (int q = 0; q < 3; q++)
+          I[r][q] = Rm[r][0] * In[0] * Rm[q][0] + Rm[r][1] * In[1] * Rm[q][1] + Rm[r][2] * In[2] * Rm[q][2];
       auto Iv = [&](const float* x, float* o) {
         for (int r = 0; r < 3; r++) o[r] = I[r][0] * x[0] + I[r][1] * x[1] + I[r][2] * x[2];
       };
@@ -821,7 +825,8 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
         for (int i = 0; i < 3; i++) {
           const float* w = A.ax[3 + i];
           A.vb[3 + i] += dot3(w, omb);  // om = sum_i w_i v_i
-          for (int k = 0; k < 3; k++) wbr[i][k] = s.qvel[3 + i] * omb[k] + s.qacc[3 + i] * alAb[k] + A.xa[3 + i] * alBb[k];
+          for (int k = 0; k < 3; k++)
+            wbr[i][k] = s.qvel[3 + i] * omb[k] + s.qacc[3 + i] * alAb[k] + A.xa[3 + i] * alBb[k];
         }
         for (int i = 0; i < 6; i++) {
           const float lam = A.lam[i], yd = A.y[i], ad = s.qacc[i], vd = s.qvel[i];

@@ -115,7 +115,9 @@ __device__ __forceinline__ void cross(const float* a, const float* b, float* o) 
   float x = a[1] * b[2] - a[2] * b[1], y = a[2] * b[0] - a[0] * b[2], z = a[0] * b[1] - a[1] * b[0];
   o[0] = x; o[1] = y; o[2] = z;
 }
-__device__ __forceinline__ float dot3(const float* a, const float* b) { return a[0] * b[0] + a[1] * b[1] + a[2] * b[2]; }
+__device__ __forceinline__ float dot3(const float* a, const float* b) {
+  return a[0] * b[0] + a[1] * b[1] + a[2] * b[2];
+}
 __device__ __forceinline__ void qrot(const float* q, const float* v, float* o) {  // o = q v q^-1
   float t[3], u[3];
   const float qv[3] = {q[1], q[2], q[3]};
@@ -435,7 +437,8 @@ __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, 
       if (lane == 0) dinv[col] = inv;
     }
     __syncwarp();
-    if (k0 == 0) {  // the tail rows' entries in block 0's columns: (A(32 + l, c) - sum_{q<c} L(32 + l, q) L(c, q)) / L(c, c)
+    // the tail rows' entries in block 0's columns: (A(32 + l, c) - sum_{q<c} L(32 + l, q) L(c, q)) / L(c, c)
+    if (k0 == 0) {
       if (lane < NT) {
         float e[CB];
 #pragma unroll
@@ -1155,7 +1158,8 @@ static __device__ const PairTable g_pair_ab = make_pair_table();
 __device__ __noinline__ void hessian(World& s, int lane) {
   const int ngroup = uni(s.ngroup);
   const int kslot = __ldg(g_kslot.slot + lane);
-  for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(s.L)[e] = reinterpret_cast<const float4*>(s.M)[e];
+  for (int e = lane; e < NTRIP / 4; e += 32)
+    reinterpret_cast<float4*>(s.L)[e] = reinterpret_cast<const float4*>(s.M)[e];
   __syncwarp();
   for (int r = lane; r < s.nlim; r += 32)  // one limit row per dof: distinct diagonal entries
     if (s.efc_jar[r] < 0.f) s.L[TRI(s.efc_a[r], s.efc_a[r])] += s.efc_D[r];

@@ -111,7 +111,8 @@ def main(argv=None):
         dist.destroy_process_group()
     if rank == 0:
         v = vec.cpu().tolist()
-        print(json.dumps({"metric": "BPTT rollout world-steps/s (fwd+grad)", "n_gpus": world, "worlds_per_gpu": a.worlds,
+        print(json.dumps({"metric": "BPTT rollout world-steps/s (fwd+grad)", "n_gpus": world,
+                          "worlds_per_gpu": a.worlds,
                           "steps": a.steps, "ms_per_rollout": t.item(),
                           "value": world * a.worlds * a.steps / (t.item() / 1e3), "unit": "world-steps/s",
                           "loss": v[0], "ctrl_grad_norm": v[1] ** 0.5, "rows": v[2], "nonfinite_rows": v[3],

@@ -14,7 +14,8 @@ def test_oracle_poses_match_mujoco_warp_contacts(golden):
     checked, worst = 0, 0.0
     for w in range(len(d["qpos"])):
         for c in range(int(d["con_count"][w])):
-            pr, dist, pos, nrm = int(d["con"][w, c, 0]), float(d["con"][w, c, 1]), d["con"][w, c, 2:5], d["con"][w, c, 5:8]
+            cw = d["con"][w, c]
+            pr, dist, pos, nrm = int(cw[0]), float(cw[1]), cw[2:5], cw[5:8]
             g1, g2 = int(m["pair_g1"][pr]), int(m["pair_g2"][pr])
             if m["geom_type"][g1] != 0:
                 continue  # floor contacts only

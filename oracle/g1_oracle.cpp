@@ -691,6 +691,51 @@ int g1_oracle_step(int nw, const double* qpos, const double* qvel, const double*
   return 0;
 }
 
+// One substep's matrices at a given state, float64 (test infrastructure, for checking the factors a tape records):
+// M (with armature), Q = M + h kv and the Newton Hessian H = M + sum D_r J_r' J_r over the rows active at qacc
+// (J_r qacc - aref_r < 0), each (nw, NV, NV); nrow (nw,) the rows built. The state is the substep's input (qpos,
+// qvel, ctrl, fric, com); qacc its Newton solution (reference step.py:1523 hessian at the final zones;
+// host.py / step.py:1969 implicitfast for Q).
+int g1_oracle_matrices(int nw, const double* qpos, const double* qvel, const double* qacc, const double* ctrl,
+                       const double* fric, const double* com, double* M, double* Q, double* H, int* nrow) {
+  if (nw < 0) return 1;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int iw = 0; iw < nw; iw++) {
+    World<double>* w = new World<double>();
+    double c[NU];
+    for (int i = 0; i < NQ; i++) w->qpos[i] = qpos[(size_t)iw * NQ + i];
+    for (int i = 0; i < NV; i++) { w->qvel[i] = qvel[(size_t)iw * NV + i]; w->qacc[i] = qacc[(size_t)iw * NV + i]; }
+    for (int i = 0; i < NU; i++) c[i] = ctrl[(size_t)iw * NU + i];
+    w->ctrl = c;
+    w->fric = fric[iw];
+    w->com = v3(com[3 * iw], com[3 * iw + 1], com[3 * iw + 2]);
+    w->unsupported = 0;
+    const double h = G1_TIMESTEP;
+    kinematics(*w);
+    dynamics(*w);
+    collision(*w);
+    make_rows(*w, h);
+    double* m = M + (size_t)iw * NV * NV;
+    double* q = Q + (size_t)iw * NV * NV;
+    double* hh = H + (size_t)iw * NV * NV;
+    for (int i = 0; i < NV; i++)
+      for (int j = 0; j < NV; j++) {
+        m[i * NV + j] = hh[i * NV + j] = q[i * NV + j] = w->M[i][j];
+        if (i == j) q[i * NV + j] += h * g1_dof_kv[i];
+      }
+    for (int r = 0; r < w->nrow; r++) {
+      double jar = -w->aref[r];
+      for (int i = 0; i < NV; i++) jar += w->J[r][i] * w->qacc[i];
+      if (jar < 0)
+        for (int i = 0; i < NV; i++)
+          for (int j = 0; j < NV; j++) hh[i * NV + j] += w->D[r] * w->J[r][i] * w->J[r][j];
+    }
+    nrow[iw] = w->nrow;
+    delete w;
+  }
+  return 0;
+}
+
 // sizes: nq, nv, nu, nbody, ngeom, npair, maxcon, nefc
 void g1_oracle_sizes(long long* out) {
   const long long s[8] = {NQ, NV, NU, NBODY, NGEOM, NPAIR, MAXCON, NEFC};

@@ -33,6 +33,8 @@ def lib():
         d, i = ctypes.c_void_p, ctypes.c_int
         _lib.g1_oracle_step.argtypes = [i, d, d, d, d, d, d, i, i, ctypes.c_double, i, i, d, d, d, d, d]
         _lib.g1_oracle_step.restype = i
+        _lib.g1_oracle_matrices.argtypes = [i] + [d] * 10
+        _lib.g1_oracle_matrices.restype = i
     return _lib
 
 
@@ -57,6 +59,20 @@ def step(qpos, qvel, warm, ctrl, friction, com, iterations=10, substeps=4, tol=1
     if rc:
         raise ValueError(f"g1_oracle_step failed ({rc})")
     return (oq, ov, ow, info, st) if stats else (oq, ov, ow, info)
+
+
+def matrices(qpos, qvel, qacc, ctrl, friction, com):
+    """(M, M + h kv, H, nrow) of one substep at its input state and Newton solution qacc, float64 (B, 35, 35) each:
+    the mass matrix with armature, the implicitfast matrix and the Newton Hessian at the rows active at qacc."""
+    B = np.asarray(qpos).shape[0]
+    args = [_c(qpos, (B, NQ)), _c(qvel, (B, NV)), _c(qacc, (B, NV)), _c(ctrl, (B, NU)), _c(friction, (B,)),
+            _c(com, (B, 3))]
+    M, Q, H = (np.zeros((B, NV, NV)) for _ in range(3))
+    nrow = np.zeros(B, np.int32)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    if lib().g1_oracle_matrices(B, *map(p, args), p(M), p(Q), p(H), p(nrow)):
+        raise ValueError("g1_oracle_matrices failed")
+    return M, Q, H, nrow
 
 
 def quat_mul(a, b):

@@ -954,7 +954,7 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
   __syncwarp();
   for (int i = lane; i < NV; i += 32) A.lam[i] = A.y[i];
   __syncwarp();
-  chol_solve(s.L, s.dinv, A.y, lane);
+  chol_solve<true>(s.L, s.dinv, A.y, lane);  // L_Q is in tree-block order
   for (int i = lane; i < NV; i += 32) A.lam[i] -= h * ld(g1_dof_kv + i) * A.y[i];
   // A2: lambda = H^-1 abar* with L_H
   copy_factor(s.L, rec + T_LH, lane);

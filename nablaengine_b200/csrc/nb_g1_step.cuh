@@ -37,7 +37,8 @@ enum : int { UNSUPPORTED_PAIR = 1, CONTACT_OVERFLOW = 4, ROW_OVERFLOW = 16 };
 
 // The forward tape: one record of REC_WORDS float32 words per world and substep (record w * nsub + k), what the
 // adjoint reads: the substep's input state, the Newton solution a*, a_adv = (M + h kv)^-1 M a*, the Cholesky factors
-// of the Newton Hessian at the final zones (L_H) and of M + h kv (L_Q) with their inverse diagonals, the contact
+// of the Newton Hessian at the final zones (L_H, dof order) and of M + h kv (L_Q, tree-block order: tb_factor) with
+// their inverse diagonals, the contact
 // table (pair | slot << 9, two 16-bit entries per word, contact order), the rows' final zone bits, the actuator
 // clamp mask (dof bits) and a header
 constexpr int T_QPOS = 0, T_QVEL = 36, T_ASTAR = 71, T_AADV = 106, T_DINVH = 141, T_DINVQ = 176, T_LH = 211;
@@ -455,17 +456,108 @@ __device__ __noinline__ void chol_factor(const float* A, float* L, float* dinv, 
   }
 }
 
+// ---- the mass matrix's factor in tree-block order -------------------------------------------------------------
+// The G1's dofs form five chains below the free root (dofs 0..5): left leg 6..11 and right leg 12..17 (children of
+// the root), the waist 18..20, left arm 21..27 and right arm 28..34 (children of the waist's last body). M (and
+// M + h kv) couples a dof only with its ancestors and descendants, so in the order legs, arms, waist, root (leaves
+// first) its Cholesky factor keeps that pattern: each limb's block factors on its own (the four in parallel), which
+// also gives the limb's columns of its ancestors' rows, and the 9 x 9 waist + root block factors last, after the
+// limbs' products are subtracted (reference src/nablaengine/g1_engine/source.py CHOL_SOLVE and MuJoCo's mj_factorM,
+// which use the same sparsity in reverse dof order). The factor is stored dense (packed lower triangle in that
+// order, zeros outside the pattern), so chol_solve<true> solves with it on vectors in dof order.
+__host__ __device__ constexpr int tb_dof(int p) { return p < 12 ? p + 6 : (p < 26 ? p + 9 : (p < 29 ? p - 8 : p - 29)); }
+__host__ __device__ constexpr int tb_pos(int d) { return d < 6 ? d + 29 : (d < 18 ? d - 6 : (d < 21 ? d + 8 : d - 9)); }
+static_assert(tb_pos(tb_dof(0)) == 0 && tb_pos(tb_dof(25)) == 25 && tb_pos(tb_dof(26)) == 26 &&
+              tb_pos(tb_dof(34)) == 34 && tb_dof(12) == 21 && tb_dof(26) == 18 && tb_dof(29) == 0, "tree-block order");
+
+// right-looking elimination of N columns (positions cp0 .. cp0 + N - 1) on register rows: lane gb + li holds the
+// row at position rowpos over those columns (the block's own rows first: lane gb + k is column k's row)
+template <int N>
+__device__ __forceinline__ void tb_rows(float (&a)[N], int li, int gb, bool act, int rowpos, int cp0, float* L,
+                                        float* dinv) {
+#pragma unroll
+  for (int k = 0; k < N; k++) {
+    const float piv = __shfl_sync(FULL, a[k], gb + k);
+    const float inv = rsqrt_nr(fmaxf(piv, 1e-30f));
+    const float l = a[k] * inv;  // L(row, column k); the pivot's own lane: sqrt(piv)
+    if (act && li >= k) L[TRI(rowpos, cp0 + k)] = l;
+    if (act && li == k) dinv[cp0 + k] = inv;
+#pragma unroll
+    for (int j = k + 1; j < N; j++) a[j] -= l * __shfl_sync(FULL, l, gb + j);
+  }
+}
+
+// L L' = P (A + kv h diag(kv)) P' with A packed in dof order (the mass matrix), P the tree-block order; L and dinv in
+// that order (L may not alias A)
+__device__ __noinline__ void tb_factor(const float* A, bool kv, float* L, float* dinv, int lane) {
+  const float h = G1_TIMESTEP;
+  for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(L)[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  const int gb = lane & 16, li = lane - gb;
+  {  // the arms (left on lanes 0..15, right on 16..31): the arm's 7 rows, then the waist's 3 and the root's 6
+    const int first = gb ? 28 : 21;
+    const int r = li < 7 ? first + li : (li < 10 ? 11 + li : li - 10);
+    float a[7];
+#pragma unroll
+    for (int q = 0; q < 7; q++)
+      a[q] = sym(A, r, first + q) + (kv && r == first + q ? h * ld(g1_dof_kv + r) : 0.f);
+    tb_rows<7>(a, li, gb, true, tb_pos(r), tb_pos(first), L, dinv);
+  }
+  {  // the legs (left on lanes 0..11, right on 16..27): the leg's 6 rows, then the root's 6
+    const int first = gb ? 12 : 6;
+    const bool act = li < 12;
+    const int r = li < 6 ? first + li : (act ? li - 6 : 0);
+    float a[6];
+#pragma unroll
+    for (int q = 0; q < 6; q++)
+      a[q] = act ? sym(A, r, first + q) + (kv && r == first + q ? h * ld(g1_dof_kv + r) : 0.f) : 0.f;
+    tb_rows<6>(a, li, gb, act, tb_pos(r), tb_pos(first), L, dinv);
+  }
+  __syncwarp();
+  // the waist + root block (positions 26..34) minus the limbs' products: entry (u, v), u >= v; the waist's rows hold
+  // no leg columns (positions 0..11)
+  for (int e = lane; e < 45; e += 32) {
+    int u = (int)((sqrtf(8.f * e + 1.f) - 1.f) * 0.5f);
+    if (TRI(u + 1, 0) <= e) u++;
+    if (TRI(u, 0) > e) u--;
+    const int v = e - TRI(u, 0), pu = 26 + u, pv = 26 + v, du = tb_dof(pu), dv = tb_dof(pv);
+    const float* Lu = L + TRI(pu, 0);
+    const float* Lv = L + TRI(pv, 0);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll 1
+    for (int c = u >= 3 && v >= 3 ? 0 : 12; c < 26; c += 2) {
+      s0 += Lu[c] * Lv[c];
+      s1 += Lu[c + 1] * Lv[c + 1];
+    }
+    L[TRI(pu, pv)] = sym(A, du, dv) + (kv && u == v ? h * ld(g1_dof_kv + du) : 0.f) - (s0 + s1);
+  }
+  __syncwarp();
+  {  // the 9 x 9 block's factor on lanes 0..8
+    const bool act = lane < 9;
+    const int u = act ? lane : 0;
+    float a[9];
+#pragma unroll
+    for (int q = 0; q < 9; q++) a[q] = L[TRI(26 + max(u, q), 26 + min(u, q))];
+    __syncwarp();
+    tb_rows<9>(a, lane, 0, act, 26 + u, 26, L, dinv);
+  }
+  __syncwarp();
+}
+
 // b <- (L L')^-1 b with the factor L and dinv = 1 / diag(L) in shared memory. Lane l keeps entry l (rows 0..31, the
 // leading block, in blocks of 4: the block's 4 unknowns are solved redundantly on every lane from the block's
 // diagonal entries (broadcast loads) and their current values (shuffles), then every other entry is updated with the
 // block's 4 columns (forward: L(i, block), backward: L(block, i), read as rows); every lane keeps the NT tail rows
 // 32..NV-1, solved after the leading block going forward (their sums over it by warp reductions) and before it going
 // backward (their columns applied to every lane's entry)
+// PERM: L is in tree-block order (tb_factor) and b in dof order: entry p of the solve is b[tb_dof(p)]
+template <bool PERM = false>
 __device__ __noinline__ void chol_solve(const float* L, const float* dinv, float* b, int lane) {
   static_assert(NV - NT == 32, "the leading block is one entry per lane");
-  float y = b[lane], t[NT];
+  const int i0 = PERM ? tb_dof(lane) : lane;
+  float y = b[i0], t[NT];
 #pragma unroll
-  for (int m = 0; m < NT; m++) t[m] = b[32 + m];
+  for (int m = 0; m < NT; m++) t[m] = b[PERM ? tb_dof(32 + m) : 32 + m];
   __syncwarp();
 #pragma unroll 1
   for (int k0 = 0; k0 < 32; k0 += CB) {
@@ -527,10 +619,10 @@ __device__ __noinline__ void chol_solve(const float* L, const float* dinv, float
       if (lane < k0) y -= L[TRI(k0 + c, lane)] * x[c];
     }
   }
-  b[lane] = y;
+  b[i0] = y;
 #pragma unroll
   for (int m = 0; m < NT; m++)
-    if (lane == m) b[32 + m] = t[m];
+    if (lane == m) b[PERM ? tb_dof(32 + m) : 32 + m] = t[m];
   __syncwarp();
 }
 
@@ -1430,11 +1522,9 @@ __device__ __noinline__ void substep_pre(World& s, int lane, float* rec) {
   mass_and_force(s, lane);
   PROF(s, 2);
   // qacc_smooth = M^-1 qfrc_smooth
-  for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
   for (int i = lane; i < NV; i += 32) s.qacc0[i] = s.qsm[i];
-  __syncwarp();
-  chol_factor(s.L, s.L, s.dinv, lane);
-  chol_solve(s.L, s.dinv, s.qacc0, lane);
+  tb_factor(s.M, false, s.L, s.dinv, lane);
+  chol_solve<true>(s.L, s.dinv, s.qacc0, lane);
   PROF(s, 3);
   collision(s, lane);
   PROF(s, 4);
@@ -1492,12 +1582,9 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
     stats[4] = s.nfact; stats[5] = s.ncand; stats[6] = s.ncon_raw; stats[7] = 0;
   }
   // implicitfast: (M + h kv) a_adv = M qacc; qvel += h a_adv; qpos integrated with the new qvel
-  for (int e = lane; e < NTRI; e += 32) s.L[e] = s.M[e];
-  __syncwarp();
-  for (int i = lane; i < NV; i += 32) { s.L[TRI(i, i)] += h * ld(g1_dof_kv + i); s.tmp[i] = s.Ma[i]; }
-  __syncwarp();
-  chol_factor(s.L, s.L, s.dinv, lane);
-  chol_solve(s.L, s.dinv, s.tmp, lane);
+  for (int i = lane; i < NV; i += 32) s.tmp[i] = s.Ma[i];
+  tb_factor(s.M, true, s.L, s.dinv, lane);
+  chol_solve<true>(s.L, s.dinv, s.tmp, lane);
   if (rec) {
     tape_put(rec + T_LQ, s.L, NTRI, lane);
     tape_put(rec + T_DINVQ, s.dinv, NV, lane);

@@ -27,7 +27,7 @@ constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // transitions in step, each world's Newton iterations on their own): 3.81 ms against 3.84 at the same code, and
 // it needs the Newton loop to fit the instruction cache (~40 KB measured for 10 warps on separate paths).
 constexpr int TAPE_WORDS = REC_WORDS;
-constexpr long long ABI_VERSION = 1;
+constexpr long long ABI_VERSION = 2;  // 2: the tape's L_Q in tree-block order
 
 __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __restrict__ qpos,
                                                       const float* __restrict__ qvel, const float* __restrict__ warm,

@@ -98,28 +98,24 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 constexpr size_t SMEM = sizeof(World) * WPB;
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
-// worlds per block of k_adjoint and rows (warps) per block of k_jacobian: 10 x 21.9 KB, one block per SM. The
-// adjoint's worlds meet at a block barrier before every substep, so the SM's warps run the same code together (one
-// instruction stream; measured at B = 4096: 1.06 ms against 1.14 ms with one world per block and no barrier); the
-// Jacobian's 10 rows of one world share its records in L1 and stay together without one (12.7 ms per 1024 worlds
-// against 14.2 with 2 rows per block)
-constexpr int AWPB = 10, JWPB = 10;
+// worlds per block of k_adjoint: 10 x 21.9 KB, one block per SM. The worlds meet at a block barrier before every
+// substep, so the SM's warps run the same code together (one instruction stream; measured at B = 4096: 1.06 ms
+// against 1.14 ms with one world per block and no barrier)
+constexpr int AWPB = 10;
 struct AdjBlock { AWorld s; Adj a; };
-constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB, JSMEM = sizeof(AdjBlock) * JWPB;
+constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
 
-// One world's adjoint over its nsub records tw (w's first record): the output cotangent is (gq, gv) (qpos form, in
-// any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel') when unit >= 0.
-// Leaves the input cotangents in A.qout (dof tangent), A.vb, A.ub; returns the replay flags. block_sync: a block
-// barrier before every substep (every warp of the block calls this with the same nsub).
-__device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int nsub, float fric, const float* comw,
-                                      const float* ctrlw, const float* gq, const float* gv, int unit, int clamp_kv,
-                                      float clamp_soft, int normal, int lane, bool block_sync) {
+// The starting cotangent of one adjoint over nsub records tw (the world's first record): the output cotangent is
+// (gq, gv) (qpos form, in any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel')
+// when unit >= 0; into A.qout (dof tangent), A.vb, with A.ub cleared
+template <class RW>
+__device__ __noinline__ void adj_row_init(RW& A, const float* tw, int nsub, const float* gq, const float* gv, int unit,
+                                          int normal, int lane) {
   const float h = G1_TIMESTEP;
-  if (lane == 0) { s.fric = fric; A.normal = normal; }
-  if (lane < 3) s.com[lane] = comw[lane];
+  if (lane == 0) A.normal = normal;
   auto cq = [&](int i) { return unit >= 0 ? (i == unit ? 1.f : 0.f) : gq[i]; };
   auto cv = [&](int i) { return unit >= 0 ? (i + NQ == unit ? 1.f : 0.f) : gv[i]; };
-  for (int i = lane; i < NU; i += 32) { A.u[i] = ctrlw ? ctrlw[i] : 0.f; A.ub[i] = 0.f; }
+  for (int i = lane; i < NU; i += 32) A.ub[i] = 0.f;
   for (int i = lane; i < NV; i += 32) A.vb[i] = cv(i);
   // the output cotangent in the dof tangent: the quaternion part at the output quaternion q' (re-integrated from the
   // last record): 1/2 Im(q'* gq) / |q'|^2
@@ -148,6 +144,17 @@ __device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int ns
     for (int k = 0; k < 3; k++) A.qout[3 + k] = 0.5f * m[1 + k] / n2;
   }
   __syncwarp();
+}
+
+// One world's adjoint (one warp): leaves the input cotangents in A.qout (dof tangent), A.vb, A.ub; returns the replay
+// flags. block_sync: a block barrier before every substep (every warp of the block calls this with the same nsub).
+__device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int nsub, float fric, const float* comw,
+                                      const float* ctrlw, const float* gq, const float* gv, int clamp_kv,
+                                      float clamp_soft, int normal, int lane, bool block_sync) {
+  if (lane == 0) s.fric = fric;
+  if (lane < 3) s.com[lane] = comw[lane];
+  for (int i = lane; i < NU; i += 32) A.u[i] = ctrlw ? ctrlw[i] : 0.f;
+  adj_row_init(A, tw, nsub, gq, gv, -1, normal, lane);
   int flags = 0;
   for (int k = nsub - 1; k >= 0; k--) {
     if (block_sync) __syncthreads();  // (the same value on every thread of the block)
@@ -176,7 +183,7 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
   const size_t w64 = (size_t)w;
   const float* tw = tape + w64 * nsub * REC_WORDS;
   const int flags = adj_world(s, A, tw, nsub, fric[w], com + w64 * 3, ctrl ? ctrl + w64 * NU : nullptr,
-                              gq_out + w64 * NQ, gv_out + w64 * NV, -1, clamp_kv, clamp_soft, normal, lane, true);
+                              gq_out + w64 * NQ, gv_out + w64 * NV, clamp_kv, clamp_soft, normal, lane, true);
   if (!active) return;
   // the input qpos gradient in qpos form: (q_lin, 2 xi (0, q_rot), q_hinge), xi the input quaternion
   for (int i = lane; i < NV; i += 32) {
@@ -196,30 +203,58 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
 }
 
 // The step Jacobian (B, 71, 99): row r = the VJP of output r (qpos' in qpos form 0..35, qvel' 36..70) in the
-// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). One warp per (world, row); a block holds JWPB consecutive
-// (world, row) pairs (they read the same records). info (B,): the replay flags ORed over the rows (zeroed by the
-// launcher).
-constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU;
-__global__ void __launch_bounds__(JWPB * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
-                                                        const float* __restrict__ fric, const float* __restrict__ com,
-                                                        float* __restrict__ jac, int* __restrict__ info,
-                                                        const float* __restrict__ ctrl, float clamp_soft,
-                                                        int clamp_kv, int normal) {
+// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). A block holds JR rows of one world (one warp each, JBLK
+// blocks per world) and one copy of what the rows share per record (the record's state and replay on warp 0, both
+// factors on warp 1), so the rows keep only their cotangents' state (AdjRow, 12.3 KB) and twelve fit an
+// SM. info (B,): the replay flags ORed over the rows (zeroed by the launcher).
+constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = 12, JBLK = (JROWS + JR - 1) / JR;
+struct JacBlock {
+  AWorld s;
+  float LH[NTRI], dinvH[NV + 1];
+  AdjShared W;
+  AdjRow r[JR];
+};
+constexpr size_t JSMEM = sizeof(JacBlock);
+static_assert(JSMEM <= 227 * 1024, "one Jacobian block per SM");
+__global__ void __launch_bounds__(JR * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
+                                                      const float* __restrict__ fric, const float* __restrict__ com,
+                                                      float* __restrict__ jac, int* __restrict__ info,
+                                                      const float* __restrict__ ctrl, float clamp_soft, int clamp_kv,
+                                                      int normal) {
   extern __shared__ __align__(16) unsigned char smem[];
+  JacBlock& jb = *reinterpret_cast<JacBlock*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // (world, row) pairs in order, JWPB per block: no idle warps (a block spans at most two worlds; measured 7 %
-  // faster than blocks of one world's rows, 71 = 8 x 10 - 9); no barriers (they cost 17 % here: the rows of a world
-  // run the same code and stay together)
-  const long long g = (long long)blockIdx.x * JWPB + warp;
-  if (g >= (long long)nw * JROWS) return;
-  const int w = (int)(g / JROWS), row = (int)(g % JROWS);
-  AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
+  const int w = blockIdx.x / JBLK, row = (blockIdx.x % JBLK) * JR + warp;
+  const bool active = row < JROWS;  // (the last block's spare warp stays for the barriers)
   const size_t w64 = (size_t)w;
-  const int flags = adj_world(blk.s, blk.a, tape + w64 * nsub * REC_WORDS, nsub, fric[w], com + w64 * 3,
-                              ctrl ? ctrl + w64 * NU : nullptr, nullptr, nullptr, row, clamp_kv, clamp_soft, normal,
-                              lane, false);
+  const float* tw = tape + w64 * nsub * REC_WORDS;
+  AdjRow& A = jb.r[warp];
+  if (warp == 0) {
+    if (lane == 0) jb.s.fric = fric[w];
+    if (lane < 3) jb.s.com[lane] = com[w64 * 3 + lane];
+    for (int i = lane; i < NU; i += 32) jb.W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
+  }
+  if (active) adj_row_init(A, tw, nsub, nullptr, nullptr, row, normal, lane);
+  int flags = 0;
+  for (int k = nsub - 1; k >= 0; k--) {
+    const float* rec = tw + (size_t)k * REC_WORDS;
+    __syncthreads();  // every row is done with the previous record's shared data
+    if (warp == 0) {
+      adj_record(jb.s, jb.W, rec, nullptr, nullptr, lane);
+      adj_replay(jb.s, jb.W, lane);
+    } else if (warp == 1) {
+      copy_factor(jb.s.L, rec + T_LQ, lane);
+      copy_factor(jb.LH, rec + T_LH, lane);
+      for (int i = lane; i < NV; i += 32) { jb.s.dinv[i] = rec[T_DINVQ + i]; jb.dinvH[i] = rec[T_DINVH + i]; }
+    }
+    __syncthreads();
+    if (active) {
+      adj_row_solve(jb.s, jb.W, A, rec, jb.LH, jb.dinvH, lane);
+      flags |= adj_row_rest(jb.s, jb.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
+    }
+  }
+  if (!active) return;
   float* out = jac + (w64 * JROWS + row) * JCOLS;
-  const Adj& A = blk.a;
   for (int i = lane; i < NV; i += 32) { out[i] = A.qout[i]; out[NV + i] = A.vb[i]; }
   for (int i = lane; i < NU; i += 32) out[2 * NV + i] = A.ub[i];
   if (lane == 0 && flags) atomicOr(info + w, flags);
@@ -393,8 +428,8 @@ int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, con
   if (clamp_kv == 2 && !ctrl) return (int)cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(info, 0, sizeof(int) * (size_t)nw, stream);
   if (e != cudaSuccess) return (int)e;
-  const unsigned jblocks = (unsigned)(((long long)nw * JROWS + JWPB - 1) / JWPB);
-  k_jacobian<<<jblocks, JWPB * 32, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
+  const unsigned jblocks = (unsigned)((long long)nw * JBLK);
+  k_jacobian<<<jblocks, JR * 32, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
                                                                  clamp_soft, clamp_kv, normal);
   return (int)cudaGetLastError();
 }

@@ -67,9 +67,38 @@ struct __align__(16) Adj {
 #endif
 };
 
+// The Jacobian's split of Adj: what the rows (cotangents) of one world share per record, and each row's own state
+struct __align__(16) AdjShared {
+  float xa[NV], aadv[NV], u[NU];
+  float om[NB][3], alA[NB][3], aoA[NB][3], alB[NB][3], aoB[NB][3];
+  float VA[NB][6], VV[NB][6];
+  float ax[NV][3];
+  unsigned clamp_lo, clamp_hi;
+  unsigned zone[NEFC / 32];
+  int nlim_tape, pad_[3];
+};
+struct __align__(16) AdjRow {
+  float lam[NV], y[NV], vb[NV], qb[NV], ub[NU], qout[NV], tmp2[NV], ql[NV];
+  float VL[NB][6], VY[NB][6];
+  float dep[NB][24];
+  float up[NB][18];
+  union {
+    float sub[NB][36];
+    struct {
+      float cw[32][30];
+      int cbody[32];
+    };
+  };
+  int flags, normal, pad_[2];
+#ifdef NB_PROFILE
+  long long prof_t;
+#endif
+};
+
 // ---- replay ---------------------------------------------------------------------------------------------------------
 // poses, the dofs' axes and both channels' velocities / accelerations (lane = body, by depth level)
-__device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
+template <class SH>
+__device__ __noinline__ void adj_replay_kin(AWorld& s, SH& W, int lane) {
   // lane = body. Poses by pointer jumping over the ancestors (a rigid transform composes associatively: 4 rounds
   // for depths up to 15), then the velocities and both channels' accelerations as path sums of per-body increments
   // (each increment needs only its parent's already-summed quantities), 4 rounds each: 16 dependent rounds
@@ -113,7 +142,7 @@ __device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
   float Xp[3];
   for (int k = 0; k < 3; k++) { Xp[k] = __shfl_sync(FULL, X[k], p); r[k] = X[k] - Xp[k]; }
   const float vd = b >= 2 && b < NB ? s.qvel[d] : 0.f, ad = b >= 2 && b < NB ? s.qacc[d] : 0.f;
-  const float xd = b >= 2 && b < NB ? A.xa[d] : 0.f;
+  const float xd = b >= 2 && b < NB ? W.xa[d] : 0.f;
   // path sums: om (increment w vd; the root R w_local)
   auto path_sum = [&](float* a) {
     int pp = p;
@@ -127,7 +156,7 @@ __device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
   float om[3] = {0.f, 0.f, 0.f}, alA[3] = {0.f, 0.f, 0.f}, alB[3] = {0.f, 0.f, 0.f};
   if (b == 1) {
     const float wl[3] = {s.qvel[3], s.qvel[4], s.qvel[5]};
-    const float al[3] = {s.qacc[3], s.qacc[4], s.qacc[5]}, xl[3] = {A.xa[3], A.xa[4], A.xa[5]};
+    const float al[3] = {s.qacc[3], s.qacc[4], s.qacc[5]}, xl[3] = {W.xa[3], W.xa[4], W.xa[5]};
     qrot(Q, wl, om);
     qrot(Q, al, alA);
     qrot(Q, xl, alB);
@@ -152,7 +181,7 @@ __device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
     float alAp[3], alBp[3];
     for (int k = 0; k < 3; k++) { alAp[k] = __shfl_sync(FULL, alA[k], p); alBp[k] = __shfl_sync(FULL, alB[k], p); }
     if (b == 1) {
-      for (int k = 0; k < 3; k++) { aoA[k] = s.qacc[k]; aoB[k] = A.xa[k]; }
+      for (int k = 0; k < 3; k++) { aoA[k] = s.qacc[k]; aoB[k] = W.xa[k]; }
       aoA[2] -= G1_GRAVITY_Z;
     } else if (body) {
       float u2[3], u3[3], u4[3], u5[3];
@@ -169,16 +198,16 @@ __device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
     for (int k = 0; k < 4; k++) s.Q[b][k] = Q[k];
     for (int k = 0; k < 3; k++) {
       s.X[b][k] = X[k];
-      A.om[b][k] = om[k]; A.alA[b][k] = alA[k]; A.aoA[b][k] = aoA[k]; A.alB[b][k] = alB[k]; A.aoB[b][k] = aoB[k];
+      W.om[b][k] = om[k]; W.alA[b][k] = alA[k]; W.aoA[b][k] = aoA[k]; W.alB[b][k] = alB[k]; W.aoB[b][k] = aoB[k];
     }
     if (b >= 2)
-      for (int k = 0; k < 3; k++) A.ax[d][k] = w[k];
+      for (int k = 0; k < 3; k++) W.ax[d][k] = w[k];
     if (b == 1)
       for (int k = 0; k < 3; k++) {
         const float e[3] = {k == 0 ? 1.f : 0.f, k == 1 ? 1.f : 0.f, k == 2 ? 1.f : 0.f};
         float wk[3];
         qrot(Q, e, wk);
-        for (int t = 0; t < 3; t++) { A.ax[3 + k][t] = wk[t]; A.ax[k][t] = e[t]; }
+        for (int t = 0; t < 3; t++) { W.ax[3 + k][t] = wk[t]; W.ax[k][t] = e[t]; }
       }
   }
   __syncwarp();
@@ -186,12 +215,14 @@ __device__ __noinline__ void adj_replay_kin(AWorld& s, Adj& A, int lane) {
 
 // the motion of body b (angular, linear velocity of the world origin) for the generalised vector v: pointer jumping
 // over the ancestor dofs, with the motion vectors s_i = (w_i, X_b x w_i) (root translations: (0, e_k))
-__device__ __noinline__ void adj_motion(const AWorld& s, const Adj& A, const float* v, float (*out)[6], int lane) {
+template <class SH>
+__device__ __noinline__ void adj_motion(const AWorld& s, const SH& W, const float* v, float (*out)[6],
+                                      int lane) {
   float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   int par = 0;
   if (lane == 1) {
     for (int k = 0; k < 3; k++) {
-      a[k] = v[3] * A.ax[3][k] + v[4] * A.ax[4][k] + v[5] * A.ax[5][k];
+      a[k] = v[3] * W.ax[3][k] + v[4] * W.ax[4][k] + v[5] * W.ax[5][k];
       a[3 + k] = v[k];
     }
     float xw[3];
@@ -201,8 +232,8 @@ __device__ __noinline__ void adj_motion(const AWorld& s, const Adj& A, const flo
     const int d = lane + 4;
     const float vd = v[d];
     float xw[3];
-    cross(s.X[lane], A.ax[d], xw);
-    for (int k = 0; k < 3; k++) { a[k] = vd * A.ax[d][k]; a[3 + k] = vd * xw[k]; }
+    cross(s.X[lane], W.ax[d], xw);
+    for (int k = 0; k < 3; k++) { a[k] = vd * W.ax[d][k]; a[3 + k] = vd * xw[k]; }
     par = ldi(g1_body_parent + lane);
   }
 #pragma unroll
@@ -258,7 +289,9 @@ __device__ __forceinline__ void impedance_d(const float* solimp, float pos, floa
 // Contacts (lane = contact): replay the tape's contact (pair, slot) from the geom poses, its rows' forces at the
 // tape's zones, the cotangents of J x for x = lambda, a*, v as forces at the contact point (deposited as wrenches on
 // the two bodies) and the geometry's pose wrenches. Returns the replay mismatch flag of this lane.
-__device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, float (*cw)[30], int c0, int lane) {
+template <class SH, class RW>
+__device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const float* rec, float (*cw)[30], int c0,
+                                        int lane) {
   const int ncon = s.ncon;
   const int c = c0 + lane;
   float out[30];
@@ -373,7 +406,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
     // relative point velocities u(x) = dV_lin + dW x pos for x = lambda, a*, v; jd_d(x) = fr_d . u(x)
     float u[3][3], jd[3][3];
     for (int m = 0; m < 3; m++) {
-      const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? A.VA : A.VV);
+      const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? W.VA : W.VV);
       float dV[6], t[3];
       for (int k = 0; k < 6; k++) dV[k] = B[b2][k] - B[b1][k];
       cross(dV, pos, t);
@@ -387,7 +420,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
     const float kterm = kk * imp * dist;
     for (int t = 0; t < nr; t++) {
       const int r = r0 + t;
-      if (!((A.zone[r >> 5] >> (r & 31)) & 1u)) continue;
+      if (!((W.zone[r >> 5] >> (r & 31)) & 1u)) continue;
       const float sg = (t & 1) ? -1.f : 1.f;
       const int kd = 1 + (t >> 1);
       const float w1 = dim == 3 ? sg * mu : 0.f;
@@ -411,7 +444,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
       for (int dd = 0; dd < 3; dd++)
         for (int k = 0; k < 3; k++) { ub[k] += jdb[m][dd] * fr[3 * dd + k]; frb[3 * dd + k] += jdb[m][dd] * u[m][k]; }
       // u = dV_lin + dW x pos: the wrench (pos x ubar, ubar); pos gets ubar x dW
-      const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? A.VA : A.VV);
+      const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? W.VA : W.VV);
       float dW[3], t[3];
       for (int k = 0; k < 3; k++) dW[k] = B[b2][k] - B[b1][k];
       cross(ub, dW, t);
@@ -522,7 +555,8 @@ __device__ __noinline__ int adj_contacts(AWorld& s, Adj& A, const float* rec, fl
 
 // lane = body: adds the batch's contact terms (contacts c0 .. c0 + 31, in contact order): G(x) with sign + on body 2,
 // - on body 1; the pose wrenches of each body's points
-__device__ __noinline__ void adj_contact_deposit(const AWorld& s, Adj& A, const float (*cw)[30], int c0, int lane) {
+template <class RW>
+__device__ __noinline__ void adj_contact_deposit(const AWorld& s, RW& A, const float (*cw)[30], int c0, int lane) {
   const int n = min(32, s.ncon - c0);
   if (lane < NB && lane > 0) {
     float acc[24];
@@ -545,7 +579,8 @@ __device__ __noinline__ void adj_contact_deposit(const AWorld& s, Adj& A, const 
 
 // limit rows (lane = dof, dofs 6..NV-1): replay with the forward's test, force at the tape's zone; direct tangent
 // and velocity cotangents of the dof
-__device__ __noinline__ int adj_limits(AWorld& s, Adj& A, const float* rec, int lane) {
+template <class SH, class RW>
+__device__ __noinline__ int adj_limits(AWorld& s, const SH& W, RW& A, const float* rec, int lane) {
   const float h = G1_TIMESTEP;
   int nlim = 0, mismatch = 0;
   const unsigned below = (1u << lane) - 1u;
@@ -561,7 +596,7 @@ __device__ __noinline__ int adj_limits(AWorld& s, Adj& A, const float* rec, int 
     const unsigned bal = __ballot_sync(FULL, on);
     if (on) {
       const int r = nlim + __popc(bal & below);
-      const bool active = (A.zone[r >> 5] >> (r & 31)) & 1u;
+      const bool active = (W.zone[r >> 5] >> (r & 31)) & 1u;
       if (active) {
         const float pos = fminf(dlo, dhi), sg = dlo < dhi ? 1.f : -1.f;
         const float sr[2] = {ld(g1_jnt_solref), ld(g1_jnt_solref + 1)};
@@ -583,7 +618,7 @@ __device__ __noinline__ int adj_limits(AWorld& s, Adj& A, const float* rec, int 
     }
     nlim += __popc(bal);
   }
-  mismatch = nlim != A.nlim_tape;
+  mismatch = nlim != W.nlim_tape;
   __syncwarp();
   return mismatch;
 }
@@ -598,7 +633,8 @@ __device__ __forceinline__ float wrench_dot(const float* P, const float* w, cons
 // The leaf-to-root sweep (lane = body, deepest level first): each body's local reverse of both ID channels (its
 // COM acceleration, wrench and inertia), the velocity / acceleration recursion cotangents to its parent, the
 // subtree sums, and its dofs' tangent and velocity cotangents
-__device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
+template <class SH, class RW>
+__device__ __noinline__ void adj_sweep(AWorld& s, const SH& W, RW& A, int lane) {
   const int b = lane;
   const int depth = b < NB ? ldi(g1_body_depth + b) : -1;
   const int nch = b < NB ? ldi(g1_body_nchild + b) : 0;
@@ -616,8 +652,8 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
   if (b >= 1 && b < NB) {
     for (int k = 0; k < 4; k++) Q[k] = s.Q[b][k];
     for (int k = 0; k < 3; k++) {
-      X[k] = s.X[b][k]; om[k] = A.om[b][k]; alA[k] = A.alA[b][k]; aoA[k] = A.aoA[b][k];
-      alB[k] = A.alB[b][k]; aoB[k] = A.aoB[b][k];
+      X[k] = s.X[b][k]; om[k] = W.om[b][k]; alA[k] = W.alA[b][k]; aoA[k] = W.aoA[b][k];
+      alB[k] = W.alB[b][k]; aoB[k] = W.aoB[b][k];
     }
     // this body's own terms
     {
@@ -764,11 +800,11 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
       for (int k = 0; k < 18; k++) up[k] = 0.f;
       if (b >= 2) {
         const int p = ldi(g1_body_parent + b);
-        float w[3] = {A.ax[d][0], A.ax[d][1], A.ax[d][2]}, Xp[3], omp[3], alAp[3], alBp[3], r[3];
+        float w[3] = {W.ax[d][0], W.ax[d][1], W.ax[d][2]}, Xp[3], omp[3], alAp[3], alBp[3], r[3];
         for (int k = 0; k < 3; k++) {
-          Xp[k] = s.X[p][k]; omp[k] = A.om[p][k]; alAp[k] = A.alA[p][k]; alBp[k] = A.alB[p][k]; r[k] = X[k] - Xp[k];
+          Xp[k] = s.X[p][k]; omp[k] = W.om[p][k]; alAp[k] = W.alA[p][k]; alBp[k] = W.alB[p][k]; r[k] = X[k] - Xp[k];
         }
-        const float vd = s.qvel[d], ad = s.qacc[d], xd = A.xa[d];
+        const float vd = s.qvel[d], ad = s.qacc[d], xd = W.xa[d];
         float wb[3] = {0.f, 0.f, 0.f}, t[3], z[3], zb[3], rb[3];
         // A: om_b = om_p + w vd; al_b = al_p + om_p x (w vd) + w ad; ao_b = ao_p + al_p x r + om_p x (om_p x r)
         for (int k = 0; k < 3; k++) { up[k] = omb[k]; up[3 + k] = alAb[k]; up[6 + k] = aoAb[k]; }
@@ -823,10 +859,10 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
         float t[3];
         float wbr[3][3];
         for (int i = 0; i < 3; i++) {
-          const float* w = A.ax[3 + i];
+          const float* w = W.ax[3 + i];
           A.vb[3 + i] += dot3(w, omb);  // om = sum_i w_i v_i
           for (int k = 0; k < 3; k++)
-            wbr[i][k] = s.qvel[3 + i] * omb[k] + s.qacc[3 + i] * alAb[k] + A.xa[3 + i] * alBb[k];
+            wbr[i][k] = s.qvel[3 + i] * omb[k] + s.qacc[3 + i] * alAb[k] + W.xa[3 + i] * alBb[k];
         }
         for (int i = 0; i < 6; i++) {
           const float lam = A.lam[i], yd = A.y[i], ad = s.qacc[i], vd = s.qvel[i];
@@ -836,7 +872,7 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
           if (i < 3) {
             A.vb[i] += S[27 + i];  // s = (0, e_i)
           } else {
-            const float* w = A.ax[i];
+            const float* w = W.ax[i];
             A.vb[i] += wrench_dot(S + 24, w, X);
             cross(sb + 3, X, t);
             for (int k = 0; k < 3; k++) wbr[i - 3][k] += sb[k] + t[k];
@@ -847,13 +883,13 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
           }
         }
         for (int i = 0; i < 3; i++) {
-          cross(A.ax[3 + i], wbr[i], t);
+          cross(W.ax[3 + i], wbr[i], t);
           for (int k = 0; k < 3; k++) rho[k] += t[k];
         }
         for (int k = 0; k < 3; k++) P[k] += rho[k];
         for (int k = 0; k < 6; k++) S[30 + k] += P[k];
         for (int i = 0; i < 3; i++) A.qb[i] += S[33 + i];
-        for (int i = 3; i < 6; i++) A.qb[i] += wrench_dot(S + 30, A.ax[i], X);
+        for (int i = 3; i < 6; i++) A.qb[i] += wrench_dot(S + 30, W.ax[i], X);
       }
       for (int k = 0; k < 36; k++) A.sub[b][k] = S[k];
       for (int k = 0; k < 18; k++) A.up[b][k] = up[k];
@@ -862,10 +898,6 @@ __device__ __noinline__ void adj_sweep(AWorld& s, Adj& A, int lane) {
   }
 }
 
-// one substep of the adjoint: rec = its tape record; A.qout / A.vb in: the cotangents of the substep's output
-// (tangent, velocity); out: of its input (A.qout, A.vb); A.ub accumulates the ctrl gradient
-// block_sync: every warp of the block calls this together; a block barrier before the limit rows and the sweep
-// re-aligns the worlds after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
 // dst[0..NTRI) <- src (a factor from the tape): each lane's 20 loads issued before its first store, so the copy
 // waits for one memory round trip instead of one per element
 __device__ __forceinline__ void copy_factor(float* dst, const float* src, int lane) {
@@ -878,39 +910,94 @@ __device__ __forceinline__ void copy_factor(float* dst, const float* src, int la
     if (lane + 32 * q < NTRI) dst[lane + 32 * q] = v[q];
 }
 
-__device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
-                                        float (*cw)[30], int lane, bool block_sync = false) {
-  const float h = G1_TIMESTEP;
-  int flags = 0;
-  // A0: the record
+// One substep of the adjoint from its tape record rec. What every cotangent of the record shares: adj_record (the
+// record's state into s and W; with LH given also both factors: L_Q into s.L / s.dinv, L_H into LH / dinvH) and
+// adj_replay (the replayed poses, velocities and accelerations, the motions of a* and v, the geom poses and contact
+// rows). One cotangent, A.qout / A.vb in (the substep output's tangent and velocity cotangents), out the input's
+// (A.qout, A.vb), A.ub accumulating the ctrl gradient: adj_row_solve (the integrator and both solves; without LH it
+// copies each factor into s.L just before its solve) and adj_row_rest. block_sync: every warp of the block calls adj_row together; a block barrier before the limit
+// rows and the sweep re-aligns the worlds after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
+template <class SH>
+__device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, float* LH, float* dinvH, int lane) {
   for (int i = lane; i < NQ; i += 32) s.qpos[i] = rec[T_QPOS + i];
   for (int i = lane; i < NV; i += 32) {
     s.qvel[i] = rec[T_QVEL + i];
     s.qacc[i] = rec[T_ASTAR + i];
-    A.aadv[i] = rec[T_AADV + i];
-    A.xa[i] = s.qacc[i] - A.aadv[i];
-    A.ql[i] = 0.f;
+    W.aadv[i] = rec[T_AADV + i];
+    W.xa[i] = s.qacc[i] - W.aadv[i];
   }
   const unsigned hdr = __float_as_uint(rec[T_HDR]);
   if (lane == 0) {
     s.ncon = hdr & 255u;
     s.nefc = (hdr >> 8) & 255u;
-    A.nlim_tape = (hdr >> 16) & 255u;
-    A.clamp_lo = __float_as_uint(rec[T_CLAMP]);
-    for (int k = 0; k < NEFC / 32; k++) A.zone[k] = __float_as_uint(rec[T_ZONE + k]);
-    A.clamp_hi = __float_as_uint(rec[T_CLAMP + 1]);
+    W.nlim_tape = (hdr >> 16) & 255u;
+    W.clamp_lo = __float_as_uint(rec[T_CLAMP]);
+    for (int k = 0; k < NEFC / 32; k++) W.zone[k] = __float_as_uint(rec[T_ZONE + k]);
+    W.clamp_hi = __float_as_uint(rec[T_CLAMP + 1]);
   }
   for (int c = lane; c < MAXCON; c += 32) {
     const unsigned e = (__float_as_uint(rec[T_CON + c / 2]) >> (16 * (c & 1))) & 0xffffu;
     s.con_pair[c] = (int)(e & 511u);
     s.con_slot[c] = (unsigned char)(e >> 9);
   }
+  if (LH) {
+    copy_factor(s.L, rec + T_LQ, lane);
+    copy_factor(LH, rec + T_LH, lane);
+    for (int i = lane; i < NV; i += 32) { s.dinv[i] = rec[T_DINVQ + i]; dinvH[i] = rec[T_DINVH + i]; }
+  }
+  __syncwarp();
+}
+
+template <class SH>
+__device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
+  // the replay: poses and both channels; the motions of a* and v
+  adj_replay_kin(s, W, lane);
+  adj_motion(s, W, s.qacc, W.VA, lane);
+  adj_motion(s, W, s.qvel, W.VV, lane);
+  // geom poses; the contacts' rows: the same numbering as the forward (limit rows first)
+  for (int g = lane; g < NG; g += 32) {
+    const int b = ldi(g1_geom_body + g);
+    const float gp[3] = {ld(g1_geom_pos + 3 * g), ld(g1_geom_pos + 3 * g + 1), ld(g1_geom_pos + 3 * g + 2)};
+    const float gq[4] = {ld(g1_geom_quat + 4 * g), ld(g1_geom_quat + 4 * g + 1), ld(g1_geom_quat + 4 * g + 2),
+                         ld(g1_geom_quat + 4 * g + 3)};
+    float t[3];
+    qrot(s.Q[b], gp, t);
+    for (int k = 0; k < 3; k++) s.u.col.gx[g][k] = s.X[b][k] + t[k];
+    qmul(s.Q[b], gq, s.u.col.gq[g]);
+  }
+  {
+    const int ncon = s.ncon;
+    int r0 = W.nlim_tape;
+    for (int c0 = 0; c0 < ncon; c0 += 32) {
+      const int c = c0 + lane;
+      const int want = c < ncon ? (ldi(g1_pair_dim + s.con_pair[c]) == 3 ? 4 : 1) : 0;
+      int incl = want;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int first = r0 + incl - want;
+      if (c < ncon) {
+        s.con_row0[c] = (unsigned char)min(first, 255);
+        s.con_nrow[c] = (unsigned char)max(0, min(want, NEFC - first));
+      }
+      r0 += __shfl_sync(FULL, incl, 31);
+    }
+  }
+  __syncwarp();
+}
+
+template <class SH, class RW>
+__device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, const float* rec, const float* LH,
+                                              const float* dinvH, int lane) {
+  const float h = G1_TIMESTEP;
+  for (int i = lane; i < NV; i += 32) A.ql[i] = 0.f;
   __syncwarp();
   PROF_START(A);
   // A1: the integrator. v' = v + h a_adv; root rotation: q' = q exp(h w' / 2)
   {
     for (int i = lane; i < NV; i += 32) {
-      const float vnew = s.qvel[i] + h * A.aadv[i];
+      const float vnew = s.qvel[i] + h * W.aadv[i];
       A.tmp2[i] = vnew;
     }
     __syncwarp();
@@ -949,78 +1036,58 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
   }
   PROF(A, 0);
   // y = (M + h kv)^-1 abar_adv with L_Q; abar* = abar_adv - h kv y
-  copy_factor(s.L, rec + T_LQ, lane);
-  for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVQ + i];
-  __syncwarp();
+  if (!LH) {
+    copy_factor(s.L, rec + T_LQ, lane);
+    for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVQ + i];
+  }
   for (int i = lane; i < NV; i += 32) A.lam[i] = A.y[i];
   __syncwarp();
   chol_solve<true>(s.L, s.dinv, A.y, lane);  // L_Q is in tree-block order
   for (int i = lane; i < NV; i += 32) A.lam[i] -= h * ld(g1_dof_kv + i) * A.y[i];
   // A2: lambda = H^-1 abar* with L_H
-  copy_factor(s.L, rec + T_LH, lane);
-  for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVH + i];
-  __syncwarp();
-  chol_solve(s.L, s.dinv, A.lam, lane);
+  if (!LH) {
+    __syncwarp();
+    copy_factor(s.L, rec + T_LH, lane);
+    for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVH + i];
+    __syncwarp();
+    chol_solve(s.L, s.dinv, A.lam, lane);
+  } else {
+    __syncwarp();
+    chol_solve(LH, dinvH, A.lam, lane);
+  }
   PROF(A, 1);
-  // A3: replay poses and both channels; the motions of lambda, y, a*, v
-  adj_replay_kin(s, A, lane);
-  adj_motion(s, A, A.lam, A.VL, lane);
-  adj_motion(s, A, A.y, A.VY, lane);
-  adj_motion(s, A, s.qacc, A.VA, lane);
-  adj_motion(s, A, s.qvel, A.VV, lane);
+}
+
+template <class SH, class RW>
+__device__ __forceinline__ int adj_row_rest(AWorld& s, const SH& W, RW& A, const float* rec, int clamp_kv,
+                                            float clamp_soft, float (*cw)[30], int lane, bool block_sync) {
+  const float h = G1_TIMESTEP;
+  int flags = 0;
+  // A3: the motions of lambda and y (the replay and those of a*, v are shared)
+  adj_motion(s, W, A.lam, A.VL, lane);
+  adj_motion(s, W, A.y, A.VY, lane);
   for (int b = lane; b < NB; b += 32)
     for (int k = 0; k < 24; k++) A.dep[b][k] = 0.f;
   PROF(A, 2);
-  // A5: the contacts (geom poses, rows as in the forward), in batches of 32
-  for (int g = lane; g < NG; g += 32) {
-    const int b = ldi(g1_geom_body + g);
-    const float gp[3] = {ld(g1_geom_pos + 3 * g), ld(g1_geom_pos + 3 * g + 1), ld(g1_geom_pos + 3 * g + 2)};
-    const float gq[4] = {ld(g1_geom_quat + 4 * g), ld(g1_geom_quat + 4 * g + 1), ld(g1_geom_quat + 4 * g + 2),
-                         ld(g1_geom_quat + 4 * g + 3)};
-    float t[3];
-    qrot(s.Q[b], gp, t);
-    for (int k = 0; k < 3; k++) s.u.col.gx[g][k] = s.X[b][k] + t[k];
-    qmul(s.Q[b], gq, s.u.col.gq[g]);
-  }
-  // the contacts' rows: the same numbering as the forward (limit rows first)
-  {
-    const int ncon = s.ncon;
-    int r0 = A.nlim_tape;
-    for (int c0 = 0; c0 < ncon; c0 += 32) {
-      const int c = c0 + lane;
-      const int want = c < ncon ? (ldi(g1_pair_dim + s.con_pair[c]) == 3 ? 4 : 1) : 0;
-      int incl = want;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(FULL, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int first = r0 + incl - want;
-      if (c < ncon) {
-        s.con_row0[c] = (unsigned char)min(first, 255);
-        s.con_nrow[c] = (unsigned char)max(0, min(want, NEFC - first));
-      }
-      r0 += __shfl_sync(FULL, incl, 31);
-    }
-  }
   __syncwarp();
   PROF(A, 3);
   int mism = 0;
   for (int c0 = 0; c0 < s.ncon; c0 += 32) {
-    mism |= adj_contacts(s, A, rec, cw, c0, lane);
+    mism |= adj_contacts(s, W, A, rec, cw, c0, lane);
     adj_contact_deposit(s, A, cw, c0, lane);
   }
   if (__any_sync(FULL, mism)) flags |= ADJ_REPLAY_MISMATCH;
   PROF(A, 4);
   // A6: the limit rows; actuators
   if (block_sync) __syncthreads();
-  if (adj_limits(s, A, rec, lane)) flags |= ADJ_REPLAY_MISMATCH;
+  if (adj_limits(s, W, A, rec, lane)) flags |= ADJ_REPLAY_MISMATCH;
   for (int i = lane; i < NV; i += 32) {
     if (i < 6) continue;
     const float lam = A.lam[i], kp = ld(g1_dof_kp + i), kv = ld(g1_dof_kv + i);
-    const bool clamped = i < 32 ? (A.clamp_lo >> i) & 1u : (A.clamp_hi >> (i - 32)) & 1u;
+    const bool clamped = i < 32 ? (W.clamp_lo >> i) & 1u : (W.clamp_hi >> (i - 32)) & 1u;
     float wq = clamped ? 0.f : 1.f, wv = clamped ? (clamp_kv == 0 ? 1.f : 0.f) : 1.f;
     if (clamped && clamp_kv == 2 && clamp_soft > 0.f) {
-      const float f = kp * (A.u[i - 6] - s.qpos[i + 1]) - kv * s.qvel[i], lim = ld(g1_dof_frclim + i);
+      const float f = kp * (W.u[i - 6] - s.qpos[i + 1]) - kv * s.qvel[i], lim = ld(g1_dof_frclim + i);
       const float o = fmaxf(0.f, (fabsf(f) - lim) / lim);
       wq = wv = __expf(-o / clamp_soft);
     }
@@ -1033,12 +1100,21 @@ __device__ __noinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int
   for (int i = lane; i < NV; i += 32) A.qb[i] = 0.f;
   __syncwarp();
   PROF(A, 5);
-  adj_sweep(s, A, lane);
+  adj_sweep(s, W, A, lane);
   PROF(A, 6);
   // A8: the input state's tangent cotangent
   for (int i = lane; i < NV; i += 32) A.qout[i] = A.qb[i] + A.ql[i];
   __syncwarp();
   return flags;
+}
+
+// the adjoint's substep (one cotangent per world): both parts in one warp, the factors copied as they are needed
+__device__ __forceinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
+                                           float (*cw)[30], int lane, bool block_sync = false) {
+  adj_record(s, A, rec, nullptr, nullptr, lane);
+  adj_row_solve(s, A, A, rec, nullptr, nullptr, lane);
+  adj_replay(s, A, lane);
+  return adj_row_rest(s, A, A, rec, clamp_kv, clamp_soft, cw, lane, block_sync);
 }
 
 }  // namespace nbg1

@@ -204,9 +204,10 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
 
 // The step Jacobian (B, 71, 99): row r = the VJP of output r (qpos' in qpos form 0..35, qvel' 36..70) in the
 // tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). A block holds JR rows of one world (one warp each, JBLK
-// blocks per world) and one copy of what the rows share per record (the record's state and replay on warp 0, both
-// factors on warp 1), so the rows keep only their cotangents' state (AdjRow, 12.3 KB) and twelve fit an
-// SM. info (B,): the replay flags ORed over the rows (zeroed by the launcher).
+// blocks per world) and one copy of what the rows share per record, kept by a helper warp: it loads the record and
+// both factors, then replays the record while the rows run their integrator step and solves. The rows keep only
+// their cotangents' state (AdjRow, 12.3 KB), so twelve fit an SM. info (B,): the replay flags ORed over the rows
+// (zeroed by the launcher).
 constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = 12, JBLK = (JROWS + JR - 1) / JR;
 struct JacBlock {
   AWorld s;
@@ -216,20 +217,21 @@ struct JacBlock {
 };
 constexpr size_t JSMEM = sizeof(JacBlock);
 static_assert(JSMEM <= 227 * 1024, "one Jacobian block per SM");
-__global__ void __launch_bounds__(JR * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
-                                                      const float* __restrict__ fric, const float* __restrict__ com,
-                                                      float* __restrict__ jac, int* __restrict__ info,
-                                                      const float* __restrict__ ctrl, float clamp_soft, int clamp_kv,
-                                                      int normal) {
+__global__ void __launch_bounds__((JR + 1) * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
+                                                            const float* __restrict__ fric,
+                                                            const float* __restrict__ com, float* __restrict__ jac,
+                                                            int* __restrict__ info, const float* __restrict__ ctrl,
+                                                            float clamp_soft, int clamp_kv, int normal) {
   extern __shared__ __align__(16) unsigned char smem[];
   JacBlock& jb = *reinterpret_cast<JacBlock*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool helper = warp == JR;
   const int w = blockIdx.x / JBLK, row = (blockIdx.x % JBLK) * JR + warp;
-  const bool active = row < JROWS;  // (the last block's spare warp stays for the barriers)
+  const bool active = !helper && row < JROWS;  // (the last block's spare row stays for the barriers)
   const size_t w64 = (size_t)w;
   const float* tw = tape + w64 * nsub * REC_WORDS;
-  AdjRow& A = jb.r[warp];
-  if (warp == 0) {
+  AdjRow& A = jb.r[helper ? 0 : warp];
+  if (helper) {
     if (lane == 0) jb.s.fric = fric[w];
     if (lane < 3) jb.s.com[lane] = com[w64 * 3 + lane];
     for (int i = lane; i < NU; i += 32) jb.W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
@@ -239,19 +241,12 @@ __global__ void __launch_bounds__(JR * 32) k_jacobian(int nw, int nsub, const fl
   for (int k = nsub - 1; k >= 0; k--) {
     const float* rec = tw + (size_t)k * REC_WORDS;
     __syncthreads();  // every row is done with the previous record's shared data
-    if (warp == 0) {
-      adj_record(jb.s, jb.W, rec, nullptr, nullptr, lane);
-      adj_replay(jb.s, jb.W, lane);
-    } else if (warp == 1) {
-      copy_factor(jb.s.L, rec + T_LQ, lane);
-      copy_factor(jb.LH, rec + T_LH, lane);
-      for (int i = lane; i < NV; i += 32) { jb.s.dinv[i] = rec[T_DINVQ + i]; jb.dinvH[i] = rec[T_DINVH + i]; }
-    }
+    if (helper) adj_record(jb.s, jb.W, rec, jb.LH, jb.dinvH, lane);
     __syncthreads();
-    if (active) {
-      adj_row_solve(jb.s, jb.W, A, rec, jb.LH, jb.dinvH, lane);
-      flags |= adj_row_rest(jb.s, jb.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
-    }
+    if (helper) adj_replay(jb.s, jb.W, lane);
+    else if (active) adj_row_solve(jb.s, jb.W, A, rec, jb.LH, jb.dinvH, lane);
+    __syncthreads();
+    if (active) flags |= adj_row_rest(jb.s, jb.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
   }
   if (!active) return;
   float* out = jac + (w64 * JROWS + row) * JCOLS;
@@ -429,7 +424,7 @@ int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, con
   cudaError_t e = cudaMemsetAsync(info, 0, sizeof(int) * (size_t)nw, stream);
   if (e != cudaSuccess) return (int)e;
   const unsigned jblocks = (unsigned)((long long)nw * JBLK);
-  k_jacobian<<<jblocks, JR * 32, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
+  k_jacobian<<<jblocks, (JR + 1) * 32, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
                                                                  clamp_soft, clamp_kv, normal);
   return (int)cudaGetLastError();
 }

@@ -1061,7 +1061,6 @@ __device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, con
 template <class SH, class RW>
 __device__ __forceinline__ int adj_row_rest(AWorld& s, const SH& W, RW& A, const float* rec, int clamp_kv,
                                             float clamp_soft, float (*cw)[30], int lane, bool block_sync) {
-  const float h = G1_TIMESTEP;
   int flags = 0;
   // A3: the motions of lambda and y (the replay and those of a*, v are shared)
   adj_motion(s, W, A.lam, A.VL, lane);

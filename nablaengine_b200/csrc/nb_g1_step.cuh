@@ -701,24 +701,32 @@ __device__ __forceinline__ bool bounding(const World& s, int pr) {
   return dot3(dif, dif) <= rb * rb;
 }
 
-// Narrow phase of candidate pair pr: returns the number of contacts (0..2, dist < 0) and, when write is set,
-// stores them at contact slots base, base + 1 (those below MAXCON). MuJoCo Warp's primitives at margin 0.
-__device__ __noinline__ int collide(World& s, int pr, bool write, int base, int* unsup) {
+// up to two contacts of one candidate pair (slot, distance, point, frame rows), kept in registers until the warp's
+// prefix sum gives their contact indices
+struct Hit {
+  int n, slot[2];
+  float dist[2], pos[2][3], fr[2][9];
+};
+
+// Narrow phase of candidate pair pr: its contacts (0..2, dist < 0) into h (h.n counted up from 0). MuJoCo Warp's
+// primitives at margin 0.
+__device__ __forceinline__ void collide(World& s, int pr, Hit& h, int* unsup) {
   const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
   const int t1 = ldi(g1_geom_type + g1), t2 = ldi(g1_geom_type + g2);
   float p1[3], p2[3];
   for (int k = 0; k < 3; k++) { p1[k] = s.u.col.gx[g1][k]; p2[k] = s.u.col.gx[g2][k]; }
   const float r1 = ld(g1_geom_size + 3 * g1), r2 = ld(g1_geom_size + 3 * g2);
-  int n = 0;
   auto emit = [&](int slot, float dist, const float* pos, const float* fr) {
-    const int c = base + n;
-    n++;
-    if (!write || c >= MAXCON) return;
-    s.con_pair[c] = pr;
-    s.con_slot[c] = (unsigned char)slot;
-    s.con_dist[c] = dist;
-    for (int k = 0; k < 3; k++) s.con_pos[c][k] = pos[k];
-    for (int k = 0; k < 9; k++) s.con_fr[c][k] = fr[k];
+    if (h.n == 0) {
+      h.slot[0] = slot; h.dist[0] = dist;
+      for (int k = 0; k < 3; k++) h.pos[0][k] = pos[k];
+      for (int k = 0; k < 9; k++) h.fr[0][k] = fr[k];
+    } else {
+      h.slot[1] = slot; h.dist[1] = dist;
+      for (int k = 0; k < 3; k++) h.pos[1][k] = pos[k];
+      for (int k = 0; k < 9; k++) h.fr[1][k] = fr[k];
+    }
+    h.n++;
   };
   if (t1 == 0) {  // plane (the floor) against a sphere or a capsule
     float nrm[3];
@@ -765,13 +773,13 @@ __device__ __noinline__ int collide(World& s, int pr, bool write, int base, int*
     } else {
       *unsup |= UNSUPPORTED_PAIR;
     }
-    return n;
+    return;
   }
   if (t1 == 2 && t2 == 2) {  // sphere-sphere
     float dist, pos[3], nn[3], fr[9];
     sphere_sphere(p1, r1, p2, r2, &dist, pos, nn);
     if (dist < 0.f) { make_frame(nn, fr); emit(0, dist, pos, fr); }
-    return n;
+    return;
   }
   if (t1 == 2 && t2 == 3) {  // sphere-capsule: the regularised closest point of the segment
     const float hl = ld(g1_geom_size + 3 * g2 + 1);
@@ -784,7 +792,7 @@ __device__ __noinline__ int collide(World& s, int pr, bool write, int base, int*
     float dist, pos[3], nn[3], fr[9];
     sphere_sphere(p1, r1, pt, r2, &dist, pos, nn);
     if (dist < 0.f) { make_frame(nn, fr); emit(0, dist, pos, fr); }
-    return n;
+    return;
   }
   if (t1 == 3 && t2 == 3) {  // capsule-capsule: closest points of the segments (clamp cascade)
     const float hl1 = ld(g1_geom_size + 3 * g1 + 1), hl2 = ld(g1_geom_size + 3 * g2 + 1);
@@ -830,14 +838,14 @@ __device__ __noinline__ int collide(World& s, int pr, bool write, int base, int*
         }
       }
     }
-    return n;
+    return;
   }
   *unsup |= UNSUPPORTED_PAIR;
-  return n;
+  return;
 }
 
-// geom poses, broad phase (ballot-compacted candidates in pair order), narrow phase in two passes (count, prefix
-// sum over the warp, write): contacts in pair order, deterministic
+// geom poses, broad phase (ballot-compacted candidates in pair order), narrow phase (each lane's contacts held in
+// registers, a prefix sum over the warp, then written): contacts in pair order, deterministic
 __device__ __noinline__ void collision(World& s, int lane) {
   for (int g = lane; g < NG; g += 32) {
     const int b = ldi(g1_geom_body + g);
@@ -864,14 +872,26 @@ __device__ __noinline__ void collision(World& s, int lane) {
   for (int c0 = 0; c0 < ncand; c0 += 32) {
     const int ci = c0 + lane;
     const int pr = ci < ncand ? s.u.col.cand[ci] : -1;
-    int cnt = pr >= 0 ? collide(s, pr, false, 0, &unsup) : 0;
-    int incl = cnt;
+    Hit h;
+    h.n = 0;
+    if (pr >= 0) collide(s, pr, h, &unsup);
+    int incl = h.n;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int t = __shfl_up_sync(FULL, incl, o);
       if (lane >= o) incl += t;
     }
-    if (cnt > 0) collide(s, pr, true, total + incl - cnt, &unsup);
+    const int base = total + incl - h.n;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+      const int c = base + e;
+      if (e >= h.n || c >= MAXCON) continue;
+      s.con_pair[c] = pr;
+      s.con_slot[c] = (unsigned char)h.slot[e];
+      s.con_dist[c] = h.dist[e];
+      for (int k = 0; k < 3; k++) s.con_pos[c][k] = h.pos[e][k];
+      for (int k = 0; k < 9; k++) s.con_fr[c][k] = h.fr[e][k];
+    }
     total += __shfl_sync(FULL, incl, 31);
   }
   unsup = (int)__reduce_or_sync(FULL, (unsigned)unsup);

@@ -68,3 +68,40 @@ def test_two_rank_reduction_equals_one_process(tmp_path):
     assert vec[2] == ref[2] == T * B and vec[3] == 0
     assert vec[0] == pytest.approx(ref[0], rel=1e-5)
     assert vec[1] == pytest.approx(ref[1], rel=1e-5)
+
+
+def _rank_fails(rank, world, port, out):
+    """Rank 1 fails after joining (an exception on the host, between steps: none of its collectives in flight); rank 0
+    records what its next collective does."""
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        raise SystemExit(3)
+    try:
+        rollout.reduce_stats(torch.tensor(1.0), torch.ones(4, 29))
+        msg = "completed"
+    except Exception as e:  # the failure reaches the surviving rank as an error, not a hang
+        msg = "error: " + type(e).__name__
+    with open(out, "w") as f:
+        f.write(msg)
+
+
+def test_a_failed_rank_ends_the_other_ranks_reduction_with_an_error(tmp_path):
+    import multiprocessing
+    ctx = multiprocessing.get_context("spawn")
+    out = str(tmp_path / "rank0.txt")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_fails, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    assert procs[1].exitcode == 3
+    with open(out) as f:
+        assert f.read().startswith("error"), "the surviving rank's reduction completed without its peer"

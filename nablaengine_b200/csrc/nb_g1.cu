@@ -204,15 +204,18 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
 
 // The step Jacobian (B, 71, 99): row r = the VJP of output r (qpos' in qpos form 0..35, qvel' 36..70) in the
 // tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). A block holds JR rows of one world (one warp each, JBLK
-// blocks per world) and one copy of what the rows share per record, kept by a helper warp: it loads the record and
-// both factors, then replays the record while the rows run their integrator step and solves. The rows keep only
+// blocks per world) and what the rows share per record (the record's state, both factors and the replay), prepared
+// by a helper warp one record ahead in a second buffer while the rows work on the current one. The rows keep only
 // their cotangents' state (AdjRow, 12.3 KB), so twelve fit an SM. info (B,): the replay flags ORed over the rows
 // (zeroed by the launcher).
 constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = 12, JBLK = (JROWS + JR - 1) / JR;
-struct JacBlock {
+struct JacRecord {  // what the rows share per record
   AWorld s;
   float LH[NTRI], dinvH[NV + 1];
   AdjShared W;
+};
+struct JacBlock {
+  JacRecord rec[2];  // the record the rows are on and the next one, which the helper prepares meanwhile
   AdjRow r[JR];
 };
 constexpr size_t JSMEM = sizeof(JacBlock);
@@ -231,22 +234,33 @@ __global__ void __launch_bounds__((JR + 1) * 32) k_jacobian(int nw, int nsub, co
   const size_t w64 = (size_t)w;
   const float* tw = tape + w64 * nsub * REC_WORDS;
   AdjRow& A = jb.r[helper ? 0 : warp];
+  // the helper loads and replays record k into rec[k & 1]: the last record before the loop, then record k - 1
+  // while the rows work on record k (one barrier per record)
+  auto prepare = [&](int k) {
+    JacRecord& R = jb.rec[k & 1];
+    adj_record(R.s, R.W, tw + (size_t)k * REC_WORDS, R.LH, R.dinvH, lane);
+    adj_replay(R.s, R.W, lane);
+  };
   if (helper) {
-    if (lane == 0) jb.s.fric = fric[w];
-    if (lane < 3) jb.s.com[lane] = com[w64 * 3 + lane];
-    for (int i = lane; i < NU; i += 32) jb.W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
+    for (int q = 0; q < 2; q++) {
+      if (lane == 0) jb.rec[q].s.fric = fric[w];
+      if (lane < 3) jb.rec[q].s.com[lane] = com[w64 * 3 + lane];
+      for (int i = lane; i < NU; i += 32) jb.rec[q].W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
+    }
+    prepare(nsub - 1);
   }
   if (active) adj_row_init(A, tw, nsub, nullptr, nullptr, row, normal, lane);
   int flags = 0;
   for (int k = nsub - 1; k >= 0; k--) {
-    const float* rec = tw + (size_t)k * REC_WORDS;
-    __syncthreads();  // every row is done with the previous record's shared data
-    if (helper) adj_record(jb.s, jb.W, rec, jb.LH, jb.dinvH, lane);
-    __syncthreads();
-    if (helper) adj_replay(jb.s, jb.W, lane);
-    else if (active) adj_row_solve(jb.s, jb.W, A, rec, jb.LH, jb.dinvH, lane);
-    __syncthreads();
-    if (active) flags |= adj_row_rest(jb.s, jb.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
+    __syncthreads();  // record k is ready, and every row is done with record k + 1's buffer (the helper's next)
+    if (helper) {
+      if (k > 0) prepare(k - 1);
+    } else if (active) {
+      JacRecord& R = jb.rec[k & 1];
+      const float* rec = tw + (size_t)k * REC_WORDS;
+      adj_row_solve(R.s, R.W, A, rec, R.LH, R.dinvH, lane);
+      flags |= adj_row_rest(R.s, R.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
+    }
   }
   if (!active) return;
   float* out = jac + (w64 * JROWS + row) * JCOLS;

@@ -105,3 +105,26 @@ def test_jacobian_argument_errors(golden):
         torch_ffi.jacobian(tape, t[4], t[5], clamp_kv=2)
     J, info = torch_ffi.jacobian(tape[:0], t[4][:0], t[5][:0])
     assert J.shape == (0, 71, 99)
+
+
+@pytest.mark.parametrize("substeps", [1, 3])
+def test_jacobian_rows_equal_backward_ragged_batch(substeps):
+    """A batch of 37 worlds (no multiple of anything in the launch) with an odd number of records: every row of the
+    Jacobian equals backward's VJP of its unit cotangent bit for bit in the qvel and ctrl columns."""
+    torch = _cuda()
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("vjp", B=37)
+    s["qpos"][:9, 2] -= 0.08
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda()
+         for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    tape = torch_ffi.forward(*t, substeps=substeps, tape=True)[4]
+    J = torch_ffi.jacobian(tape, t[4], t[5], substeps=substeps)[0]
+    B = J.shape[0]
+    for r in range(71):
+        cq, cv = torch.zeros(B, 36, device="cuda"), torch.zeros(B, 35, device="cuda")
+        if r < 36:
+            cq[:, r] = 1.0
+        else:
+            cv[:, r - 36] = 1.0
+        gq, gv, gu, _ = torch_ffi.backward(tape, t[4], t[5], cq, cv, substeps=substeps, clamp_kv=1, normal=0)
+        assert torch.equal(J[:, r, 35:70], gv) and torch.equal(J[:, r, 70:], gu), r

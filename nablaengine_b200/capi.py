@@ -13,7 +13,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "nabla_g1.h"
 EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward", "nb_g1_forward_stats",
            "nb_g1_adjoint", "nb_g1_jacobian", "nb_g1_kinematics", "nb_g1_kinematics_vjp", "nb_g1_diag_count",
            "nb_g1_diag_forward", "nb_g1_diag_backward")
-ABI_VERSION = 2
+ABI_VERSION = 3
 NQ, NV, NU, NBODY, MAXCON, NEFC = 36, 35, 29, 31, 64, 192
 
 _LOCK = threading.Lock()

@@ -27,7 +27,7 @@ constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // transitions in step, each world's Newton iterations on their own): 3.81 ms against 3.84 at the same code, and
 // it needs the Newton loop to fit the instruction cache (~40 KB measured for 10 warps on separate paths).
 constexpr int TAPE_WORDS = REC_WORDS;
-constexpr long long ABI_VERSION = 2;  // 2: the tape's L_Q in tree-block order
+constexpr long long ABI_VERSION = 3;  // 2: the tape's L_Q in tree-block order; 3: only its pattern's entries
 
 __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __restrict__ qpos,
                                                       const float* __restrict__ qvel, const float* __restrict__ warm,
@@ -243,10 +243,12 @@ __global__ void __launch_bounds__((JR + 1) * 32) k_jacobian(int nw, int nsub, co
   };
   if (helper) {
     for (int q = 0; q < 2; q++) {
+      for (int e = lane; e < NTRI; e += 32) jb.rec[q].s.L[e] = 0.f;  // L_Q's entries outside its pattern
       if (lane == 0) jb.rec[q].s.fric = fric[w];
       if (lane < 3) jb.rec[q].s.com[lane] = com[w64 * 3 + lane];
       for (int i = lane; i < NU; i += 32) jb.rec[q].W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
     }
+    __syncwarp();
     prepare(nsub - 1);
   }
   if (active) adj_row_init(A, tw, nsub, nullptr, nullptr, row, normal, lane);

@@ -910,6 +910,22 @@ __device__ __forceinline__ void copy_factor(float* dst, const float* src, int la
     if (lane + 32 * q < NTRI) dst[lane + 32 * q] = v[q];
 }
 
+// dst[0..NTRI) <- the tape's tree-block factor: its NTB pattern entries from src, zeros elsewhere (written here when
+// `zero`, else already there: nothing else writes outside the pattern); each lane's loads issued before its stores
+__device__ __forceinline__ void copy_factor_tb(float* dst, const float* src, int lane, bool zero) {
+  constexpr int R = (NTB + 31) / 32;
+  float v[R];
+#pragma unroll
+  for (int q = 0; q < R; q++) v[q] = lane + 32 * q < NTB ? __ldg(src + lane + 32 * q) : 0.f;
+  if (zero) {
+    for (int e = lane; e < NTRI; e += 32) dst[e] = 0.f;
+    __syncwarp();
+  }
+#pragma unroll
+  for (int q = 0; q < R; q++)
+    if (lane + 32 * q < NTB) dst[g_tb_index.e[lane + 32 * q]] = v[q];
+}
+
 // One substep of the adjoint from its tape record rec. What every cotangent of the record shares: adj_record (the
 // record's state into s and W; with LH given also both factors: L_Q into s.L / s.dinv, L_H into LH / dinvH) and
 // adj_replay (the replayed poses, velocities and accelerations, the motions of a* and v, the geom poses and contact
@@ -941,7 +957,7 @@ __device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, f
     s.con_slot[c] = (unsigned char)(e >> 9);
   }
   if (LH) {
-    copy_factor(s.L, rec + T_LQ, lane);
+    copy_factor_tb(s.L, rec + T_LQ, lane, false);  // (s.L holds L_Q only: zeroed once)
     copy_factor(LH, rec + T_LH, lane);
     for (int i = lane; i < NV; i += 32) { s.dinv[i] = rec[T_DINVQ + i]; dinvH[i] = rec[T_DINVH + i]; }
   }
@@ -1037,7 +1053,7 @@ __device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, con
   PROF(A, 0);
   // y = (M + h kv)^-1 abar_adv with L_Q; abar* = abar_adv - h kv y
   if (!LH) {
-    copy_factor(s.L, rec + T_LQ, lane);
+    copy_factor_tb(s.L, rec + T_LQ, lane, true);
     for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVQ + i];
   }
   for (int i = lane; i < NV; i += 32) A.lam[i] = A.y[i];

@@ -37,14 +37,16 @@ enum : int { UNSUPPORTED_PAIR = 1, CONTACT_OVERFLOW = 4, ROW_OVERFLOW = 16 };
 
 // The forward tape: one record of REC_WORDS float32 words per world and substep (record w * nsub + k), what the
 // adjoint reads: the substep's input state, the Newton solution a*, a_adv = (M + h kv)^-1 M a*, the Cholesky factors
-// of the Newton Hessian at the final zones (L_H, dof order) and of M + h kv (L_Q, tree-block order: tb_factor) with
-// their inverse diagonals, the contact
+// of the Newton Hessian at the final zones (L_H, dof order) and of M + h kv (L_Q, tree-block order: tb_factor, only
+// the entries of its pattern) with their inverse diagonals, the contact
 // table (pair | slot << 9, two 16-bit entries per word, contact order), the rows' final zone bits, the actuator
 // clamp mask (dof bits) and a header
 constexpr int T_QPOS = 0, T_QVEL = 36, T_ASTAR = 71, T_AADV = 106, T_DINVH = 141, T_DINVQ = 176, T_LH = 211;
-constexpr int T_LQ = T_LH + NTRI, T_CON = T_LQ + NTRI, T_ZONE = T_CON + MAXCON / 2, T_CLAMP = T_ZONE + NEFC / 32;
+constexpr int NTB_TAPE = 341;  // the tree-block factor's pattern (NTB, checked below)
+constexpr int T_LQ = T_LH + NTRI, T_CON = T_LQ + NTB_TAPE, T_ZONE = T_CON + MAXCON / 2;
+constexpr int T_CLAMP = T_ZONE + NEFC / 32;
 constexpr int T_HDR = T_CLAMP + 2, T_FLAGS = T_HDR + 1, REC_WORDS = ((T_FLAGS + 1 + 3) / 4) * 4;
-static_assert(T_LQ == 841 && REC_WORDS == 1516, "tape layout");
+static_assert(T_LQ == 841 && REC_WORDS == 1224, "tape layout");
 // TAPE_SINGULAR: a pivot of the recorded Hessian factor was clamped (at 1e-30: not positive definite in float32)
 enum : unsigned { TAPE_REFACT = 1u << 8, TAPE_NONCONV = 1u << 9, TAPE_SINGULAR = 1u << 12 };
 enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
@@ -469,6 +471,35 @@ __host__ __device__ constexpr int tb_dof(int p) { return p < 12 ? p + 6 : (p < 2
 __host__ __device__ constexpr int tb_pos(int d) { return d < 6 ? d + 29 : (d < 18 ? d - 6 : (d < 21 ? d + 8 : d - 9)); }
 static_assert(tb_pos(tb_dof(0)) == 0 && tb_pos(tb_dof(25)) == 25 && tb_pos(tb_dof(26)) == 26 &&
               tb_pos(tb_dof(34)) == 34 && tb_dof(12) == 21 && tb_dof(26) == 18 && tb_dof(29) == 0, "tree-block order");
+
+// The factor's pattern in tree-block order: entry (p, q), p >= q, is structurally nonzero when p is in q's chain or
+// in one of its ancestor chains (legs: the root; arms: the waist and the root; the waist: the root). The tape stores
+// only these NTB entries of L_Q (packed-triangle order).
+__host__ __device__ constexpr int tb_chain(int p) {  // left leg, right leg, left arm, right arm, waist, root
+  return p < 6 ? 0 : (p < 12 ? 1 : (p < 19 ? 2 : (p < 26 ? 3 : (p < 29 ? 4 : 5))));
+}
+__host__ __device__ constexpr bool tb_nonzero(int p, int q) {
+  const int a = tb_chain(p), b = tb_chain(q);
+  return a == b || a == 5 || (a == 4 && (b == 2 || b == 3));
+}
+constexpr int tb_count() {
+  int n = 0;
+  for (int p = 0; p < NV; p++)
+    for (int q = 0; q <= p; q++) n += tb_nonzero(p, q);
+  return n;
+}
+constexpr int NTB = tb_count();
+static_assert(NTB == 341 && NTB == NTB_TAPE, "the tree-block pattern of the G1");
+struct TbIndex { unsigned short e[NTB]; };
+constexpr TbIndex make_tb_index() {
+  TbIndex t{};
+  int n = 0;
+  for (int p = 0; p < NV; p++)
+    for (int q = 0; q <= p; q++)
+      if (tb_nonzero(p, q)) t.e[n++] = (unsigned short)TRI(p, q);
+  return t;
+}
+static __device__ const TbIndex g_tb_index = make_tb_index();
 
 // right-looking elimination of N columns (positions cp0 .. cp0 + N - 1) on register rows: lane gb + li holds the
 // row at position rowpos over those columns (the block's own rows first: lane gb + k is column k's row)
@@ -1606,7 +1637,7 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
   tb_factor(s.M, true, s.L, s.dinv, lane);
   chol_solve<true>(s.L, s.dinv, s.tmp, lane);
   if (rec) {
-    tape_put(rec + T_LQ, s.L, NTRI, lane);
+    for (int e = lane; e < NTB; e += 32) __stcs(rec + T_LQ + e, s.L[g_tb_index.e[e]]);
     tape_put(rec + T_DINVQ, s.dinv, NV, lane);
     tape_put(rec + T_AADV, s.tmp, NV, lane);
   }

@@ -16,8 +16,13 @@ pytestmark = pytest.mark.gpu
 T_QPOS, T_QVEL, T_ASTAR, T_AADV, T_DINVH, T_DINVQ, T_LH = 0, 36, 71, 106, 141, 176, 211
 NQ, NV, NU, NTRI = 36, 35, 29, 630
 T_LQ = T_LH + NTRI
-# L_Q is stored in tree-block order (legs, arms, waist, root: nb_g1_step.cuh tb_dof): position p holds dof TB_DOF[p]
+# L_Q is stored in tree-block order (legs, arms, waist, root: nb_g1_step.cuh tb_dof): position p holds dof TB_DOF[p],
+# and only the entries of its pattern (p in q's chain or an ancestor chain of it), in packed-triangle order
 TB_DOF = list(range(6, 18)) + list(range(21, 35)) + [18, 19, 20] + list(range(6))
+_CHAIN = [0] * 6 + [1] * 6 + [2] * 7 + [3] * 7 + [4] * 3 + [5] * 6
+TB_PATTERN = [(p, q) for p in range(35) for q in range(p + 1)
+              if _CHAIN[p] == _CHAIN[q] or _CHAIN[p] == 5 or (_CHAIN[p] == 4 and _CHAIN[q] in (2, 3))]
+NTB = len(TB_PATTERN)
 H_STEP = np.float32(0.005)
 KEYS = ("qpos", "qvel", "warm", "ctrl", "friction", "com")
 SENTINEL = np.uint32(0xA5A5A5A5)
@@ -108,7 +113,9 @@ def test_factor_of_m_plus_h_kv_matches_the_oracle_mass_matrix(taped):
     for k in range(tp.shape[1]):
         _, Q, _, _ = _oracle_matrices(s, tp, k)
         Q = Q[:, TB_DOF][:, :, TB_DOF]
-        L = _unpack(tp[:, k, T_LQ:T_LQ + NTRI].astype(np.float64))
+        L = np.zeros((tp.shape[0], NV, NV))
+        pi, qi = np.array(TB_PATTERN).T
+        L[:, pi, qi] = tp[:, k, T_LQ:T_LQ + NTB].astype(np.float64)
         e = np.linalg.norm(L @ L.transpose(0, 2, 1) - Q, axis=(1, 2)) / np.linalg.norm(Q, axis=(1, 2))
         assert np.median(e) < 2e-6 and e.max() < 2e-5, (k, np.median(e), e.max())
         d = np.diagonal(L, axis1=1, axis2=2)

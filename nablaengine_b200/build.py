@@ -34,12 +34,17 @@ def stale():
     return any(p.stat().st_mtime > t for p in DEPS)
 
 
-def build(force=False, verbose=False, extra=()):
-    """Compile the library when it is missing or older than its sources; returns its path."""
-    if not force and not stale():
-        return LIB
+PROFILE_LIB = LIBDIR / "libnabla_g1_prof.so"
+
+
+def build(force=False, verbose=False, extra=(), out=None):
+    """Compile the library when it is missing or older than its sources; returns its path. `out` and `extra`: another
+    output path and extra nvcc flags (the phase-profile build: -DNB_PROFILE into PROFILE_LIB)."""
+    lib = Path(out) if out else LIB
+    if not force and lib.exists() and not any(p.stat().st_mtime > lib.stat().st_mtime for p in DEPS):
+        return lib
     LIBDIR.mkdir(exist_ok=True)
-    tmp = LIB.with_suffix(f".tmp{os.getpid()}.so")
+    tmp = lib.with_suffix(f".tmp{os.getpid()}.so")
     cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-o", str(tmp), *map(str, SOURCES)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
@@ -49,8 +54,8 @@ def build(force=False, verbose=False, extra=()):
         raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
     if verbose:
         print(r.stderr, flush=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":

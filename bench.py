@@ -358,17 +358,17 @@ def main():
                      "hbm_peak_gbs": peaks.get("hbm_gbs")},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "world-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": a.steps * (2 if torch_ffi._DIAG_ON[0] else 1),  # k_forward (+ its diagnostics kernel)
+        "gpu_launches": a.steps * (3 if torch_ffi._DIAG_ON[0] else 2),  # k_order, k_forward (+ diagnostics)
         "fwd_grad": {"metric": "world-steps/sec fwd+grad at B=4096/GPU (BASELINE configuration 3: loss sum(qvel'^2), "
                                "VJP w.r.t. qpos, qvel, ctrl, exact mode clamp_kv=1 normal=0, torch autograd)",
                      "value": world * fg["B"] / (fg_ms[0].item() / 1e3), "unit": "world-steps/s",
                      "ms_per_step": fg_ms[0].item(), "ms_forward_with_tape": fg_ms[1].item(),
                      "ms_adjoint": fg_ms[2].item(), "worlds_per_gpu": fg["B"],
-                     "gpu_launches_per_step": 2, "l2": "flushed between timed steps"},
+                     "gpu_launches_per_step": 3, "l2": "flushed between timed steps"},
         "jacobian": {"metric": "full 71 x 99 step Jacobian (forward with tape + Jacobian kernel, exact mode), us per "
                                "world at B=4096/GPU (BASELINE configuration 4)",
                      "value": fg_ms[3].item() * 1e3 / jac["B"], "unit": "us/world", "higher_is_better": False,
-                     "ms_per_step": fg_ms[3].item(), "worlds_per_gpu": jac["B"], "gpu_launches_per_step": 2,
+                     "ms_per_step": fg_ms[3].item(), "worlds_per_gpu": jac["B"], "gpu_launches_per_step": 3,
                      "l2": "flushed between timed steps"},
         "kernel_ms": {"median": statistics.median(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
     }

@@ -27,8 +27,10 @@ typedef struct CUstream_st* cudaStream_t;
  * which the bindings check against their own constants before the first call. */
 void nb_g1_sizes(long long out[8]);
 
-/* Scratch bytes nb_g1_forward needs for nw worlds (16-byte aligned, caller-allocated, e.g. a torch uint8 tensor or
- * XLA's scratch allocator). Replaces `long long <pfx>_work_bytes(int nw)` (src/nablaengine/jax_ffi.py:265). */
+/* Scratch bytes nb_g1_forward takes for nw worlds (16-byte aligned, caller-allocated, e.g. a torch uint8 tensor or
+ * XLA's scratch allocator): the order in which the kernel's blocks take the worlds, 4 bytes per world rounded up to
+ * 16; -1 for nw < 0. Replaces `long long <pfx>_work_bytes(int nw)` (src/nablaengine/jax_ffi.py:265), whose work
+ * memory holds the split forward's hand-over records and its row-count ordering (g1_engine/host.py:229-301). */
 long long nb_g1_work_bytes(int nw);
 
 /* Per-device preparation: must run once on each device before its first step and before any stream capture (it
@@ -44,7 +46,10 @@ int nb_g1_upload(const float* consts, cudaStream_t stream);
  * pos[3], normal[3]), pair -1 past the count. tape (B, nsub, tape words) may be NULL: else the per-substep records
  * nb_g1_adjoint reads (the substep's input state, a*, a_adv, the Cholesky factors of the Newton Hessian and of
  * M + h kv, the contact table, the constraint zones, the actuator clamp masks, flags); the outputs are bitwise the
- * same with and without it. work: nb_g1_work_bytes(nw) bytes or NULL when that is 0. nw == 0 is a no-op.
+ * same with and without it. work: nb_g1_work_bytes(nw) bytes, overwritten, or NULL: with it the worlds are first
+ * sorted by root height (lowest first, a small kernel before the step) so that worlds of similar cost share a
+ * block; without it they run in index order, slower; the outputs are bitwise the same either way. nw == 0 is a
+ * no-op.
  * Replaces `int <pfx>_forward(cudaStream_t, int nw, ...)` (src/nablaengine/jax_ffi.py:266-279). */
 int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
                   const float* ctrl, const float* friction, const float* com, int iterations, int nsub, float* qpos_out,

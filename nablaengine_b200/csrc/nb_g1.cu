@@ -36,14 +36,15 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
                                                       float* __restrict__ oq, float* __restrict__ ov,
                                                       float* __restrict__ ow, int* __restrict__ info,
                                                       float* __restrict__ ocon, int* __restrict__ stats,
-                                                      float* __restrict__ tape) {
+                                                      float* __restrict__ tape, const int* __restrict__ order) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w = blockIdx.x * WPB + warp;
+  const int slot = blockIdx.x * WPB + warp;  // the warp's place in the world order (k_order), or its world index
 #if !NB_LOCKSTEP
-  if (w >= nw) return;  // whole warps leave; the block has no block-wide barrier
+  if (slot >= nw) return;  // whole warps leave; the block has no block-wide barrier
 #endif
-  const bool active = w < nw;  // (lockstep: inactive warps stay for the barriers)
+  const bool active = slot < nw;  // (lockstep: inactive warps stay for the barriers)
+  const int w = active ? (order ? __ldg(order + slot) : slot) : 0;
   World& s = reinterpret_cast<World*>(smem)[warp];
   const size_t w64 = (size_t)(active ? w : 0);
   for (int i = lane; i < NQ; i += 32) s.qpos[i] = qpos[w64 * NQ + i];
@@ -96,6 +97,46 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 }
 
 constexpr size_t SMEM = sizeof(World) * WPB;
+
+// ---- the world order ----------------------------------------------------------------------------------------------
+// A block's ten worlds iterate in lockstep, so the block takes as long as its slowest world, and which worlds share a
+// block decides how long the others wait. k_order sorts the worlds by the root height of their input state, lowest
+// first, into the order k_forward's blocks take them: a lower root puts more geoms on the floor (more contacts and
+// constraint rows, more Newton iterations: the step's iteration count correlates -0.71 with the root height on
+// seeded standing states), so a block gets worlds of similar cost and the costliest blocks start first. The
+// reference orders its Newton kernel's worlds by constraint-row count for the same reason (g1_engine/host.py:
+// 229-298, from its split forward's first kernel); the fused step has no such pre-pass, so the key is an input.
+// Each block sorts ORD_CHUNK worlds on its own: a bitonic sort of (key, index) pairs in shared memory, the index in
+// the low word making the keys distinct, so the order is deterministic. The outputs do not depend on it (a world's
+// arithmetic is the same in any warp of any block).
+constexpr int ORD_CHUNK = 4096, ORD_THREADS = 1024;
+__global__ void __launch_bounds__(ORD_THREADS) k_order(int nw, const float* __restrict__ qpos,
+                                                       int* __restrict__ order) {
+  __shared__ unsigned long long key[ORD_CHUNK];
+  const int base = blockIdx.x * ORD_CHUNK, n = min(ORD_CHUNK, nw - base);
+  int np = 2;
+  while (np < n) np <<= 1;  // the sorted span: n rounded up to a power of two, padded with the largest key
+  for (int i = threadIdx.x; i < np; i += ORD_THREADS) {
+    unsigned long long k = ~0ull;
+    if (i < n) {
+      unsigned u = __float_as_uint(__ldg(qpos + (size_t)(base + i) * NQ + 2));
+      u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // the float order as the unsigned order
+      k = ((unsigned long long)u << 32) | (unsigned)(base + i);
+    }
+    key[i] = k;
+  }
+  __syncthreads();
+  for (int k = 2; k <= np; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int t = threadIdx.x; t < np / 2; t += ORD_THREADS) {
+        const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));  // the pair (i, i + j) of compare-exchange t
+        const unsigned long long a = key[i], b = key[i + j];
+        if ((a > b) == ((i & k) == 0)) { key[i] = b; key[i + j] = a; }
+      }
+      __syncthreads();
+    }
+  for (int i = threadIdx.x; i < n; i += ORD_THREADS) order[base + i] = (int)(unsigned)key[i];
+}
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
 // worlds per block of k_adjoint: 10 x 21.9 KB, one block per SM. The worlds meet at a block barrier before every
@@ -377,7 +418,7 @@ void nb_g1_sizes(long long out[8]) {
   for (int i = 0; i < 8; i++) out[i] = v[i];
 }
 
-long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : 0; }
+long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : ((long long)nw * (long long)sizeof(int) + 15) / 16 * 16; }
 
 int nb_g1_upload(const float* consts, cudaStream_t stream) {
   (void)consts;
@@ -463,7 +504,7 @@ int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, cons
 static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
                           const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
                           float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape,
-                          int* stats) {
+                          int* stats, int* order) {
   if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return (int)cudaErrorInvalidValue;
   if (nw == 0) return 0;
   if (!qpos || !qvel || !warm || !ctrl || !friction || !com || !qpos_out || !qvel_out || !warm_out || !info)
@@ -475,17 +516,21 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
 #else
   const size_t smem = SMEM;
 #endif
+  if (order) {
+    k_order<<<(nw + ORD_CHUNK - 1) / ORD_CHUNK, ORD_THREADS, 0, stream>>>(nw, qpos, order);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+  }
   k_forward<<<blocks, WPB * 32, smem, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
-                                                qvel_out, warm_out, info, ocon, stats, tape);
+                                                qvel_out, warm_out, info, ocon, stats, tape, order);
   return (int)cudaGetLastError();
 }
 
 int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
                   const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
                   float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work) {
-  (void)work;
   return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
-                        warm_out, info, ocon, tape, nullptr);
+                        warm_out, info, ocon, tape, nullptr, static_cast<int*>(work));
 }
 
 int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
@@ -493,7 +538,7 @@ int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const fl
                         float* qpos_out, float* qvel_out, float* warm_out, int* info, int* stats) {
   if (!stats) return (int)cudaErrorInvalidValue;
   return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
-                        warm_out, info, nullptr, nullptr, stats);
+                        warm_out, info, nullptr, nullptr, stats, nullptr);
 }
 
 #ifdef NB_PROFILE

@@ -31,6 +31,7 @@ def _load():
     lib.nb_g1_adjoint.argtypes = [vp, i32, i32] + [vp] * 10 + [ctypes.c_float, i32, i32]
     lib.nb_g1_upload.argtypes = [vp, vp]
     lib.nb_g1_sizes.argtypes = [vp]
+    lib.nb_g1_work_bytes.argtypes, lib.nb_g1_work_bytes.restype = [i32], ctypes.c_longlong
     lib.nb_g1_profile_read.argtypes = [vp, i32]
     return lib
 
@@ -62,7 +63,8 @@ def run(worlds=4096):
         torch.cuda.synchronize()
         _read(lib)
         taped = cfg == "vjp"  # (the forward configuration runs without a tape, as the benchmark's forward)
-        if lib.nb_g1_forward(st, B, *map(p, t), 10, 4, *map(p, out), None, p(tape) if taped else None, None):
+        work = torch.empty((lib.nb_g1_work_bytes(B),), dtype=torch.uint8, device="cuda")  # the world order
+        if lib.nb_g1_forward(st, B, *map(p, t), 10, 4, *map(p, out), None, p(tape) if taped else None, p(work)):
             raise RuntimeError("nb_g1_forward failed")
         torch.cuda.synchronize()
         v = _read(lib)

@@ -19,7 +19,10 @@ def test_library_exports_every_declared_symbol():
 def test_sizes_and_work_bytes():
     assert capi.sizes()[:6] == [36, 35, 29, 31, 64, 192]
     lib = capi.load()
-    assert lib.nb_g1_work_bytes(4096) >= 0
+    # the world order: one int32 per world, rounded up to 16 bytes
+    assert lib.nb_g1_work_bytes(4096) == 16384
+    assert lib.nb_g1_work_bytes(37) == 160
+    assert lib.nb_g1_work_bytes(0) == 0
     assert lib.nb_g1_work_bytes(-1) < 0
 
 

@@ -137,3 +137,43 @@ def test_cuda_graph_capture_replay():
     torch.cuda.synchronize()
     for a, b in zip(ref, out):
         assert torch.equal(a, b)
+
+
+def test_world_order_changes_no_output_bit():
+    """The work memory's world order (worlds sorted by root height, lowest first, each chunk of 4096 worlds on its
+    own) only schedules: outputs, info and tape equal those of the index-order launch (work NULL) bit for bit, on a
+    ragged batch of two chunks; the order itself is a permutation, the root heights non-decreasing within a chunk,
+    ties in index order."""
+    import ctypes
+    import torch
+    from nablaengine_b200 import capi, torch_ffi
+    torch_ffi.init(0)
+    lib = capi.load()
+    s = synthetic.config_states("vjp", B=5000)
+    B, nsub, rec = 5000, 4, int(capi.sizes()[6])
+    s["qpos"][7:19, 2] = s["qpos"][3, 2]  # equal keys: the index decides
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda()
+         for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nwork = lib.nb_g1_work_bytes(B)
+    assert nwork == 16 * ((4 * B + 15) // 16)
+    runs = []
+    for work in (torch.full((nwork,), 0xAB, dtype=torch.uint8, device="cuda"), None):
+        out = [torch.empty((B, 36), device="cuda"), torch.empty((B, 35), device="cuda"),
+               torch.empty((B, 35), device="cuda"), torch.empty((B, 4), dtype=torch.int32, device="cuda")]
+        tape = torch.empty((B, nsub * rec), device="cuda")
+        rc = lib.nb_g1_forward(st, B, *map(p, t), 10, nsub, *map(p, out), None, p(tape),
+                               None if work is None else p(work))
+        torch.cuda.synchronize()
+        assert rc == 0, rc
+        runs.append([x.cpu().numpy().view(np.uint32) for x in out + [tape]] + [work])
+    for a, b in zip(runs[0][:5], runs[1][:5]):
+        assert np.array_equal(a, b)
+    order = runs[0][5].cpu().numpy()[:4 * B].view(np.int32)
+    assert np.array_equal(np.sort(order), np.arange(B))
+    z = s["qpos"][:, 2].astype(np.float32)
+    for c0 in range(0, B, 4096):
+        o = order[c0:c0 + 4096]
+        idx = np.arange(c0, min(B, c0 + 4096))
+        assert np.array_equal(o, idx[np.lexsort((idx, z[idx]))])

@@ -115,6 +115,24 @@ int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const fl
                         const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
                         float* qpos_out, float* qvel_out, float* warm_out, int* info, int* stats);
 
+/* The largest nw nb_g1_forward_noalloc accepts. */
+#define NB_G1_NOALLOC_MAX_WORLDS 262144
+
+/* nb_g1_forward for callers that cannot allocate device memory: code that runs where cudaMalloc is not allowed or
+ * not wanted (inside a host callback, on a memory budget fixed in advance, or in a runtime whose allocator the caller
+ * does not own). Same arguments, outputs and errors as nb_g1_forward without the work pointer, and bitwise the same
+ * outputs. The world order that nb_g1_forward keeps in the caller's work memory lives here in one buffer inside the
+ * library: NB_G1_NOALLOC_MAX_WORLDS int32 (1 MiB) that every device which loads the library holds until the process
+ * exits. nw above NB_G1_NOALLOC_MAX_WORLDS returns cudaErrorInvalidValue (1) and launches nothing. The first call on
+ * a device (the current device) looks up that device's copy of the buffer (cudaGetSymbolAddress, once per device):
+ * make that first call before any stream capture. Every call on a device shares the buffer: the order of one call is
+ * overwritten by the next (nothing in it needs to start at zero), so calls whose kernels overlap on the GPU, on
+ * different streams, race on it and must be serialised by the caller. The call allocates and frees nothing.
+ * No counterpart in the reference's ABI. */
+int nb_g1_forward_noalloc(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                          const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                          float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape);
+
 #ifdef __cplusplus
 }
 #endif

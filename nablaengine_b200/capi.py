@@ -12,7 +12,7 @@ from . import build as _build
 HEADER = Path(__file__).resolve().parents[1] / "include" / "nabla_g1.h"
 EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward", "nb_g1_forward_stats",
            "nb_g1_adjoint", "nb_g1_jacobian", "nb_g1_kinematics", "nb_g1_kinematics_vjp", "nb_g1_diag_count",
-           "nb_g1_diag_forward", "nb_g1_diag_backward")
+           "nb_g1_diag_forward", "nb_g1_diag_backward", "nb_g1_forward_noalloc")
 ABI_VERSION = 3
 NQ, NV, NU, NBODY, MAXCON, NEFC = 36, 35, 29, 31, 64, 192
 
@@ -49,6 +49,8 @@ def load(path=None, build_if_missing=True):
         lib.nb_g1_forward.restype = i32
         lib.nb_g1_forward_stats.argtypes = [vp, i32] + [vp] * 6 + [i32, i32] + [vp] * 5
         lib.nb_g1_forward_stats.restype = i32
+        lib.nb_g1_forward_noalloc.argtypes = [vp, i32] + [vp] * 6 + [i32, i32] + [vp] * 6
+        lib.nb_g1_forward_noalloc.restype = i32
         lib.nb_g1_adjoint.argtypes = [vp, i32, i32] + [vp] * 10 + [ctypes.c_float, i32, i32]
         lib.nb_g1_adjoint.restype = i32
         lib.nb_g1_jacobian.argtypes = [vp, i32, i32] + [vp] * 6 + [ctypes.c_float, i32, i32]

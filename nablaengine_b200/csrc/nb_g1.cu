@@ -5,6 +5,7 @@
 #include "../../include/nabla_g1.h"
 #include <algorithm>
 #include <cstddef>
+#include <mutex>
 #include "nb_g1_step.cuh"
 #include "nb_g1_adjoint.cuh"
 #include "nb_g1_kin.cuh"
@@ -539,6 +540,48 @@ int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const fl
   if (!stats) return (int)cudaErrorInvalidValue;
   return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
                         warm_out, info, nullptr, nullptr, stats, nullptr);
+}
+
+}  // extern "C"
+
+// ---- the forward without caller memory (nb_g1_forward_noalloc) ---------------------------------------------------
+// For callers that cannot allocate device memory, the world order of nb_g1_forward's work memory lives in this
+// library's own buffer: a fixed array in device memory, one copy per device, loaded with the library. Host code must
+// not pass the array's name to a kernel (on the host it names a host-side shadow, not device memory): each device's
+// address comes from cudaGetSymbolAddress, looked up on the first call made with that device current and kept.
+static __device__ __align__(256) int g_noalloc_order[NB_G1_NOALLOC_MAX_WORLDS];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mutex;
+static int* g_noalloc_addr[NOALLOC_MAX_DEVICES] = {};
+
+static int noalloc_order_address(int** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return (int)cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_order);
+    if (e != cudaSuccess) return (int)e;
+    g_noalloc_addr[dev] = static_cast<int*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return 0;
+}
+
+extern "C" {
+
+int nb_g1_forward_noalloc(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                          const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                          float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape) {
+  if (nw > NB_G1_NOALLOC_MAX_WORLDS) return (int)cudaErrorInvalidValue;  // the buffer's capacity
+  if (nw <= 0) return nw < 0 ? (int)cudaErrorInvalidValue : 0;
+  int* order = nullptr;
+  const int rc = noalloc_order_address(&order);
+  if (rc) return rc;
+  return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
+                        warm_out, info, ocon, tape, nullptr, order);
 }
 
 #ifdef NB_PROFILE

@@ -81,7 +81,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--worlds", type=int, default=WORLDS_DEFAULT, help="worlds per GPU")
     ap.add_argument("--steps", type=int, default=T_DEFAULT, help="control steps T")
-    ap.add_argument("--repeats", type=int, default=2)
+    ap.add_argument("--repeats", type=int, default=5)
     a = ap.parse_args(argv)
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -105,7 +105,8 @@ def main(argv=None):
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1))
-    t = torch.tensor([max(times)], dtype=torch.float64, device=dev)
+    # per rank the median and the slowest of the repeats, then the maximum over ranks of each
+    t = torch.tensor([sorted(times)[len(times) // 2], max(times)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.destroy_process_group()
@@ -113,8 +114,9 @@ def main(argv=None):
         v = vec.cpu().tolist()
         print(json.dumps({"metric": "BPTT rollout world-steps/s (fwd+grad)", "n_gpus": world,
                           "worlds_per_gpu": a.worlds,
-                          "steps": a.steps, "ms_per_rollout": t.item(),
-                          "value": world * a.worlds * a.steps / (t.item() / 1e3), "unit": "world-steps/s",
+                          "steps": a.steps, "repeats": a.repeats, "ms_per_rollout": t[0].item(),
+                          "ms_per_rollout_slowest": t[1].item(),
+                          "value": world * a.worlds * a.steps / (t[0].item() / 1e3), "unit": "world-steps/s",
                           "loss": v[0], "ctrl_grad_norm": v[1] ** 0.5, "rows": v[2], "nonfinite_rows": v[3],
                           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9}), flush=True)
 

@@ -107,36 +107,35 @@ constexpr size_t SMEM = sizeof(World) * WPB;
 // seeded standing states), so a block gets worlds of similar cost and the costliest blocks start first. The
 // reference orders its Newton kernel's worlds by constraint-row count for the same reason (g1_engine/host.py:
 // 229-298, from its split forward's first kernel); the fused step has no such pre-pass, so the key is an input.
-// Each block sorts ORD_CHUNK worlds on its own: a bitonic sort of (key, index) pairs in shared memory, the index in
-// the low word making the keys distinct, so the order is deterministic. The outputs do not depend on it (a world's
-// arithmetic is the same in any warp of any block).
-constexpr int ORD_CHUNK = 4096, ORD_THREADS = 1024;
+// The key orders the worlds of each chunk of ORD_CHUNK (root height as an ordered unsigned, then the world index:
+// distinct keys, so the order is deterministic), and a world's place in its chunk is its rank there, the number of
+// the chunk's keys below its own: ORD_TPW threads count it over slices of the chunk's keys, which every block of the
+// chunk stages in shared memory, so the sort spreads over ORD_CHUNK / ORD_WPB blocks with one barrier (a bitonic
+// sort of the chunk in one block took 40 us at B = 4096, 1.3 % of the step). The outputs do not depend on the
+// order (a world's arithmetic is the same in any warp of any block).
+constexpr int ORD_CHUNK = 4096, ORD_TPW = 8, ORD_THREADS = 256, ORD_WPB = ORD_THREADS / ORD_TPW;
+constexpr int ORD_BLOCKS_PER_CHUNK = ORD_CHUNK / ORD_WPB;
+__device__ __forceinline__ unsigned long long order_key(const float* qpos, int w) {
+  unsigned u = __float_as_uint(__ldg(qpos + (size_t)w * NQ + 2));
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // the float order as the unsigned order
+  return ((unsigned long long)u << 32) | (unsigned)w;
+}
 __global__ void __launch_bounds__(ORD_THREADS) k_order(int nw, const float* __restrict__ qpos,
                                                        int* __restrict__ order) {
   __shared__ unsigned long long key[ORD_CHUNK];
-  const int base = blockIdx.x * ORD_CHUNK, n = min(ORD_CHUNK, nw - base);
-  int np = 2;
-  while (np < n) np <<= 1;  // the sorted span: n rounded up to a power of two, padded with the largest key
-  for (int i = threadIdx.x; i < np; i += ORD_THREADS) {
-    unsigned long long k = ~0ull;
-    if (i < n) {
-      unsigned u = __float_as_uint(__ldg(qpos + (size_t)(base + i) * NQ + 2));
-      u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // the float order as the unsigned order
-      k = ((unsigned long long)u << 32) | (unsigned)(base + i);
-    }
-    key[i] = k;
-  }
+  const int base = (blockIdx.x / ORD_BLOCKS_PER_CHUNK) * ORD_CHUNK, n = min(ORD_CHUNK, nw - base);
+  const int first = (blockIdx.x % ORD_BLOCKS_PER_CHUNK) * ORD_WPB;  // this block's worlds: chunk positions first..
+  if (first >= n) return;  // (the whole block)
+  for (int i = threadIdx.x; i < n; i += ORD_THREADS) key[i] = order_key(qpos, base + i);
   __syncthreads();
-  for (int k = 2; k <= np; k <<= 1)
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int t = threadIdx.x; t < np / 2; t += ORD_THREADS) {
-        const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));  // the pair (i, i + j) of compare-exchange t
-        const unsigned long long a = key[i], b = key[i + j];
-        if ((a > b) == ((i & k) == 0)) { key[i] = b; key[i + j] = a; }
-      }
-      __syncthreads();
-    }
-  for (int i = threadIdx.x; i < n; i += ORD_THREADS) order[base + i] = (int)(unsigned)key[i];
+  const int sub = threadIdx.x % ORD_TPW, i = first + threadIdx.x / ORD_TPW;  // i: this group's world
+  const unsigned long long mine = i < n ? key[i] : 0ull;
+  int rank = 0;
+#pragma unroll 4
+  for (int v = sub; v < n; v += ORD_TPW) rank += key[v] < mine;
+#pragma unroll
+  for (int o = ORD_TPW / 2; o > 0; o >>= 1) rank += __shfl_xor_sync(FULL, rank, o);  // the group's lanes
+  if (sub == 0 && i < n) order[base + rank] = base + i;
 }
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
@@ -518,7 +517,7 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
   const size_t smem = SMEM;
 #endif
   if (order) {
-    k_order<<<(nw + ORD_CHUNK - 1) / ORD_CHUNK, ORD_THREADS, 0, stream>>>(nw, qpos, order);
+    k_order<<<(nw + ORD_CHUNK - 1) / ORD_CHUNK * ORD_BLOCKS_PER_CHUNK, ORD_THREADS, 0, stream>>>(nw, qpos, order);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
   }

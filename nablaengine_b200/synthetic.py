@@ -14,7 +14,7 @@ import numpy as np
 
 MODEL = Path(__file__).resolve().parent / "model" / "g1_model.npz"
 NQ, NV, NU = 36, 35, 29
-# BASELINE.json configurations: (name, worlds per GPU, seed)
+# the benchmark configurations 1-5 (CPU reference, forward, VJP, Jacobian, rollout): worlds per GPU, seed
 CONFIGS = {
     "cpu_reference": dict(B=256, seed=0),
     "forward": dict(B=4096, seed=1),

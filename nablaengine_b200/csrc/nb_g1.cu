@@ -249,7 +249,10 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
 // by a helper warp one record ahead in a second buffer while the rows work on the current one. The rows keep only
 // their cotangents' state (AdjRow, 12.3 KB), so twelve fit an SM. info (B,): the replay flags ORed over the rows
 // (zeroed by the launcher).
-constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = 12, JBLK = (JROWS + JR - 1) / JR;
+#ifndef NB_JR
+#define NB_JR 12
+#endif
+constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = NB_JR, JBLK = (JROWS + JR - 1) / JR;
 struct JacRecord {  // what the rows share per record
   AWorld s;
   float LH[NTRI], dinvH[NV + 1];

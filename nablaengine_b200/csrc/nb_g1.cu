@@ -142,7 +142,10 @@ __global__ void __launch_bounds__(ORD_THREADS) k_order(int nw, const float* __re
 // worlds per block of k_adjoint: 10 x 21.9 KB, one block per SM. The worlds meet at a block barrier before every
 // substep, so the SM's warps run the same code together (one instruction stream; measured at B = 4096: 1.06 ms
 // against 1.14 ms with one world per block and no barrier)
-constexpr int AWPB = 10;
+#ifndef NB_AWPB
+#define NB_AWPB 10
+#endif
+constexpr int AWPB = NB_AWPB;
 struct AdjBlock { AWorld s; Adj a; };
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
 

@@ -19,7 +19,6 @@ the float64 oracle port stands in), rank 0 only, each step a bounded sample of t
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -91,33 +90,125 @@ class Clocks:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def traffic_per_world():
-    """DRAM bytes per world of one forward launch from the committed ncu summary (None if absent)."""
-    p = ROOT / "profiles" / "k_forward.md"
-    if not p.exists():
-        return None
-    m = re.search(r"dram_bytes_per_world:\s*([0-9.eE+-]+)", p.read_text())
-    return float(m.group(1)) if m else None
+# DRAM bytes (read + write) per world of one forward launch: ncu `dram__bytes_read.sum + dram__bytes_write.sum` of
+# k_forward on 1480 configuration-2 worlds with the world order (one wave; the capture command is in
+# profiles/k_forward.md), divided by the worlds; the inputs and outputs of the step, nothing re-read
+FORWARD_DRAM_BYTES_PER_WORLD = 847
 
 
-def cpu_baseline(seconds=12.0):
-    """The float64 oracle (all host threads) on BASELINE configuration 1 (256 seeded worlds), repeated ~12 s."""
+def cpu_baseline(seconds=10.0, corpus_seconds=6.0):
+    """The float64 oracle (all host threads) on BASELINE configuration 1 (256 seeded worlds, repeated ~10 s) and on
+    the reference's corpus mf_s0 (its first 1024 states, ~6 s), beside the reference's published MuJoCo C numbers on
+    the same corpus (MuJoCo C itself is not installed on the box)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     from nablaengine_b200 import synthetic
+    threads = oracle.threads_available()
+
+    def rate(args, secs):
+        oracle.step(*args, iterations=ITERATIONS, substeps=SUBSTEPS, threads=threads)  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < secs:
+            oracle.step(*args, iterations=ITERATIONS, substeps=SUBSTEPS, threads=threads)
+            n += 1
+        dt = time.perf_counter() - t0
+        return args[0].shape[0] * n / dt, n, dt
+
     s = synthetic.config_states("cpu_reference")
     args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
-    B = args[0].shape[0]
-    threads = oracle.threads_available()
-    oracle.step(*args, iterations=ITERATIONS, substeps=SUBSTEPS, threads=threads)  # warm-up
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        oracle.step(*args, iterations=ITERATIONS, substeps=SUBSTEPS, threads=threads)
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": B * n / dt, "unit": "world-steps/s", "cores": threads, "kind": "port",
-            "sample": f"{n} calls x {B} worlds of configuration 1 (seed 0), float64 oracle, {ITERATIONS} iterations "
-                      f"x {SUBSTEPS} substeps, {dt:.1f} s; MuJoCo C (the reference's CPU path) is not installed"}
+    value, n, dt = rate(args, seconds)
+    cx, _ = corpus_inputs()
+    cval, cn, cdt = rate([a[:1024] for a in cx], corpus_seconds)
+    return {"value": value, "unit": "world-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{n} calls x {args[0].shape[0]} worlds of configuration 1 (seed 0), float64 oracle, "
+                      f"{ITERATIONS} iterations x {SUBSTEPS} substeps, {dt:.1f} s; MuJoCo C (the reference's CPU path) "
+                      "is not installed on the box",
+            "corpus_mf_s0": {"value": cval, "unit": "world-steps/s", "cores": threads,
+                             "sample": f"{cn} calls x the first 1024 states of mf_s0, float64 oracle, {cdt:.1f} s",
+                             "published_mujoco_c": {cpu: {"ms_per_4096_worlds": ms, "threads": th,
+                                                          "world_steps_per_s": 4096 / (ms / 1e3)}
+                                                    for cpu, (ms, th) in PUBLISHED_CPU.items()}}}
+
+
+CORPUS = ROOT / "tests" / "golden" / "corpus_mf_s0.npz"
+# the reference's published numbers on this corpus at B = 4096 (docs/results/paper_<gpu>/paper_bench.md:91 forward,
+# :92 vjp, :35 backward, :50 Jacobian; 3-process medians for forward and vjp), ms per step (Jacobian: us per world)
+PUBLISHED = {"H100 80GB HBM3 (sm_90)": {"fwd": 1.700, "vjp": 2.728, "bwd": 0.930, "jacobian_us_per_world": 16.74},
+             "RTX PRO 6000 Blackwell Server (sm_120)": {"fwd": 1.214, "vjp": 1.784, "bwd": 0.563,
+                                                         "jacobian_us_per_world": 9.74}}
+# MuJoCo C float64 on the same corpus, 4096 worlds per step (paper_<gpu>/paper_bench.md:28), ms per step and threads
+PUBLISHED_CPU = {"AMD EPYC 9555": (34.746, 16), "Xeon Platinum 8462Y+": (57.374, 13)}
+
+
+def corpus_inputs(dev=None):
+    """The 4096 input states of the reference's benchmark corpus mf_s0 and its stored cotangent 0."""
+    with np.load(CORPUS) as z:
+        keys = ("qpos", "qvel", "qacc_warmstart", "ctrl", "friction", "com")
+        x = [np.ascontiguousarray(z[k]) for k in keys]
+        cot = [np.ascontiguousarray(z["cot_qpos"]), np.ascontiguousarray(z["cot_qvel"])]
+    if dev is None:
+        return x, cot
+    import torch
+    return [torch.from_numpy(a).to(dev) for a in x], [torch.from_numpy(a).to(dev) for a in cot]
+
+
+def paper_timeit(call, sync, rounds=6, warm_calls=5, warm_s=1.0, target_s=0.25):
+    """The reference's timing protocol (scripts/paper_bench/common.py:154-193): warm-up of at least warm_calls calls
+    and warm_s seconds (each call synchronised), then rounds + 1 rounds of n back-to-back calls with one
+    synchronisation each (n sized so a round lasts about target_s), the first round dropped; wall-clock ms per call:
+    median, p10, p90 over the kept rounds."""
+    t0, k = time.perf_counter(), 0
+    while k < warm_calls or time.perf_counter() - t0 < warm_s:
+        call()
+        sync()
+        k += 1
+    per_call = (time.perf_counter() - t0) / k
+    n = int(min(200, max(1, round(target_s / max(per_call, 1e-6)))))
+    per = []
+    for _ in range(rounds + 1):
+        t = time.perf_counter()
+        for _ in range(n):
+            call()
+        sync()
+        per.append((time.perf_counter() - t) / n)
+    a = 1e3 * np.asarray(per[1:])
+    return {"median": float(np.median(a)), "p10": float(np.percentile(a, 10)), "p90": float(np.percentile(a, 90)),
+            "n": n, "rounds": rounds}
+
+
+def measure_corpus(dev):
+    """The reference's own benchmark workload: the 4096 states of its corpus mf_s0, 10 iterations, 4 substeps, timed
+    with its protocol (paper_timeit), for the legs it publishes: fwd (forward without tape), fwd_tape, bwd (the
+    adjoint alone on one tape, the stored cotangent 0), vjp (forward with tape + adjoint) in the exact gradient mode
+    (clamp_kv=1, normal=0), and the full 71 x 99 Jacobian (forward with tape + the Jacobian kernel)."""
+    import torch
+    from nablaengine_b200 import torch_ffi
+    x, (cq, cv) = corpus_inputs(dev)
+    B = x[0].shape[0]
+    sync = torch.cuda.synchronize
+    kw = dict(iterations=ITERATIONS, substeps=SUBSTEPS)
+    q1, v1, w1, info, tape = torch_ffi.forward(*x, tape=True, **kw)
+    inf = info.cpu().numpy()
+    legs = {
+        "fwd": lambda: torch_ffi.forward(*x, **kw),
+        "fwd_tape": lambda: torch_ffi.forward(*x, tape=True, **kw),
+        "bwd": lambda: torch_ffi.backward(tape, x[4], x[5], cq, cv, clamp_kv=1, normal=0),
+        "vjp": lambda: torch_ffi.backward(torch_ffi.forward(*x, tape=True, **kw)[4], x[4], x[5], cq, cv, clamp_kv=1,
+                                          normal=0),
+        "jacobian": lambda: torch_ffi.jacobian(torch_ffi.forward(*x, tape=True, **kw)[4], x[4], x[5]),
+    }
+    out = {"workload": "the reference's corpus mf_s0 (4096 states, tests/golden/corpus_mf_s0.npz), 10 iterations x "
+                       "4 substeps, exact gradient mode; the reference's timing protocol (wall clock, back-to-back "
+                       "calls, one sync per round, median of 6 rounds after a dropped one)",
+           "worlds": B, "mean_newton_iterations_last_substep": float(inf[:, 0].mean()),
+           "mean_contacts_last_substep": float(inf[:, 1].mean()), "max_rows_last_substep": int(inf[:, 2].max())}
+    for name, fn in legs.items():
+        r = paper_timeit(fn, sync)
+        r["world_steps_per_s"] = B / (r["median"] / 1e3)
+        out[name] = r
+    out["jacobian"]["us_per_world"] = out["jacobian"]["median"] * 1e3 / B
+    out["published"] = PUBLISHED
+    return out
 
 
 def measure_fwd_grad(dev, rank, steps, warmup, flush):
@@ -194,16 +285,16 @@ def measure_jacobian(dev, rank, steps, warmup, flush):
 
 
 def run_reference(a, rank):
-    """--impl reference: rank 0 times the reference's CPU path substitute (the float64 oracle port) per step on a
-    bounded sample of the configuration-2 workload."""
+    """--impl reference: rank 0 times the reference's CPU path substitute (the float64 oracle port, all host threads)
+    per step on the whole configuration-2 workload (4096 worlds per step)."""
     if rank != 0:
         return
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     from nablaengine_b200 import synthetic
     s = synthetic.config_states("forward")
-    sample = 512  # worlds per timed step (a bounded slice of the 4096)
-    args = [s[k][:sample] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    args = [s[k] for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    B = args[0].shape[0]
     threads = oracle.threads_available()
     for _ in range(a.warmup):
         oracle.step(*args, iterations=ITERATIONS, substeps=SUBSTEPS, threads=threads)
@@ -212,18 +303,52 @@ def run_reference(a, rank):
         t0 = time.perf_counter()
         oracle.step(*args, iterations=ITERATIONS, substeps=SUBSTEPS, threads=threads)
         times.append(time.perf_counter() - t0)
-    value = sample * len(times) / sum(times)
+    value = B * len(times) / sum(times)
     out = {"metric": METRIC, "value": value, "unit": "world-steps/s", "impl": "reference", "n_gpus": a.gpus,
-           "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * B_PER_GPU / value,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * B / value,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
            "config": {"workload": "forward control step, BASELINE configuration 2 (B=4096 seeded synthetic G1 "
-                                  "states; the timed sample: the first 512 worlds per step)",
+                                  "states, all 4096 per timed step)",
                       "iterations": ITERATIONS, "substeps": SUBSTEPS, "cpu_threads": threads},
            "cpu_baseline": {"value": value, "unit": "world-steps/s", "cores": threads, "kind": "port",
-                            "sample": f"{sample} of the 4096 worlds per step, float64 oracle; MuJoCo C (the "
-                                      "reference's CPU path) is not installed on the box"},
+                            "sample": f"all {B} worlds per step, float64 oracle; MuJoCo C (the reference's CPU path) "
+                                      "is not installed on the box"},
            "e2e": {"value": value, "unit": "world-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
+
+
+def profile_case(a):
+    """--profile-case K: a small case for ncu captures, the kernel K (forward: configuration-2 states; adjoint: one
+    forward with tape, then the adjoint, configuration-3 states, exact mode; jacobian: configuration-4 states)
+    launched --launches times on --worlds seeded worlds (default 1480: one wave of the forward). Capture the last
+    launch with ncu (-k regex:k_<K> -s <launches - 1> -c 1); no timing is printed."""
+    import torch
+    from nablaengine_b200 import synthetic, torch_ffi
+    cfg = {"forward": "forward", "adjoint": "vjp", "jacobian": "jacobian", "corpus": None}[a.profile_case]
+    if cfg is None:
+        x, _ = corpus_inputs("cuda")
+        x = [t[:a.worlds] for t in x]
+    else:
+        s = synthetic.config_states(cfg, B=a.worlds)
+        x = [torch.from_numpy(s[k]).cuda() for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    if a.profile_case in ("forward", "corpus"):
+        for _ in range(a.launches):
+            out = torch_ffi.forward(*x)
+        torch.cuda.synchronize()
+        print("ok forward, mean Newton iterations of the last substep", out[3][:, 0].float().mean().item())
+        return
+    q1, v1, w1, info, tape = torch_ffi.forward(*x, tape=True)
+    if a.profile_case == "adjoint":
+        gq, gv = torch.zeros_like(q1), 2 * v1
+        for _ in range(a.launches):
+            r = torch_ffi.backward(tape, x[4], x[5], gq, gv, clamp_kv=1, normal=0)
+        torch.cuda.synchronize()
+        print("ok adjoint, |g_ctrl| =", r[2].norm().item())
+    else:
+        for _ in range(a.launches):
+            J, jinfo = torch_ffi.jacobian(tape, x[4], x[5])
+        torch.cuda.synchronize()
+        print("ok jacobian, |J| =", J.norm().item())
 
 
 def main():
@@ -233,7 +358,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-corpus", action="store_true", help="skip the corpus leg")
+    ap.add_argument("--profile-case", choices=("forward", "adjoint", "jacobian", "corpus"), default=None,
+                    help="run a small case of one kernel for an ncu capture instead of the benchmark")
+    ap.add_argument("--worlds", type=int, default=1480, help="--profile-case: worlds")
+    ap.add_argument("--launches", type=int, default=3, help="--profile-case: launches of the kernel")
     a = ap.parse_args()
+    if a.profile_case:
+        return profile_case(a)
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if a.impl == "reference":
@@ -292,6 +424,7 @@ def main():
     jac = measure_jacobian(dev, rank, max(1, min(a.steps, 3)), 1, flush)
     fg_ms = torch.tensor([fg["ms"], fg["ms_fwd_tape"], fg["ms_adjoint"], jac["ms"]], dtype=torch.float64,
                          device=dev)
+    corpus = measure_corpus(dev) if world == 1 and not a.no_corpus else None
 
     # end to end through the public API: pinned host inputs in, host outputs back, every step
     host = [t.cpu().pin_memory() for t in x]
@@ -331,7 +464,7 @@ def main():
         return
     ms = 1e3 * t_s / a.steps
     achieved = flop_step / (ms / 1e3) / 1e12
-    tpw = traffic_per_world()
+    tpw = FORWARD_DRAM_BYTES_PER_WORLD
     peaks = load_peaks()
     out = {
         "metric": METRIC, "value": value, "unit": "world-steps/s", "n_gpus": world, "steps": a.steps,
@@ -353,12 +486,13 @@ def main():
                                   f"{peaks.get('sm_max_mhz', 1965.0):.0f} MHz; MEASURED_PEAKS.json has no FP32 "
                                   "figure); the path has no GEMM or HBM-bound kernel",
                      "flop_per_step": flop_step,
-                     "traffic": None if tpw is None else tpw * B,
+                     "traffic": tpw * B,
                      "hbm_achieved_gbs": (B * (556 + 440) / (ms / 1e3)) / 1e9,
                      "hbm_peak_gbs": peaks.get("hbm_gbs")},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "world-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": a.steps * (3 if torch_ffi._DIAG_ON[0] else 2),  # k_order, k_forward (+ diagnostics)
+        # k_order, k_forward (+ the diagnostics counters and the last-forward record)
+        "gpu_launches": a.steps * (4 if torch_ffi.diagnostics_enabled() else 2),
         "fwd_grad": {"metric": "world-steps/sec fwd+grad at B=4096/GPU (BASELINE configuration 3: loss sum(qvel'^2), "
                                "VJP w.r.t. qpos, qvel, ctrl, exact mode clamp_kv=1 normal=0, torch autograd)",
                      "value": world * fg["B"] / (fg_ms[0].item() / 1e3), "unit": "world-steps/s",
@@ -372,6 +506,8 @@ def main():
                      "l2": "flushed between timed steps"},
         "kernel_ms": {"median": statistics.median(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
     }
+    if corpus is not None:
+        out["corpus"] = corpus
     if world == 1 and not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline()
     print(json.dumps(out), flush=True)

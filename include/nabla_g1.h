@@ -106,6 +106,22 @@ int nb_g1_diag_forward(cudaStream_t stream, unsigned long long* counters, int nw
 int nb_g1_diag_backward(cudaStream_t stream, unsigned long long* counters, int nw, const float* gq, const float* gv,
                         const float* gctrl, const float* gq_out, const float* gv_out, int* info);
 
+/* The record of one forward call, from that call's info (B,4): rec[4] (device memory, uint32) = [worlds, contacts
+ * summed over the worlds, the most contacts of one world, the most constraint rows of one world], info's counts being
+ * the last substep's; rec2 (may be NULL) receives a copy (e.g. the record kept per batch size). One small kernel,
+ * stream-ordered after the forward it reads; the sum is kept modulo 2^32. Replaces the reference's last-forward record
+ * `k_last_fwd` / `k_last_read` and its slots per batch size (src/nablaengine/jax_ffi.py:352-425, `last_forward`
+ * :1487), which it keeps in the library; here the caller owns the record's memory. */
+int nb_g1_last_forward(cudaStream_t stream, int nw, const int* info, unsigned* rec, unsigned* rec2);
+
+/* The launch shapes on device dev (after nb_g1_upload on it): out[8] = [the forward's dynamic shared memory per
+ * block (bytes), the forward's resident worlds per SM, the adjoint's shared memory per block, its resident worlds per
+ * SM, the Jacobian's shared memory per block, its resident output rows per SM, the device's SM count, 0]; a world or
+ * row count of 0 means the kernel does not fit the device. Restores the caller's current device. Replaces
+ * `int <pfx>_launch(int dev, long long* o)` (src/nablaengine/jax_ffi.py:243-253: the adjoint's shared memory and
+ * resident worlds per SM). */
+int nb_g1_launch(int dev, long long out[8]);
+
 /* nb_g1_forward plus the per-substep work counters stats (B, nsub, 8) int32: contacts kept, constraint rows, Newton
  * iterations, line-search evaluations, Hessian factorisations, broad-phase candidate pairs, contacts found, 0; the
  * outputs are bitwise those of nb_g1_forward. The counters feed the
@@ -125,7 +141,9 @@ int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const fl
  * library: NB_G1_NOALLOC_MAX_WORLDS int32 (1 MiB) that every device which loads the library holds until the process
  * exits. nw above NB_G1_NOALLOC_MAX_WORLDS returns cudaErrorInvalidValue (1) and launches nothing. The first call on
  * a device (the current device) looks up that device's copy of the buffer (cudaGetSymbolAddress, once per device):
- * make that first call before any stream capture. Every call on a device shares the buffer: the order of one call is
+ * make that first call before any stream capture. The address is kept for the rest of the process: cudaDeviceReset
+ * on a device destroys its context and the buffer with it, and the kept address then points at nothing, so after a
+ * reset of a device do not call nb_g1_forward_noalloc on it again in the same process. Every call on a device shares the buffer: the order of one call is
  * overwritten by the next (nothing in it needs to start at zero), so calls whose kernels overlap on the GPU, on
  * different streams, race on it and must be serialised by the caller. The call allocates and frees nothing.
  * No counterpart in the reference's ABI. */

@@ -2,7 +2,7 @@
 
 nvcc cross-compiles without a GPU, so this runs anywhere the CUDA toolkit is installed; the built .so travels with
 the repository to the GPU machines. `python -m nablaengine_b200.build` rebuilds when a source is newer than the
-library.
+library or the library was built with other nvcc flags (recorded in a stamp file beside it).
 """
 import os
 import shutil
@@ -27,21 +27,35 @@ def nvcc():
     raise RuntimeError("nvcc not found: the CUDA toolkit is needed to build libnabla_g1.so")
 
 
-def stale():
-    if not LIB.exists():
+def _stamp(lib):
+    return lib.with_name(lib.name + ".flags")
+
+
+def _flags_text(extra):
+    return " ".join([*ARCH, *FLAGS, *extra])
+
+
+def stale(lib=LIB, extra=()):
+    """True when `lib` is missing, older than a source, or was built with other nvcc flags (the stamp file beside it
+    records them)."""
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in DEPS)
+    t = lib.stat().st_mtime
+    if any(p.stat().st_mtime > t for p in DEPS):
+        return True
+    stamp = _stamp(lib)
+    return not stamp.exists() or stamp.read_text() != _flags_text(extra)
 
 
 PROFILE_LIB = LIBDIR / "libnabla_g1_prof.so"
 
 
 def build(force=False, verbose=False, extra=(), out=None):
-    """Compile the library when it is missing or older than its sources; returns its path. `out` and `extra`: another
-    output path and extra nvcc flags (the phase-profile build: -DNB_PROFILE into PROFILE_LIB)."""
+    """Compile the library when it is missing, older than its sources or built with other flags; returns its path.
+    `out` and `extra`: another output path and extra nvcc flags (the phase-profile build: -DNB_PROFILE into
+    PROFILE_LIB)."""
     lib = Path(out) if out else LIB
-    if not force and lib.exists() and not any(p.stat().st_mtime > lib.stat().st_mtime for p in DEPS):
+    if not force and not stale(lib, extra):
         return lib
     LIBDIR.mkdir(exist_ok=True)
     tmp = lib.with_suffix(f".tmp{os.getpid()}.so")
@@ -55,6 +69,7 @@ def build(force=False, verbose=False, extra=(), out=None):
     if verbose:
         print(r.stderr, flush=True)
     os.replace(tmp, lib)
+    _stamp(lib).write_text(_flags_text(extra))
     return lib
 
 

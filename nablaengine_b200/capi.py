@@ -12,7 +12,8 @@ from . import build as _build
 HEADER = Path(__file__).resolve().parents[1] / "include" / "nabla_g1.h"
 EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward", "nb_g1_forward_stats",
            "nb_g1_adjoint", "nb_g1_jacobian", "nb_g1_kinematics", "nb_g1_kinematics_vjp", "nb_g1_diag_count",
-           "nb_g1_diag_forward", "nb_g1_diag_backward", "nb_g1_forward_noalloc")
+           "nb_g1_diag_forward", "nb_g1_diag_backward", "nb_g1_forward_noalloc", "nb_g1_last_forward",
+           "nb_g1_launch")
 ABI_VERSION = 3
 NQ, NV, NU, NBODY, MAXCON, NEFC = 36, 35, 29, 31, 64, 192
 
@@ -60,6 +61,8 @@ def load(path=None, build_if_missing=True):
         lib.nb_g1_diag_count.argtypes, lib.nb_g1_diag_count.restype = [], i64
         lib.nb_g1_diag_forward.argtypes, lib.nb_g1_diag_forward.restype = [vp, vp, i32, i32, i32, vp, vp], i32
         lib.nb_g1_diag_backward.argtypes, lib.nb_g1_diag_backward.restype = [vp, vp, i32] + [vp] * 6, i32
+        lib.nb_g1_last_forward.argtypes, lib.nb_g1_last_forward.restype = [vp, i32, vp, vp, vp], i32
+        lib.nb_g1_launch.argtypes, lib.nb_g1_launch.restype = [i32, vp], i32
         sizes = (ctypes.c_longlong * 8)()
         lib.nb_g1_sizes(sizes)
         want = (NQ, NV, NU, NBODY, MAXCON, NEFC)

@@ -13,7 +13,7 @@
 namespace nbg1 {
 
 #ifndef NB_WPB
-#define NB_WPB 10
+#define NB_WPB 14
 #endif
 #ifndef NB_LOCKSTEP
 #define NB_LOCKSTEP 1
@@ -407,6 +407,37 @@ __global__ void k_diag_bwd(unsigned long long* d, int nw, const float* gq, const
 }
 static unsigned diag_grid(int nw) { return (unsigned)std::max(1, std::min(148, (nw + 255) / 256)); }
 
+// The record of one forward call from its info (B,4): [worlds, contacts summed over the worlds, the most contacts and
+// the most constraint rows of one world] (info's counts are the last substep's), written whole into rec and, when
+// given, rec2. One block: a strided pass per thread, then a warp and a block reduction (exact integer sums).
+constexpr int LAST_THREADS = 256;
+__global__ void __launch_bounds__(LAST_THREADS) k_last_forward(int nw, const int* __restrict__ info,
+                                                               unsigned* __restrict__ rec, unsigned* __restrict__ rec2) {
+  __shared__ unsigned part[3][LAST_THREADS / 32];
+  unsigned sum = 0, cmax = 0, rmax = 0;  // (the contact sum modulo 2^32, as every word of the record)
+  for (int w = threadIdx.x; w < nw; w += LAST_THREADS) {
+    const unsigned c = (unsigned)max(info[4 * w + 1], 0), r = (unsigned)max(info[4 * w + 2], 0);
+    sum += c;
+    cmax = max(cmax, c);
+    rmax = max(rmax, r);
+  }
+  sum = __reduce_add_sync(FULL, sum);
+  cmax = __reduce_max_sync(FULL, cmax);
+  rmax = __reduce_max_sync(FULL, rmax);
+  const int wid = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) { part[0][wid] = sum; part[1][wid] = cmax; part[2][wid] = rmax; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned t = 0, c = 0, r = 0;
+    for (int i = 0; i < LAST_THREADS / 32; i++) { t += part[0][i]; c = max(c, part[1][i]); r = max(r, part[2][i]); }
+    const unsigned v[4] = {(unsigned)nw, t, c, r};
+    for (int k = 0; k < 4; k++) {
+      rec[k] = v[k];
+      if (rec2) rec2[k] = v[k];
+    }
+  }
+}
+
 static_assert(sizeof(World) % 16 == 0, "world records stay 16-byte aligned");
 static_assert(offsetof(World, M) % 16 == 0 && offsetof(World, L) % 16 == 0, "float4 copies of the triangles");
 
@@ -455,6 +486,31 @@ int nb_g1_diag_backward(cudaStream_t stream, unsigned long long* counters, int n
 }
 
 long long nb_g1_diag_count(void) { return NDIAG; }
+
+int nb_g1_last_forward(cudaStream_t stream, int nw, const int* info, unsigned* rec, unsigned* rec2) {
+  if (nw < 0 || !rec || (nw > 0 && !info)) return (int)cudaErrorInvalidValue;
+  k_last_forward<<<1, LAST_THREADS, 0, stream>>>(nw, info, rec, rec2);
+  return (int)cudaGetLastError();
+}
+
+int nb_g1_launch(int dev, long long out[8]) {
+  for (int i = 0; i < 8; i++) out[i] = 0;
+  int old = -1, nsm = 0, fb = 0, ab = 0, jb = 0;
+  cudaError_t e = cudaGetDevice(&old);
+  if (e != cudaSuccess) return (int)e;
+  if ((e = cudaSetDevice(dev)) != cudaSuccess) return (int)e;
+  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fb, k_forward, WPB * 32, SMEM);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ab, k_adjoint, AWPB * 32, ASMEM);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&jb, k_jacobian, (JR + 1) * 32, JSMEM);
+  const cudaError_t e2 = cudaSetDevice(old);
+  if (e == cudaSuccess) e = e2;
+  if (e != cudaSuccess) return (int)e;
+  const long long v[8] = {(long long)SMEM, (long long)fb * WPB, (long long)ASMEM, (long long)ab * AWPB,
+                          (long long)JSMEM, (long long)jb * JR, nsm, 0};
+  for (int i = 0; i < 8; i++) out[i] = v[i];
+  return 0;
+}
 
 int nb_g1_kinematics(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* com,
                      float* qpos_n, float* xpos, float* xquat, float* cvel, float* subtree_com) {

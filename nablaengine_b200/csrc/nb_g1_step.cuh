@@ -16,6 +16,7 @@
 //    candidates), so results are bitwise reproducible run to run.
 #pragma once
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 #define NB_REAL float
@@ -25,13 +26,22 @@
 namespace nbg1 {
 
 constexpr int NQ = G1_NQ, NV = G1_NV, NU = G1_NU, NB = G1_NBODY, NG = G1_NGEOM, NP = G1_NPAIR;
-constexpr int MAXCON = 64, NEFC = 192, KDOF = 16, MAXD = G1_MAXDEPTH;
+constexpr int MAXCON = 64, NEFC = 192, KDOF = 16, MAXD = G1_MAXDEPTH;  // the capacity of the ABI and the tape
+#ifndef NB_WCON
+#define NB_WCON 64
+#endif
+#ifndef NB_WROWS
+#define NB_WROWS 192
+#endif
+constexpr int WCON = NB_WCON, WROWS = NB_WROWS;  // the capacity of a World record (contacts, constraint rows)
+static_assert(WCON <= MAXCON && WROWS <= NEFC && WCON % 32 == 0 && WROWS % 32 == 0, "World capacity");
 static_assert(G1_NV == G1_NBODY + 4, "dof d >= 6 is the hinge of body d - 4 (one hinge per body after the root)");
+__host__ __device__ constexpr int TRI(int i, int j) { return i * (i + 1) / 2 + j; }  // packed lower triangle, j <= i
 constexpr int NTRI = NV * (NV + 1) / 2;
 constexpr int NTRIP = (NTRI + 3) / 4 * 4;  // the packed triangles' storage in World: whole float4s
+
 constexpr unsigned FULL = 0xffffffffu;
-constexpr int ROWS_PER_LANE = (NEFC + 31) / 32;
-__host__ __device__ constexpr int TRI(int i, int j) { return i * (i + 1) / 2 + j; }  // packed lower triangle, j <= i
+constexpr int ROWS_PER_LANE = (WROWS + 31) / 32;
 
 enum : int { UNSUPPORTED_PAIR = 1, CONTACT_OVERFLOW = 4, ROW_OVERFLOW = 16 };
 
@@ -66,45 +76,66 @@ __device__ unsigned long long g_prof[NPROF];
 #define PROF_COUNT(k, n) do { } while (0)
 #endif
 
+// The world record, resident in shared memory for the whole control step. Its scratch overlaps by phase: the smooth
+// phase's body terms (sm: kinematics to mass_and_force) share their space with everything from collision on (the
+// contacts, their groups and rows), and the collision phase's geom poses and candidate list (col) with the rows,
+// which make_rows writes after collision; what a phase reads was written in the same substep after the previous
+// owner of that space was done with it.
 struct __align__(16) World {
-  float qpos[NQ], qvel[NV], qacc[NV], ctrl[NU], com[3], fric;
-  float Q[NB][4], X[NB][3];            // body poses
-  float dw[NV][3], dv[NV][3];          // dof motion about O: angular axis, velocity of the point O
-  float BV[NB][6];                     // body spatial motion at O (angular, linear) for a generalised vector
   float M[NTRIP], L[NTRIP];            // mass matrix (with armature), factor scratch (16-byte aligned)
-  float qsm[NV], qacc0[NV], Ma[NV], grad[NV], p[NV], Mp[NV], tmp[NV], dinv[NV + 1];
+  float qpos[NQ], qvel[NV], qacc[NV], ctrl[NU], com[3], fric;
+  float X[NB][3];                      // body positions (Q: orientations, until collision)
+  float dw[NV][3], dv[NV][3];          // dof motion about O: angular axis, velocity of the point O
+  float qsm[NV], qacc0[NV], Ma[NV], grad[NV], p[NV], dinv[NV + 1];  // p: the Newton direction, then a_adv
   union {
-    struct { float om[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
-    struct { float gx[NG][3], gq[NG][4]; unsigned short cand[NP + 2]; } col;                 // collision phase
-    struct { float K[21], P[KDOF][6]; unsigned char dof[KDOF]; } hs;                        // Hessian assembly
-  } u;
-  unsigned long long grp_mask[MAXCON];  // contacts of group g (same body pair) as bits
-  short lim_row[NV];                    // the dof's limit row, or -1
-  unsigned char con_grp[MAXCON], grp_lead[MAXCON];
+    float BV[NB][6];                   // body spatial motion at O (angular, linear) for a generalised vector: rows_jv
+    struct { float K[21], P[KDOF][6]; unsigned char dof[KDOF]; } hs;  // Hessian assembly
+  };
   int ngroup, nls, nfact, pad3_;        // groups; line-search evaluations, factorisations (work counters)
   float ncost;                          // Newton state between iterations: cost, iterations, converged, same zones
   int nit_cur, ndone, nsame;
   unsigned clamp_lo, clamp_hi;          // actuator force at its limit (dof bits), for the tape
   int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
-  int con_pair[MAXCON];
-  unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
-  unsigned short con_bb[MAXCON];       // the contact's bodies b1 | b2 << 8 (contact_setup on)
-  float con_dist[MAXCON], con_mu[MAXCON];
-  float con_fr[MAXCON][9];             // frame rows: normal, tangent 1, tangent 2
-  float con_pos[MAXCON][3];
-  union {  // per-contact scratch, each consumed by the phase that writes it
-    float jd[MAXCON][3];  // J_d v per frame row
-    float wr[MAXCON][6];  // the contact wrench at O (moment, force)
-    float C[MAXCON][5];   // contact_setup: the group key in C[c][0]
-  } cs;
-  float efc_D[NEFC], efc_aref[NEFC], efc_jar[NEFC], efc_jv[NEFC];
-  short efc_a[NEFC];                   // dof (limit row) or contact
-  signed char efc_b[NEFC];             // limit sign, or the contact row t (n + mu t1, n - mu t1, n + mu t2, ...)
-  unsigned char efc_kind[NEFC];
+  union {
+    struct {  // from kinematics to the geom poses at the start of collision
+      float Q[NB][4];                   // body orientations
+      struct { float om[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
+    };
+    struct {  // collision on
+      unsigned long long grp_mask[WCON];  // contacts of group g (same body pair) as bits
+      int con_pair[WCON];
+      unsigned char con_slot[WCON], con_row0[WCON], con_nrow[WCON];
+      unsigned short con_bb[WCON];        // the contact's bodies b1 | b2 << 8 (contact_setup on)
+      float con_dist[WCON], con_mu[WCON];
+      float con_fr[WCON][6];              // frame rows: normal, tangent 1 (tangent 2 = normal x tangent 1)
+      float con_pos[WCON][3];
+      union {  // per-contact scratch, each consumed by the phase that writes it
+        float jd[WCON][3];  // J_d v per frame row
+        float wr[WCON][6];  // the contact wrench at O (moment, force)
+        struct { int key[WCON]; unsigned char lead[WCON], grp[WCON]; } g;  // contact_setup: the groups
+      } cs;
+      short lim_row[NV];                  // the dof's limit row, or -1
+      union {
+        struct {  // make_rows on
+          float efc_D[WROWS];
+          float efc_jar[WROWS];           // J a - aref at the current acceleration a (from make_rows to the
+                                          // Newton start: aref)
+          short efc_a[WROWS];             // dof (limit row) or contact
+          signed char efc_b[WROWS];       // limit sign, or the contact row t (n + mu t1, n - mu t1, n + mu t2, ...)
+          unsigned char efc_kind[WROWS];
+        };
+        struct { float gx[NG][3], gq[NG][4]; unsigned short cand[NP + 2]; } col;  // collision phase
+      };
+    };
+  };
 #ifdef NB_PROFILE
   long long prof_t;
 #endif
 };
+
+// collision computes the geom poses from Q into col, then writes the contacts (over Q): Q must not share col's space
+static_assert(offsetof(World, Q) + sizeof(World::Q) <= offsetof(World, col) ||
+              offsetof(World, col) + sizeof(World::col) <= offsetof(World, Q), "Q and col overlap");
 
 // ---- small vector helpers --------------------------------------------------------------------------------------
 __device__ __forceinline__ void qmul(const float* a, const float* b, float* o) {
@@ -173,18 +204,18 @@ __device__ __noinline__ void kinematics(World& s, int lane) {
         qrot(s.Q[1], wl, om);
         for (int k = 0; k < 3; k++) {
           s.X[1][k] = s.qpos[k];
-          s.u.sm.om[1][k] = om[k];
-          s.u.sm.al[1][k] = 0.f;
-          s.u.sm.ao[1][k] = 0.f;
+          s.sm.om[1][k] = om[k];
+          s.sm.al[1][k] = 0.f;
+          s.sm.ao[1][k] = 0.f;
         }
-        s.u.sm.ao[1][2] = -G1_GRAVITY_Z;
+        s.sm.ao[1][2] = -G1_GRAVITY_Z;
       } else {
         const int p = ldi(g1_body_parent + b);
         float Qp[4], Xp[3], omp[3], alp[3], aop[3];
         for (int k = 0; k < 4; k++) Qp[k] = s.Q[p][k];
         for (int k = 0; k < 3; k++) {
-          Xp[k] = s.X[p][k]; omp[k] = s.u.sm.om[p][k];
-          alp[k] = s.u.sm.al[p][k]; aop[k] = s.u.sm.ao[p][k];
+          Xp[k] = s.X[p][k]; omp[k] = s.sm.om[p][k];
+          alp[k] = s.sm.al[p][k]; aop[k] = s.sm.ao[p][k];
         }
         const float bq[4] = {ld(g1_body_quat + 4 * b), ld(g1_body_quat + 4 * b + 1), ld(g1_body_quat + 4 * b + 2),
                              ld(g1_body_quat + 4 * b + 3)};
@@ -210,9 +241,9 @@ __device__ __noinline__ void kinematics(World& s, int lane) {
         for (int k = 0; k < 4; k++) s.Q[b][k] = Q[k];
         for (int k = 0; k < 3; k++) {
           s.X[b][k] = X[k];
-          s.u.sm.om[b][k] = omp[k] + wd[k];
-          s.u.sm.al[b][k] = alp[k] + u2[k];
-          s.u.sm.ao[b][k] = aop[k] + u3[k] + wr_[k];
+          s.sm.om[b][k] = omp[k] + wd[k];
+          s.sm.al[b][k] = alp[k] + u2[k];
+          s.sm.ao[b][k] = aop[k] + u3[k] + wr_[k];
         }
       }
     }
@@ -254,7 +285,7 @@ __device__ __noinline__ void body_terms(World& s, int lane) {
       for (int k = 0; k < 3; k++) ip[k] += s.com[k];
     float c[3], Q[4], om[3], al[3], ao[3];
     for (int k = 0; k < 4; k++) Q[k] = s.Q[b][k];
-    for (int k = 0; k < 3; k++) { om[k] = s.u.sm.om[b][k]; al[k] = s.u.sm.al[b][k]; ao[k] = s.u.sm.ao[b][k]; }
+    for (int k = 0; k < 3; k++) { om[k] = s.sm.om[b][k]; al[k] = s.sm.al[b][k]; ao[k] = s.sm.ao[b][k]; }
     qrot(Q, ip, c);
     const float iq[4] = {ld(g1_body_iquat + 4 * b), ld(g1_body_iquat + 4 * b + 1), ld(g1_body_iquat + 4 * b + 2),
                          ld(g1_body_iquat + 4 * b + 3)};
@@ -290,10 +321,10 @@ __device__ __noinline__ void body_terms(World& s, int lane) {
     for (int k = 0; k < 3; k++) cO[k] = s.X[b][k] + c[k] - O[k];
     cross(cO, F, mo);
     for (int k = 0; k < 3; k++) { N[k] = Ial[k] + u1[k] + mo[k]; }
-    for (int k = 0; k < 3; k++) { s.u.sm.wr[b][k] = N[k]; s.u.sm.wr[b][3 + k] = F[k]; }
+    for (int k = 0; k < 3; k++) { s.sm.wr[b][k] = N[k]; s.sm.wr[b][3 + k] = F[k]; }
     // spatial inertia about O: rotational inertia about O (xx yy zz xy xz yz), h = m cO, m
     const float cc = dot3(cO, cO);
-    float* J = s.u.sm.I[b];
+    float* J = s.sm.I[b];
     J[0] = I[0][0] + m * (cc - cO[0] * cO[0]);
     J[1] = I[1][1] + m * (cc - cO[1] * cO[1]);
     J[2] = I[2][2] + m * (cc - cO[2] * cO[2]);
@@ -308,15 +339,15 @@ __device__ __noinline__ void body_terms(World& s, int lane) {
   for (int L = MAXD - 1; L >= 1; L--) {
     if (depth == L && nch > 0) {
       float wr[6], I[10];
-      for (int k = 0; k < 6; k++) wr[k] = s.u.sm.wr[b][k];
-      for (int k = 0; k < 10; k++) I[k] = s.u.sm.I[b][k];
+      for (int k = 0; k < 6; k++) wr[k] = s.sm.wr[b][k];
+      for (int k = 0; k < 10; k++) I[k] = s.sm.I[b][k];
       for (int c = 0; c < nch; c++) {
         const int ch = ldi(g1_body_child + 3 * b + c);
-        for (int k = 0; k < 6; k++) wr[k] += s.u.sm.wr[ch][k];
-        for (int k = 0; k < 10; k++) I[k] += s.u.sm.I[ch][k];
+        for (int k = 0; k < 6; k++) wr[k] += s.sm.wr[ch][k];
+        for (int k = 0; k < 10; k++) I[k] += s.sm.I[ch][k];
       }
-      for (int k = 0; k < 6; k++) s.u.sm.wr[b][k] = wr[k];
-      for (int k = 0; k < 10; k++) s.u.sm.I[b][k] = I[k];
+      for (int k = 0; k < 6; k++) s.sm.wr[b][k] = wr[k];
+      for (int k = 0; k < 10; k++) s.sm.I[b][k] = I[k];
     }
     __syncwarp();
   }
@@ -341,7 +372,7 @@ __device__ __noinline__ void mass_and_force(World& s, int lane) {
     const int b = ldi(g1_dof_body + i);
     const float w[3] = {s.dw[i][0], s.dw[i][1], s.dw[i][2]}, v[3] = {s.dv[i][0], s.dv[i][1], s.dv[i][2]};
     float J[10], n[3], f[3];
-    for (int k = 0; k < 10; k++) J[k] = s.u.sm.I[b][k];
+    for (int k = 0; k < 10; k++) J[k] = s.sm.I[b][k];
     apply_inertia(J, w, v, n, f);
     // ancestor dofs j < i (the dof's own body first for the free joint's dofs) and the diagonal
     unsigned long long anc = g1_body_dofmask[b] & ((1ull << i) - 1ull);
@@ -352,7 +383,7 @@ __device__ __noinline__ void mass_and_force(World& s, int lane) {
     }
     s.M[TRI(i, i)] = dot3(w, n) + dot3(v, f) + ld(g1_dof_armature + i);
     // bias: the subtree wrench of the dof's body projected on its motion
-    const float bias = dot3(w, s.u.sm.wr[b]) + dot3(v, s.u.sm.wr[b] + 3);
+    const float bias = dot3(w, s.sm.wr[b]) + dot3(v, s.sm.wr[b] + 3);
     float act = 0.f;
     bool clamp = false;
     if (i >= 6) {
@@ -657,10 +688,10 @@ __device__ __noinline__ void chol_solve(const float* L, const float* dinv, float
   __syncwarp();
 }
 
-// out = A v (A symmetric, packed)
-// (rows 0..31: one row per lane over all 35 columns; rows 32..34: split over the lanes, column j = lane, with the
+// A v for A symmetric (packed lower triangle): lane l gets entry l in .x and, on lanes 0 .. NT - 1, entry 32 + l in
+// .y (rows 0..31: one row per lane over all 35 columns; rows 32..34: split over the lanes, column j = lane, with the
 // 3 x 3 tail block on lanes 0..2, and warp reductions)
-__device__ __noinline__ void matvec(const float* A, const float* v, float* out, int lane) {
+__device__ __noinline__ float2 matvec(const float* A, const float* v, int lane) {
   float a0 = 0.f, a1 = 0.f;
 #pragma unroll 6
   for (int j = 0; j < NV - 1; j += 2) {
@@ -678,9 +709,15 @@ __device__ __noinline__ void matvec(const float* A, const float* v, float* out, 
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
     for (int m = 0; m < NT; m++) t[m] += __shfl_xor_sync(FULL, t[m], o);
-  out[lane] = a0 + a1;
-  if (lane < NT) out[32 + lane] = lane == 0 ? t[0] : (lane == 1 ? t[1] : t[2]);
-  __syncwarp();
+  return make_float2(a0 + a1, lane == 0 ? t[0] : (lane == 1 ? t[1] : (lane == 2 ? t[2] : 0.f)));
+}
+// lane l's entries of a vector in matvec's layout: .x = v[l], .y = v[32 + l] on lanes 0 .. NT - 1 (else 0)
+__device__ __forceinline__ float2 lanes_of(const float* v, int lane) {
+  return make_float2(v[lane], lane < NT ? v[32 + lane] : 0.f);
+}
+__device__ __forceinline__ void store_lanes(float* v, float2 x, int lane) {
+  v[lane] = x.x;
+  if (lane < NT) v[32 + lane] = x.y;
 }
 
 // the dofs that move only body 1 (m1, Jacobian sign -1) / only body 2 (m2, sign +1) of contact pair pr
@@ -688,6 +725,14 @@ __device__ __forceinline__ void body_masks(unsigned bb, unsigned long long* m1, 
   const unsigned long long a = __ldg(g1_body_dofmask + (bb & 255u)), b = __ldg(g1_body_dofmask + (bb >> 8));
   *m1 = a & ~b;
   *m2 = b & ~a;
+}
+
+// contact c's frame rows: normal, tangent 1 (stored) and tangent 2 = normal x tangent 1 (both frames of the
+// primitives, make_frame's and the capsule-plane axis frame, have that third row)
+__device__ __forceinline__ void frame_rows(const World& s, int c, float* fr) {
+#pragma unroll
+  for (int k = 0; k < 6; k++) fr[k] = s.con_fr[c][k];
+  cross(fr, fr + 3, fr + 6);
 }
 
 // ---- collision ---------------------------------------------------------------------------------------------------
@@ -721,11 +766,11 @@ __device__ __forceinline__ void sphere_sphere(const float* p1, float r1, const f
 // The bounding test of pair pr at the current geom poses (no contact at zero margin when it fails)
 __device__ __forceinline__ bool bounding(const World& s, int pr) {
   const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
-  const float dif[3] = {s.u.col.gx[g2][0] - s.u.col.gx[g1][0], s.u.col.gx[g2][1] - s.u.col.gx[g1][1],
-                        s.u.col.gx[g2][2] - s.u.col.gx[g1][2]};
+  const float dif[3] = {s.col.gx[g2][0] - s.col.gx[g1][0], s.col.gx[g2][1] - s.col.gx[g1][1],
+                        s.col.gx[g2][2] - s.col.gx[g1][2]};
   if (ldi(g1_geom_type + g1) == 0) {
     float n[3];
-    zaxis(s.u.col.gq[g1], n);
+    zaxis(s.col.gq[g1], n);
     return dot3(dif, n) <= ld(g1_geom_rbound + g2);
   }
   const float rb = ld(g1_geom_rbound + g1) + ld(g1_geom_rbound + g2);
@@ -736,7 +781,7 @@ __device__ __forceinline__ bool bounding(const World& s, int pr) {
 // prefix sum gives their contact indices
 struct Hit {
   int n, slot[2];
-  float dist[2], pos[2][3], fr[2][9];
+  float dist[2], pos[2][3], fr[2][6];  // frame rows: normal, tangent 1
 };
 
 // Narrow phase of candidate pair pr: its contacts (0..2, dist < 0) into h (h.n counted up from 0). MuJoCo Warp's
@@ -745,23 +790,23 @@ __device__ __forceinline__ void collide(World& s, int pr, Hit& h, int* unsup) {
   const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
   const int t1 = ldi(g1_geom_type + g1), t2 = ldi(g1_geom_type + g2);
   float p1[3], p2[3];
-  for (int k = 0; k < 3; k++) { p1[k] = s.u.col.gx[g1][k]; p2[k] = s.u.col.gx[g2][k]; }
+  for (int k = 0; k < 3; k++) { p1[k] = s.col.gx[g1][k]; p2[k] = s.col.gx[g2][k]; }
   const float r1 = ld(g1_geom_size + 3 * g1), r2 = ld(g1_geom_size + 3 * g2);
   auto emit = [&](int slot, float dist, const float* pos, const float* fr) {
     if (h.n == 0) {
       h.slot[0] = slot; h.dist[0] = dist;
       for (int k = 0; k < 3; k++) h.pos[0][k] = pos[k];
-      for (int k = 0; k < 9; k++) h.fr[0][k] = fr[k];
+      for (int k = 0; k < 6; k++) h.fr[0][k] = fr[k];
     } else {
       h.slot[1] = slot; h.dist[1] = dist;
       for (int k = 0; k < 3; k++) h.pos[1][k] = pos[k];
-      for (int k = 0; k < 9; k++) h.fr[1][k] = fr[k];
+      for (int k = 0; k < 6; k++) h.fr[1][k] = fr[k];
     }
     h.n++;
   };
   if (t1 == 0) {  // plane (the floor) against a sphere or a capsule
     float nrm[3];
-    zaxis(s.u.col.gq[g1], nrm);
+    zaxis(s.col.gq[g1], nrm);
     const float poff = dot3(p1, nrm);
     if (t2 == 2) {
       const float dist = dot3(p2, nrm) - poff - r2;
@@ -775,7 +820,7 @@ __device__ __forceinline__ void collide(World& s, int pr, Hit& h, int* unsup) {
     } else if (t2 == 3) {
       const float hl = ld(g1_geom_size + 3 * g2 + 1);
       float ax[3], fr[9];
-      zaxis(s.u.col.gq[g2], ax);
+      zaxis(s.col.gq[g2], ax);
       float d[2], ce[2][3];
       for (int e = 0; e < 2; e++) {
         for (int k = 0; k < 3; k++) ce[e][k] = e == 0 ? p2[k] + hl * ax[k] : p2[k] - hl * ax[k];
@@ -815,7 +860,7 @@ __device__ __forceinline__ void collide(World& s, int pr, Hit& h, int* unsup) {
   if (t1 == 2 && t2 == 3) {  // sphere-capsule: the regularised closest point of the segment
     const float hl = ld(g1_geom_size + 3 * g2 + 1);
     float ax[3], a[3], ab[3], ap[3], pt[3];
-    zaxis(s.u.col.gq[g2], ax);
+    zaxis(s.col.gq[g2], ax);
     for (int k = 0; k < 3; k++) { a[k] = p2[k] - ax[k] * hl; ab[k] = 2.f * hl * ax[k]; ap[k] = p1[k] - a[k]; }
     const float gam = dot3(ab, ab) + 1e-6f;
     const float t = fminf(fmaxf(dot3(ap, ab) / gam, 0.f), 1.f);
@@ -828,8 +873,8 @@ __device__ __forceinline__ void collide(World& s, int pr, Hit& h, int* unsup) {
   if (t1 == 3 && t2 == 3) {  // capsule-capsule: closest points of the segments (clamp cascade)
     const float hl1 = ld(g1_geom_size + 3 * g1 + 1), hl2 = ld(g1_geom_size + 3 * g2 + 1);
     float a1[3], a2[3], df[3];
-    zaxis(s.u.col.gq[g1], a1);
-    zaxis(s.u.col.gq[g2], a2);
+    zaxis(s.col.gq[g1], a1);
+    zaxis(s.col.gq[g2], a2);
     for (int k = 0; k < 3; k++) { a1[k] *= hl1; a2[k] *= hl2; df[k] = p1[k] - p2[k]; }
     const float ma = dot3(a1, a1), mb = -dot3(a1, a2), mc = dot3(a2, a2), u = -dot3(a1, df), v = dot3(a2, df);
     const float det = ma * mc - mb * mb;
@@ -885,8 +930,8 @@ __device__ __noinline__ void collision(World& s, int lane) {
                          ld(g1_geom_quat + 4 * g + 3)};
     float t[3];
     qrot(s.Q[b], gp, t);
-    for (int k = 0; k < 3; k++) s.u.col.gx[g][k] = s.X[b][k] + t[k];
-    qmul(s.Q[b], gq, s.u.col.gq[g]);
+    for (int k = 0; k < 3; k++) s.col.gx[g][k] = s.X[b][k] + t[k];
+    qmul(s.Q[b], gq, s.col.gq[g]);
   }
   __syncwarp();
   const unsigned below = (1u << lane) - 1u;
@@ -895,14 +940,14 @@ __device__ __noinline__ void collision(World& s, int lane) {
     const int pr = lane + 32 * k;
     const bool keep = pr < NP && bounding(s, pr);
     const unsigned bal = __ballot_sync(FULL, keep);
-    if (keep) s.u.col.cand[ncand + __popc(bal & below)] = (unsigned short)pr;
+    if (keep) s.col.cand[ncand + __popc(bal & below)] = (unsigned short)pr;
     ncand += __popc(bal);
   }
   __syncwarp();
   int total = 0, unsup = 0;
   for (int c0 = 0; c0 < ncand; c0 += 32) {
     const int ci = c0 + lane;
-    const int pr = ci < ncand ? s.u.col.cand[ci] : -1;
+    const int pr = ci < ncand ? s.col.cand[ci] : -1;
     Hit h;
     h.n = 0;
     if (pr >= 0) collide(s, pr, h, &unsup);
@@ -916,12 +961,12 @@ __device__ __noinline__ void collision(World& s, int lane) {
 #pragma unroll
     for (int e = 0; e < 2; e++) {
       const int c = base + e;
-      if (e >= h.n || c >= MAXCON) continue;
+      if (e >= h.n || c >= WCON) continue;
       s.con_pair[c] = pr;
       s.con_slot[c] = (unsigned char)h.slot[e];
       s.con_dist[c] = h.dist[e];
       for (int k = 0; k < 3; k++) s.con_pos[c][k] = h.pos[e][k];
-      for (int k = 0; k < 9; k++) s.con_fr[c][k] = h.fr[e][k];
+      for (int k = 0; k < 6; k++) s.con_fr[c][k] = h.fr[e][k];
     }
     total += __shfl_sync(FULL, incl, 31);
   }
@@ -929,8 +974,8 @@ __device__ __noinline__ void collision(World& s, int lane) {
   if (lane == 0) {
     s.ncand = ncand;
     s.ncon_raw = total;
-    s.ncon = min(total, MAXCON);
-    s.unsup |= unsup | (total > MAXCON ? CONTACT_OVERFLOW : 0);
+    s.ncon = min(total, WCON);
+    s.unsup |= unsup | (total > WCON ? CONTACT_OVERFLOW : 0);
   }
   __syncwarp();
 }
@@ -950,7 +995,7 @@ __device__ __noinline__ void contact_setup(World& s, int lane) {
     // the contact point relative to O (the frame rows' moments are (pos - O) x row)
     for (int k = 0; k < 3; k++) s.con_pos[c][k] -= O[k];
   }
-  // group leaders: the first contact of each (body1, body2); the key is kept in cs.C[c][0] for a moment
+  // group leaders: the first contact of each (body1, body2); the keys are kept in cs.g for a moment
   int ngroup = 0;
   for (int c0 = 0; c0 < ncon; c0 += 32) {
     const int c = c0 + lane;
@@ -961,26 +1006,26 @@ __device__ __noinline__ void contact_setup(World& s, int lane) {
       s.con_bb[c] = (unsigned short)(b1 | b2 << 8);
       key = b1 * 32 + b2;
       for (int e = 0; e < c0; e++)  // an earlier chunk (only past 32 contacts)
-        if (__float_as_int(s.cs.C[e][0]) == key) { lead = e; break; }
+        if (s.cs.g.key[e] == key) { lead = e; break; }
     }
     const unsigned same = __match_any_sync(FULL, key);
     if (lead == c) lead = c0 + __ffs(same) - 1;
     const bool leader = c < ncon && lead == c;
     const unsigned bal = __ballot_sync(FULL, leader);
     if (c < ncon) {
-      s.cs.C[c][0] = __int_as_float(key);
-      s.grp_lead[c] = (unsigned char)lead;
-      if (leader) s.con_grp[c] = (unsigned char)(ngroup + __popc(bal & ((1u << lane) - 1u)));
+      s.cs.g.key[c] = key;
+      s.cs.g.lead[c] = (unsigned char)lead;
+      if (leader) s.cs.g.grp[c] = (unsigned char)(ngroup + __popc(bal & ((1u << lane) - 1u)));
     }
     ngroup += __popc(bal);
     __syncwarp();
   }
-  for (int c = lane; c < ncon; c += 32) s.con_grp[c] = s.con_grp[s.grp_lead[c]];
+  for (int c = lane; c < ncon; c += 32) s.cs.g.grp[c] = s.cs.g.grp[s.cs.g.lead[c]];
   __syncwarp();
   for (int g = lane; g < ngroup; g += 32) {
     unsigned long long m = 0ull;
     for (int c = 0; c < ncon; c++)
-      if (s.con_grp[c] == g) m |= 1ull << c;
+      if (s.cs.g.grp[c] == g) m |= 1ull << c;
     s.grp_mask[g] = m;
   }
   if (lane == 0) s.ngroup = ngroup;
@@ -1028,23 +1073,30 @@ __device__ __noinline__ void contact_jv(World& s, int lane) {
     // the relative velocity at the contact point: v_O + w x (pos - O); frame row d: row . that
     cross(dV, s.con_pos[c], u);
     for (int k = 0; k < 3; k++) u[k] += dV[3 + k];
-    for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(s.con_fr[c] + 3 * d, u);
+    float fr[9];
+    frame_rows(s, c, fr);
+    for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(fr + 3 * d, u);
   }
   __syncwarp();
 }
 
-// J v of every row into out (contact rows from cs.jd, limit rows from v)
-__device__ __noinline__ void rows_jv(World& s, const float* v, float* out, int lane) {
+// J v of every row into registers: row r = lane + 32 t into o[t], 0 past the row count (contact rows from cs.jd,
+// limit rows from v)
+__device__ __forceinline__ void rows_jv(World& s, const float* v, float (&o)[ROWS_PER_LANE], int lane) {
   body_motion(s, v, lane);
   contact_jv(s, lane);
   const int nefc = s.nefc;
-  for (int r = lane; r < nefc; r += 32) {
-    const int kind = s.efc_kind[r], a = s.efc_a[r], b = s.efc_b[r];
-    float val;
-    if (kind == ROW_LIMIT) val = b * v[a];
-    else if (kind == ROW_PYRAMID) val = s.cs.jd[a][0] + ((b & 1) ? -1.f : 1.f) * s.con_mu[a] * s.cs.jd[a][1 + (b >> 1)];
-    else val = s.cs.jd[a][0];
-    out[r] = val;
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++) {
+    const int r = lane + 32 * t;
+    float val = 0.f;
+    if (r < nefc) {
+      const int kind = s.efc_kind[r], a = s.efc_a[r], b = s.efc_b[r];
+      if (kind == ROW_LIMIT) val = b * v[a];
+      else if (kind == ROW_PYRAMID) val = s.cs.jd[a][0] + ((b & 1) ? -1.f : 1.f) * s.con_mu[a] * s.cs.jd[a][1 + (b >> 1)];
+      else val = s.cs.jd[a][0];
+    }
+    o[t] = val;
   }
   __syncwarp();
 }
@@ -1096,7 +1148,7 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
       s.efc_kind[r] = ROW_LIMIT; s.efc_a[r] = (short)i; s.efc_b[r] = (signed char)sg;
       s.lim_row[i] = (short)r;
       s.efc_D[r] = 1.f / R;
-      s.efc_aref[r] = -b * (sg * s.qvel[i]) - k * imp * pos;
+      s.efc_jar[r] = -b * (sg * s.qvel[i]) - k * imp * pos;  // aref until newton_begin
     }
     nlim += __popc(bal);
   }
@@ -1119,7 +1171,7 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
     }
     const int first = r0 + incl - want;
     if (valid) {
-      const int nr = max(0, min(want, NEFC - first));
+      const int nr = max(0, min(want, WROWS - first));
       s.con_row0[c] = (unsigned char)min(first, 255);
       s.con_nrow[c] = (unsigned char)nr;
       const float mu = s.con_mu[c];
@@ -1141,36 +1193,35 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
         s.efc_a[r] = (short)c;
         s.efc_b[r] = (signed char)t;
         s.efc_D[r] = D;
-        s.efc_aref[r] = -b * vel - k * imp * dist;
+        s.efc_jar[r] = -b * vel - k * imp * dist;  // aref until newton_begin
       }
     }
     r0 += __shfl_sync(FULL, incl, 31);
   }
   if (lane == 0) {
     s.nlim = nlim;
-    s.nefc = min(r0, NEFC);
-    if (r0 > NEFC) s.unsup |= ROW_OVERFLOW;
+    s.nefc = min(r0, WROWS);
+    if (r0 > WROWS) s.unsup |= ROW_OVERFLOW;
   }
   __syncwarp();
 }
 
 // ---- Newton solver -------------------------------------------------------------------------------------------------
-// Ma = M a and jar = J a - aref at the current qacc
-__device__ __noinline__ void refresh(World& s, int lane) {
-  matvec(s.M, s.qacc, s.Ma, lane);
-  rows_jv(s, s.qacc, s.efc_jar, lane);
-  for (int r = lane; r < s.nefc; r += 32) s.efc_jar[r] -= s.efc_aref[r];
-  __syncwarp();
+// The constrained acceleration a minimises c(a) = 1/2 (a - a0)' M (a - a0) + sum_r s_r(J_r a - aref_r) with a0 =
+// qacc_smooth and s_r(x) = 1/2 D_r x^2 for x < 0 (the row's quadratic zone), 0 else: MuJoCo's primal Newton method on
+// the pyramidal cone (reference g1_engine/step.py:1969-2137). Its Gauss term's lane-wise part, 1/2 (M a - qfrc_smooth)
+// (a - a0) (M a0 = qfrc_smooth), for a dof pair in matvec's layout; the rows' part for the lane's rows.
+__device__ __forceinline__ float gauss_part(const World& s, float2 ma, float2 a, int lane) {
+  float g = 0.5f * (ma.x - s.qsm[lane]) * (a.x - s.qacc0[lane]);
+  if (lane < NT) g += 0.5f * (ma.y - s.qsm[32 + lane]) * (a.y - s.qacc0[32 + lane]);
+  return g;
 }
-
-__device__ __noinline__ float total_cost(World& s, int lane) {
+__device__ __forceinline__ float rows_part(const float (&x)[ROWS_PER_LANE], const float (&D)[ROWS_PER_LANE]) {
   float g = 0.f;
-  for (int i = lane; i < NV; i += 32) g += 0.5f * (s.Ma[i] - s.qsm[i]) * (s.qacc[i] - s.qacc0[i]);
-  for (int r = lane; r < s.nefc; r += 32) {
-    const float x = s.efc_jar[r];
-    if (x < 0.f) g += 0.5f * s.efc_D[r] * x * x;
-  }
-  return warp_sum(g);
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++)
+    if (x[t] < 0.f) g += 0.5f * D[t] * x[t] * x[t];
+  return g;
 }
 
 // grad = M qacc - qfrc_smooth - J' f with f = -D jar on the active rows; returns |grad|. J' f: each contact's
@@ -1189,9 +1240,10 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
     }
     const float mu = s.con_mu[c];
     const float F[3] = {f[0] + f[1] + f[2] + f[3], mu * (f[0] - f[1]), mu * (f[2] - f[3])};
-    float w[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float w[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, fr[9];
+    frame_rows(s, c, fr);
     for (int d = 0; d < 3; d++)
-      for (int k = 0; k < 3; k++) w[3 + k] += F[d] * s.con_fr[c][3 * d + k];
+      for (int k = 0; k < 3; k++) w[3 + k] += F[d] * fr[3 * d + k];
     cross(s.con_pos[c], w + 3, w);  // moment about O: (pos - O) x force
     for (int k = 0; k < 6; k++) s.cs.wr[c][k] = w[k];
   }
@@ -1328,7 +1380,8 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       const int r = s.con_row0[c] + t;
       if (!(s.efc_jar[r] < 0.f)) continue;
       const float D = s.efc_D[r], mu = ((t & 1) ? -1.f : 1.f) * s.con_mu[c];
-      const float* f = s.con_fr[c];
+      float f[9];
+      frame_rows(s, c, f);
       const int k = 3 + 3 * (t >> 1);
       const float u[3] = {f[0] + mu * f[k], f[1] + mu * f[k + 1], f[2] + mu * f[k + 2]};
       float a[6];
@@ -1349,7 +1402,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     kred_level<6, 4>(v, lane);
     kred_level<3, 2>(v, lane);
     kred_level<2, 1>(v, lane);
-    if (kslot >= 0) s.u.hs.K[kslot] = v[0];
+    if (kslot >= 0) s.hs.K[kslot] = v[0];
     __syncwarp();
     const int lead = __ffsll((long long)gm) - 1;
     unsigned long long m1, m2;
@@ -1368,7 +1421,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
       if (k < nsup) {
         const int i = k < nlo ? (int)__fns(slo, 0, k + 1) : 32 + (int)__fns(shi, 0, k - nlo + 1);
         const float sg = ((m2 >> i) & 1ull) ? 1.f : -1.f;
-        const float* K = s.u.hs.K;
+        const float* K = s.hs.K;
         const float v[6] = {sg * s.dw[i][0], sg * s.dw[i][1], sg * s.dw[i][2], sg * s.dv[i][0], sg * s.dv[i][1],
                             sg * s.dv[i][2]};
         // K rows from the packed upper triangle
@@ -1383,8 +1436,8 @@ __device__ __noinline__ void hessian(World& s, int lane) {
           }
           P[r] = acc;
         }
-        for (int r = 0; r < 6; r++) s.u.hs.P[k][r] = P[r];
-        s.u.hs.dof[k] = (unsigned char)i;
+        for (int r = 0; r < 6; r++) s.hs.P[k][r] = P[r];
+        s.hs.dof[k] = (unsigned char)i;
       }
     }
     __syncwarp();
@@ -1397,9 +1450,9 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     for (int e = lane; e < npair; e += 32) {
       const unsigned ab = __ldg(g_pair_ab.ab + e);
       const int a = ab & 255u, b = ab >> 8;
-      const int da = s.u.hs.dof[a], db = s.u.hs.dof[b];
+      const int da = s.hs.dof[a], db = s.hs.dof[b];
       const float sa = ((m2 >> da) & 1ull) ? 1.f : -1.f;
-      const float* P = s.u.hs.P[b];
+      const float* P = s.hs.P[b];
       const float v = sa * (s.dw[da][0] * P[0] + s.dw[da][1] * P[1] + s.dw[da][2] * P[2] + s.dv[da][0] * P[3]
                             + s.dv[da][1] * P[4] + s.dv[da][2] * P[5]);
       s.L[TRI(da, db)] += v;
@@ -1413,30 +1466,99 @@ __device__ __noinline__ void hessian(World& s, int lane) {
 #endif
 }
 
-// Newton from the warm start (or qacc_smooth when that costs less): newton_begin picks the start and forms the
-// gradient; newton_iter runs one iteration (Hessian and factor unless no row changed its zone, solve, exact line
-// search, update, gradient, stopping test). The state between iterations (cost, count, converged, same zones) lives
+// The Newton start: of the two candidates, the warm start (qacc on entry) and a0 itself, the one with the lower cost
+// (a tie takes a0); then its gradient. The rows' aref, left in efc_jar by make_rows, becomes J a - aref there. Then
+// newton_iter runs one iteration at a time (Hessian and factor unless no row changed its zone, solve, exact line
+// search, update, gradient, stopping test); the state between iterations (cost, count, converged, same zones) lives
 // in the world record, so the caller can run the iterations of several worlds in lockstep.
 __device__ __noinline__ void newton_begin(World& s, int lane) {
+  // (values live across the calls below are kept few: what a call must preserve goes to the stack)
+  const int nefc = uni(s.nefc);
+  float x[ROWS_PER_LANE];
+  auto minus_aref = [&]() {  // x = J a - aref, 0 past the rows
+#pragma unroll
+    for (int t = 0; t < ROWS_PER_LANE; t++) x[t] = lane + 32 * t < nefc ? x[t] - s.efc_jar[lane + 32 * t] : 0.f;
+  };
+  auto rows_cost = [&]() {
+    float g = 0.f;
+#pragma unroll
+    for (int t = 0; t < ROWS_PER_LANE; t++) {
+      const float D = lane + 32 * t < nefc ? s.efc_D[lane + 32 * t] : 0.f;
+      if (x[t] < 0.f) g += 0.5f * D * x[t] * x[t];
+    }
+    return g;
+  };
+  // the warm start: its rows' J a - aref parked in L (free until the first Hessian)
+  const float2 mw = matvec(s.M, s.qacc, lane);
+  rows_jv(s, s.qacc, x, lane);
+  minus_aref();
+  const float cost_w = warp_sum(gauss_part(s, mw, lanes_of(s.qacc, lane), lane) + rows_cost());
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++) s.L[lane + 32 * t] = x[t];
+  // a0: its Gauss term is 0 (a - a0 = 0); its M a0 is needed only when a0 is kept
+  rows_jv(s, s.qacc0, x, lane);
+  minus_aref();
+  const float cost_0 = warp_sum(rows_cost());
+  const bool warm = uall(cost_0 > cost_w);
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++)
+    if (lane + 32 * t < nefc) s.efc_jar[lane + 32 * t] = warm ? s.L[lane + 32 * t] : x[t];
+  if (!warm) store_lanes(s.qacc, lanes_of(s.qacc0, lane), lane);
+  __syncwarp();
+  store_lanes(s.Ma, warm ? mw : matvec(s.M, s.qacc0, lane), lane);
   if (lane == 0) { s.nls = 0; s.nfact = 0; }
-  refresh(s, lane);
-  float cost = total_cost(s, lane);
-  // keep the warm start's qacc, Ma, jar in tmp / p / jv in case it stays the start
-  for (int i = lane; i < NV; i += 32) { s.tmp[i] = s.qacc[i]; s.qacc[i] = s.qacc0[i]; s.p[i] = s.Ma[i]; }
-  for (int r = lane; r < s.nefc; r += 32) s.efc_jv[r] = s.efc_jar[r];
   __syncwarp();
-  refresh(s, lane);
-  const float cost0 = total_cost(s, lane);
-  if (uall(cost0 > cost)) {
-    for (int i = lane; i < NV; i += 32) { s.qacc[i] = s.tmp[i]; s.Ma[i] = s.p[i]; }
-    for (int r = lane; r < s.nefc; r += 32) s.efc_jar[r] = s.efc_jv[r];
-    __syncwarp();
-  } else {
-    cost = cost0;
-  }
   newton_grad(s, lane, 0.f);
-  if (lane == 0) { s.ncost = cost; s.nit_cur = 0; s.ndone = 0; s.nsame = 0; }
+  if (lane == 0) { s.ncost = warm ? cost_w : cost_0; s.nit_cur = 0; s.ndone = 0; s.nsame = 0; }
   __syncwarp();
+}
+
+// The exact line search along the Newton direction p. On the ray a + alpha p the cost is a convex piecewise quadratic
+// f(alpha) with slope f'(alpha) = a1 + alpha a2 + sum_{x_r + alpha j_r < 0} D_r j_r (x_r + alpha j_r) and curvature
+// f''(alpha) = a2 + sum_{same rows} D_r j_r^2 (a1 = (M a - qfrc_smooth) . p, a2 = p' M p; x_r = J_r a - aref_r,
+// j_r = J_r p). It is minimised by 1-D Newton steps kept inside a bracket of the minimiser, with the stopping rules
+// of MuJoCo's exact line search as the reference applies them (reference g1_engine/step.py:2032-2084): no descent at
+// alpha = 0; the slope below 1e-7 of its value at 0; a Newton step that stayed on its quadratic piece (the rows'
+// zones the same at the new point: that point is the piece's, so the ray's, minimiser, found without evaluating the
+// slope there); at most 40 slope evaluations. A Newton step outside the bracket is replaced by its midpoint, or by a
+// doubling while no upper end is known.
+struct LineSearchResult { float alpha; int evals; };
+__device__ __forceinline__ LineSearchResult exact_line_search(const float (&x)[ROWS_PER_LANE],
+                                                              const float (&j)[ROWS_PER_LANE],
+                                                              const float (&D)[ROWS_PER_LANE], float a1, float a2) {
+  float Dj[ROWS_PER_LANE], Djj[ROWS_PER_LANE];
+#pragma unroll
+  for (int t = 0; t < ROWS_PER_LANE; t++) { Dj[t] = D[t] * j[t]; Djj[t] = Dj[t] * j[t]; }
+  float alpha = 0.f, below = 0.f, above = 1e30f, slope0 = 0.f;
+  unsigned zones_before = 0u;  // this lane's rows in the quadratic zone at the previous trial point (bit t)
+  bool newton_step = false;    // the step to the current point was a Newton step inside the bracket
+  int evals = 0;
+  while (true) {
+    unsigned zones = 0u;
+    float fd = 0.f, fdd = 0.f;
+#pragma unroll
+    for (int t = 0; t < ROWS_PER_LANE; t++) {
+      const float xt = x[t] + alpha * j[t];
+      if (xt < 0.f) { zones |= 1u << t; fd += Dj[t] * xt; fdd += Djj[t]; }
+    }
+    if (__all_sync(FULL, newton_step && zones == zones_before)) break;  // landed on the piece's minimiser
+    if (evals == 40) break;
+    evals++;
+    fd = warp_sum(fd) + a1 + alpha * a2;
+    fdd = warp_sum(fdd) + a2;
+    if (evals == 1) {
+      slope0 = fd;
+      if (uall(slope0 >= 0.f)) break;  // p is no descent direction: stay at alpha = 0
+    }
+    if (uall(fabsf(fd) <= 1e-7f * fabsf(slope0))) break;
+    if (fd < 0.f) below = alpha; else above = alpha;
+    float next = alpha - fd / fdd;
+    newton_step = next > below && next < above;
+    if (!newton_step) next = above < 1e29f ? 0.5f * (below + above) : 2.f * fmaxf(alpha, 1e-6f);
+    zones_before = zones;
+    alpha = next;
+  }
+  return {alpha, evals};
 }
 
 __device__ __noinline__ void newton_iter(World& s, int lane) {
@@ -1454,62 +1576,32 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
   __syncwarp();
   chol_solve(s.L, s.dinv, s.p, lane);
   PROF(s, 9);
-  // exact line search along p: the cost is piecewise quadratic in alpha
-  rows_jv(s, s.p, s.efc_jv, lane);
-  matvec(s.M, s.p, s.Mp, lane);
-  float a1 = 0.f, a2 = 0.f;
-  for (int i = lane; i < NV; i += 32) { a1 += (s.Ma[i] - s.qsm[i]) * s.p[i]; a2 += s.p[i] * s.Mp[i]; }
-  a1 = warp_sum(a1);
-  a2 = warp_sum(a2);
   const int nefc = uni(s.nefc);
-  // per row: jar, J p, D J p and D (J p)^2 (the row's slope and curvature factors along p)
-  float rx[ROWS_PER_LANE], rj[ROWS_PER_LANE], rD[ROWS_PER_LANE], rdj[ROWS_PER_LANE], rdjj[ROWS_PER_LANE];
+  const float2 mp = matvec(s.M, s.p, lane);
+  float x[ROWS_PER_LANE], jp[ROWS_PER_LANE], D[ROWS_PER_LANE];
+  rows_jv(s, s.p, jp, lane);
 #pragma unroll
   for (int t = 0; t < ROWS_PER_LANE; t++) {
     const int r = lane + 32 * t;
-    const bool v = r < nefc;
-    rx[t] = v ? s.efc_jar[r] : 0.f;
-    rj[t] = v ? s.efc_jv[r] : 0.f;
-    rD[t] = v ? s.efc_D[r] : 0.f;
-    rdj[t] = rD[t] * rj[t];
-    rdjj[t] = rdj[t] * rj[t];
+    x[t] = r < nefc ? s.efc_jar[r] : 0.f;
+    D[t] = r < nefc ? s.efc_D[r] : 0.f;
   }
-  float alpha = 0.f, lo = 0.f, hi = 1e30f, d0 = 0.f;
-  unsigned zprev = 0u;
-  bool nwt = false;
-  int nls = 0;
-  for (int k = 0; k <= 40; k++) {
-    PROF_COUNT(17, 1);
-    float fd = 0.f, fdd = 0.f;
-    unsigned z = 0u;
-#pragma unroll
-    for (int t = 0; t < ROWS_PER_LANE; t++) {
-      const float x = rx[t] + alpha * rj[t];
-      if (x < 0.f) { z |= 1u << t; fd += rdj[t] * x; fdd += rdjj[t]; }
-    }
-    if (__all_sync(FULL, nwt && z == zprev)) break;  // the Newton step kept every row on its piece: exact minimum
-    if (k == 40) break;
-    nls++;
-    fd = warp_sum(fd) + a1 + alpha * a2;
-    fdd = warp_sum(fdd) + a2;
-    if (k == 0) { d0 = fd; if (uall(d0 >= 0.f)) break; }
-    if (uall(fabsf(fd) <= 1e-7f * fabsf(d0))) break;
-    if (fd < 0.f) lo = alpha; else hi = alpha;
-    float nx = alpha - fd / fdd;
-    nwt = nx > lo && nx < hi;
-    if (!nwt) nx = hi < 1e29f ? 0.5f * (lo + hi) : 2.f * fmaxf(alpha, 1e-6f);
-    zprev = z;
-    alpha = nx;
-  }
-  if (lane == 0) s.nls += nls;
-  // move along p; the new cost (0.5 (Ma - qsm)(qacc - qacc_smooth) + the rows' costs) is summed with |grad|
-  float cpart = 0.f;
-  for (int i = lane; i < NV; i += 32) {
-    const float qa = s.qacc[i] + alpha * s.p[i], ma = s.Ma[i] + alpha * s.Mp[i];
-    s.qacc[i] = qa;
-    s.Ma[i] = ma;
-    cpart += 0.5f * (ma - s.qsm[i]) * (qa - s.qacc0[i]);
-  }
+  const float2 p = lanes_of(s.p, lane), ma = lanes_of(s.Ma, lane);
+  float a1 = (ma.x - s.qsm[lane]) * p.x, a2 = p.x * mp.x;
+  if (lane < NT) { a1 += (ma.y - s.qsm[32 + lane]) * p.y; a2 += p.y * mp.y; }
+  a1 = warp_sum(a1);
+  a2 = warp_sum(a2);
+  const LineSearchResult ls = exact_line_search(x, jp, D, a1, a2);
+  const float alpha = ls.alpha;
+  if (lane == 0) s.nls += ls.evals;
+  PROF_COUNT(17, ls.evals);
+  // the step: a, M a and the rows' J a - aref are linear in alpha; the new cost is summed with |grad|
+  float2 a = lanes_of(s.qacc, lane);
+  a.x += alpha * p.x; a.y += alpha * p.y;
+  const float2 man = make_float2(ma.x + alpha * mp.x, ma.y + alpha * mp.y);
+  store_lanes(s.qacc, a, lane);
+  store_lanes(s.Ma, man, lane);
+  float cpart = gauss_part(s, man, a, lane);
   bool chg = false;
 #ifdef NB_PROFILE
   int nchg = 0;  // rows changing zone (profile builds: a histogram of them)
@@ -1517,12 +1609,12 @@ __device__ __noinline__ void newton_iter(World& s, int lane) {
 #pragma unroll
   for (int t = 0; t < ROWS_PER_LANE; t++) {
     const int r = lane + 32 * t;
-    const float xn = rx[t] + alpha * rj[t];
-    chg |= (xn < 0.f) != (rx[t] < 0.f);
+    const float xn = x[t] + alpha * jp[t];
+    chg |= (xn < 0.f) != (x[t] < 0.f);
 #ifdef NB_PROFILE
-    nchg += r < nefc && (xn < 0.f) != (rx[t] < 0.f);
+    nchg += r < nefc && (xn < 0.f) != (x[t] < 0.f);
 #endif
-    if (xn < 0.f) cpart += 0.5f * rD[t] * xn * xn;
+    if (xn < 0.f) cpart += 0.5f * D[t] * xn * xn;
     if (r < nefc) s.efc_jar[r] = xn;
   }
   const bool same_zones = !__any_sync(FULL, chg);
@@ -1633,15 +1725,16 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
     stats[4] = s.nfact; stats[5] = s.ncand; stats[6] = s.ncon_raw; stats[7] = 0;
   }
   // implicitfast: (M + h kv) a_adv = M qacc; qvel += h a_adv; qpos integrated with the new qvel
-  for (int i = lane; i < NV; i += 32) s.tmp[i] = s.Ma[i];
+  for (int i = lane; i < NV; i += 32) s.p[i] = s.Ma[i];
+  __syncwarp();
   tb_factor(s.M, true, s.L, s.dinv, lane);
-  chol_solve<true>(s.L, s.dinv, s.tmp, lane);
+  chol_solve<true>(s.L, s.dinv, s.p, lane);
   if (rec) {
     for (int e = lane; e < NTB; e += 32) __stcs(rec + T_LQ + e, s.L[g_tb_index.e[e]]);
     tape_put(rec + T_DINVQ, s.dinv, NV, lane);
-    tape_put(rec + T_AADV, s.tmp, NV, lane);
+    tape_put(rec + T_AADV, s.p, NV, lane);
   }
-  for (int i = lane; i < NV; i += 32) s.qvel[i] += h * s.tmp[i];
+  for (int i = lane; i < NV; i += 32) s.qvel[i] += h * s.p[i];
   __syncwarp();
   if (lane == 0) {
     s.nit = it;

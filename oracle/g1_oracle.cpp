@@ -647,7 +647,7 @@ template <class T> int substep(World<T>& w, int iterations, T tol, int* stats) {
 template <class T>
 void step_world(int iw, const double* qpos, const double* qvel, const double* warm, const double* ctrl,
                 const double* fric, const double* com, int iterations, int nsub, double tol, double* oq, double* ov,
-                double* ow, int* info, int* stats) {
+                double* ow, int* info, int* stats, double* ocon) {
   World<T>* w = new World<T>();
   T c[NU];
   for (int i = 0; i < NQ; i++) w->qpos[i] = T(qpos[(size_t)iw * NQ + i]);
@@ -665,6 +665,14 @@ void step_world(int iw, const double* qpos, const double* qvel, const double* wa
   info[4 * iw + 1] = w->ncon_raw;
   info[4 * iw + 2] = w->nrow;
   info[4 * iw + 3] = w->unsupported;
+  if (ocon)  // the last substep's kept contacts as (pair, slot, dist), pair -1 past the count
+    for (int c = 0; c < MAXCON; c++) {
+      double* o = ocon + ((size_t)iw * MAXCON + c) * 3;
+      const bool v = c < (int)w->con.size();
+      o[0] = v ? w->con[c].pair : -1.0;
+      o[1] = v ? w->con[c].slot : 0.0;
+      o[2] = v ? double(w->con[c].dist) : 0.0;
+    }
   delete w;
 }
 
@@ -676,17 +684,18 @@ extern "C" {
 // reference's algorithm, Newton capped at `iterations` with tolerance `tol` (the model's 1e-8 by default).
 // precision: 64 float64 arithmetic, 32 float32. nthreads: OpenMP threads (0: all).
 // stats: NULL or (nw, nsub, 4) int32 per substep: contacts kept, constraint rows, Newton iterations, line-search
-// evaluations (the inputs of the FLOP count of a step)
+// evaluations (the inputs of the FLOP count of a step); ocon: NULL or (nw, 64, 3) float64, the last substep's kept
+// contacts as (pair, slot, dist) in contact order, pair -1 past the count
 int g1_oracle_step(int nw, const double* qpos, const double* qvel, const double* warm, const double* ctrl,
                    const double* fric, const double* com, int iterations, int nsub, double tol, int precision,
-                   int nthreads, double* oq, double* ov, double* ow, int* info, int* stats) {
+                   int nthreads, double* oq, double* ov, double* ow, int* info, int* stats, double* ocon) {
   if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return 1;
 #pragma omp parallel for schedule(dynamic, 4) num_threads(nthreads > 0 ? nthreads : omp_get_max_threads())
   for (int w = 0; w < nw; w++) {
     if (precision == 32)
-      step_world<float>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info, stats);
+      step_world<float>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info, stats, ocon);
     else
-      step_world<double>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info, stats);
+      step_world<double>(w, qpos, qvel, warm, ctrl, fric, com, iterations, nsub, tol, oq, ov, ow, info, stats, ocon);
   }
   return 0;
 }

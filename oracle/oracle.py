@@ -31,7 +31,7 @@ def lib():
             build()
         _lib = ctypes.CDLL(str(LIB))
         d, i = ctypes.c_void_p, ctypes.c_int
-        _lib.g1_oracle_step.argtypes = [i, d, d, d, d, d, d, i, i, ctypes.c_double, i, i, d, d, d, d, d]
+        _lib.g1_oracle_step.argtypes = [i, d, d, d, d, d, d, i, i, ctypes.c_double, i, i, d, d, d, d, d, d]
         _lib.g1_oracle_step.restype = i
         _lib.g1_oracle_matrices.argtypes = [i] + [d] * 10
         _lib.g1_oracle_matrices.restype = i
@@ -44,21 +44,23 @@ def _c(x, shape):
 
 
 def step(qpos, qvel, warm, ctrl, friction, com, iterations=10, substeps=4, tol=1e-8, precision=64, threads=0,
-         stats=False):
+         stats=False, contacts=False):
     """(qpos', qvel', warm', info (B, 4) int32) of one control step, as float64 arrays; stats=True appends the
-    per-substep counts (B, substeps, 4): contacts kept, rows, Newton iterations, line-search evaluations."""
+    per-substep counts (B, substeps, 4): contacts kept, rows, Newton iterations, line-search evaluations;
+    contacts=True appends the last substep's kept contacts (B, 64, 3) as (pair, slot, dist), pair -1 past the count."""
     B = np.asarray(qpos).shape[0]
     args = [_c(qpos, (B, NQ)), _c(qvel, (B, NV)), _c(warm, (B, NV)), _c(ctrl, (B, NU)), _c(friction, (B,)),
             _c(com, (B, 3))]
     oq, ov, ow = np.zeros((B, NQ)), np.zeros((B, NV)), np.zeros((B, NV))
     info = np.zeros((B, 4), np.int32)
     st = np.zeros((B, int(substeps), 4), np.int32) if stats else None
+    con = np.zeros((B, 64, 3)) if contacts else None
     p = lambda a: None if a is None else a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
     rc = lib().g1_oracle_step(B, *map(p, args), int(iterations), int(substeps), float(tol), int(precision),
-                              int(threads), p(oq), p(ov), p(ow), p(info), p(st))
+                              int(threads), p(oq), p(ov), p(ow), p(info), p(st), p(con))
     if rc:
         raise ValueError(f"g1_oracle_step failed ({rc})")
-    return (oq, ov, ow, info, st) if stats else (oq, ov, ow, info)
+    return (oq, ov, ow, info) + ((st,) if stats else ()) + ((con,) if contacts else ())
 
 
 def matrices(qpos, qvel, qacc, ctrl, friction, com):

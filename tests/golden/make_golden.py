@@ -13,6 +13,9 @@ The outputs are small subsets of the reference's Apache-2.0 benchmark data (benc
                    pos[3], normal[3]): pins the body poses of the kinematics outputs
   truth_jac.npz    16 of mf_s0's Jacobian states (the G0 sample): inputs, the MuJoCo C float64 FD Jacobian (71 x 99,
                    stored float32 by the reference, h = 1e-6, tangent columns), its per-column floor, validity bits
+  corpus_mf_s0.npz the whole mf_s0 corpus the reference's published timings run on (4096 states): the step inputs,
+                   the stored cotangent 0 (its fwd+grad and backward legs use it) and the MuJoCo C labels of the
+                   state's heaviest substep (contacts, rows, solver iterations)
 
 Existing files are kept unless --force is given (each is written once; the tests pin their contents).
 
@@ -35,6 +38,13 @@ def main():
     ref = Path(a.ref)
     data = ref / "benchmarks" / "data"
     write = lambda name: a.force or not (HERE / name).exists()  # noqa: E731
+    if write("corpus_mf_s0.npz"):
+        c = np.load(data / "mf_s0.npz")
+        corp = {k: c[k] for k in INPUTS}
+        corp.update(cot_qpos=c["cot_qpos"][:, 0], cot_qvel=c["cot_qvel"][:, 0], ncon_max=c["label_ncon_max"],
+                    nefc_max=c["label_nefc_max"], niter_max=c["label_niter_max"])
+        np.savez_compressed(HERE / "corpus_mf_s0.npz", **corp)
+        print("corpus_mf_s0.npz", (HERE / "corpus_mf_s0.npz").stat().st_size, "bytes")
     if write("truth_jac.npz"):
         c, t = np.load(data / "mf_s0.npz"), np.load(data / "truth" / "mf_s0.npz")
         n = 16

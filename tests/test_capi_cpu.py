@@ -37,6 +37,17 @@ def test_forward_rejects_bad_arguments_without_launching():
     assert lib.nb_g1_forward(nul, 0, *[nul] * 6, 10, 4, *[nul] * 7) == 0  # no worlds: a no-op
 
 
+def test_small_entries_reject_bad_arguments_without_launching():
+    lib = capi.load()
+    nul = ctypes.c_void_p(0)
+    assert lib.nb_g1_last_forward(nul, -1, nul, nul, nul) == 1  # cudaErrorInvalidValue
+    assert lib.nb_g1_last_forward(nul, 4, nul, nul, nul) == 1   # no info / record
+    out = (ctypes.c_longlong * 8)(*range(1, 9))
+    rc = lib.nb_g1_launch(0, out)
+    if rc:  # no usable device here: an error code and a zeroed record
+        assert list(out) == [0] * 8
+
+
 def test_torch_api_type_errors_on_cpu_tensors():
     import torch
     s = {k: torch.from_numpy(v) for k, v in synthetic.states(2, 0).items()}

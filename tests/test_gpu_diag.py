@@ -51,3 +51,39 @@ def test_overflow_warning():
     from nablaengine_b200 import torch_ffi
     with pytest.warns(RuntimeWarning, match="contact capacity"):
         assert torch_ffi.warn_overflow({"fwd_contact_overflow_worlds": 2, "fwd_row_overflow_worlds": 0}) == 2
+
+
+def test_last_forward_record():
+    """The last-forward record (nb_g1_last_forward): worlds, contacts summed, the most contacts and rows of a world,
+    from the call's info; one record per batch size besides the latest (the reference's last_forward)."""
+    torch = _cuda()
+    from nablaengine_b200 import synthetic, torch_ffi
+    xs = {}
+    for B in (64, 32):
+        s = synthetic.config_states("vjp", B=B)
+        xs[B] = [torch.from_numpy(s[k]).cuda() for k in KEYS]
+    info = {B: torch_ffi.forward(*xs[B])[3].cpu().numpy() for B in (64, 32)}
+    want = {B: {"worlds": B, "contacts": int(i[:, 1].sum()), "max_contacts": int(i[:, 1].max()),
+                "max_rows": int(i[:, 2].max())} for B, i in info.items()}
+    assert torch_ffi.last_forward() == want[32]
+    assert torch_ffi.last_forward(32) == want[32]
+    assert torch_ffi.last_forward(64) == want[64]
+    assert torch_ffi.last_forward(5) == dict.fromkeys(torch_ffi.LAST, 0)
+
+
+def test_launch_info():
+    """nb_g1_launch: the kernels' shared memory and resident worlds (rows) per SM on this device."""
+    torch = _cuda()
+    import ctypes
+    from nablaengine_b200 import capi, torch_ffi
+    d = torch_ffi.launch_info(0)
+    props = torch.cuda.get_device_properties(0)
+    assert d["sms"] == props.multi_processor_count
+    assert d["forward_worlds_per_sm"] >= 10 and d["adjoint_worlds_per_sm"] >= 10 and d["jacobian_rows_per_sm"] >= 12
+    for k in ("forward_smem_bytes", "adjoint_smem_bytes", "jacobian_smem_bytes"):
+        assert 0 < d[k] <= 227 * 1024
+    out = (ctypes.c_longlong * 8)()
+    assert capi.load().nb_g1_launch(0, out) == 0
+    assert list(out[:7]) == [d[k] for k in ("forward_smem_bytes", "forward_worlds_per_sm", "adjoint_smem_bytes",
+                                            "adjoint_worlds_per_sm", "jacobian_smem_bytes", "jacobian_rows_per_sm",
+                                            "sms")]

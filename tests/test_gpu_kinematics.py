@@ -83,8 +83,7 @@ def test_step_kinematics_is_kinematics_of_the_output_and_differentiates():
     tape = torch_ffi.forward(*x, tape=True)[4]
     z = lambda *sh: torch.zeros(sh, device="cuda")  # noqa: E731
     cot = (z(32, 36), torch.ones(32, 31, 3, device="cuda"), z(32, 31, 4), 2 * out[6].detach(), z(32, 31, 3))
-    gq1, gv1 = torch_ffi._kinematics_backward_impl(q1, v1, x[5], cot, gq_in=z(32, 36),
-                                                   gv_in=torch.ones(32, 35, device="cuda"))
+    gq1, gv1 = torch_ffi.kinematics_backward(q1, v1, x[5], cot, z(32, 36), torch.ones(32, 35, device="cuda"))
     gq, _, _, _ = torch_ffi.backward(tape, x[4], x[5], gq1, gv1)
     err = (q.grad - gq).norm() / gq.norm()
     assert float(err) < 1e-5, float(err)

@@ -41,7 +41,7 @@ def test_fake_shapes():
     torch = _cuda()
     from torch._subclasses.fake_tensor import FakeTensorMode
     from nablaengine_b200 import torch_ffi
-    ops = torch_ffi._ops()
+    ops = torch_ffi.custom_ops()
     x = _x(4)
     with FakeTensorMode(allow_non_fake_inputs=True) as mode:
         fx = [mode.from_tensor(t) for t in x]
@@ -62,7 +62,7 @@ def test_backward_with_kinematics_cotangents():
     kc = (torch.zeros(B, 36, device="cuda"), torch.ones(B, 31, 3, device="cuda"), torch.zeros(B, 31, 4, device="cuda"),
           torch.zeros(B, 31, 6, device="cuda"), torch.zeros(B, 31, 3, device="cuda"))
     a = torch_ffi.backward(tape, x[4], x[5], gq, gv, kinematics=(q1, v1) + kc)
-    cq, cv = torch_ffi._kinematics_backward_impl(q1, v1, x[5], kc, gq_in=gq, gv_in=gv)
+    cq, cv = torch_ffi.kinematics_backward(q1, v1, x[5], kc, gq, gv)
     b = torch_ffi.backward(tape, x[4], x[5], cq, cv)
     for u, w in zip(a[:3], b[:3]):
         assert torch.equal(u, w)
@@ -82,8 +82,8 @@ def test_cuda_graph_of_forward_backward_jacobian_kinematics():
         g = torch_ffi.backward(tape, x[4], x[5], z(64, 36), 2 * v1)
         J, _ = torch_ffi.jacobian(tape, x[4], x[5])
         k = torch_ffi.kinematics(q1, v1, x[5])
-        kg = torch_ffi._kinematics_backward_impl(q1, v1, x[5], (z(64, 36), k[1], z(64, 31, 4), z(64, 31, 6),
-                                                                z(64, 31, 3)))
+        kg = torch_ffi.kinematics_backward(q1, v1, x[5], (z(64, 36), k[1], z(64, 31, 4), z(64, 31, 6),
+                                                          z(64, 31, 3)))
         return (q1, v1, w1, info) + tuple(g) + (J,) + tuple(k) + tuple(kg)
 
     ref = run()

@@ -53,6 +53,29 @@ def test_forward_noalloc_equals_forward_on_two_calls_in_a_row():
             assert np.array_equal(a, b), name  # bitwise: the same kernels on the same order
 
 
+def test_forward_noalloc_allocates_no_device_memory():
+    """A call with every buffer already in place leaves the device's free memory and torch's reserved memory as they
+    were (after a first call, which may load the kernels' code)."""
+    torch, lib, rec = _setup()
+    from nablaengine_b200 import synthetic
+    s = synthetic.config_states("forward", B=2048)
+    B = 2048
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda() for k in KEYS]
+    out = [torch.empty((B, 36), device="cuda"), torch.empty((B, 35), device="cuda"),
+           torch.empty((B, 35), device="cuda"), torch.empty((B, 4), dtype=torch.int32, device="cuda")]
+    p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    call = lambda: lib.nb_g1_forward_noalloc(st, B, *map(p, t), 10, 4, *map(p, out), None, None)  # noqa: E731
+    assert call() == 0
+    torch.cuda.synchronize()
+    free0, reserved0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_reserved()
+    for _ in range(3):
+        assert call() == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_reserved() == reserved0
+
+
 def test_forward_noalloc_rejects_more_worlds_than_its_buffer():
     torch, lib, _ = _setup()
     nul = ctypes.c_void_p(0)

@@ -4,7 +4,7 @@ library) in which lane 0 of every world adds the clock64() cycles of each phase 
 world's own elapsed time per phase (its warp shares the SM with nine others), so the table gives shares, not a
 kernel time. Needs a CUDA device.
 
-    python -m nablaengine_b200.phase_profile [--worlds 4096]
+    python -m nablaengine_b200.phase_profile [--worlds 4096] [--npz states.npz]
 """
 import argparse
 import ctypes
@@ -44,7 +44,16 @@ def _read(lib, n=32):
     return np.array(list(buf), np.float64)
 
 
-def run(worlds=4096):
+def _npz_states(path, worlds):
+    """Forward inputs from an .npz of states (keys qpos, qvel, warm or qacc_warmstart, ctrl, friction, com)."""
+    with np.load(path) as z:
+        warm = "warm" if "warm" in z.files else "qacc_warmstart"
+        s = {k: np.ascontiguousarray(z[w][:worlds]) for k, w in zip(KEYS, ("qpos", "qvel", warm, "ctrl",
+                                                                           "friction", "com"))}
+    return s
+
+
+def run(worlds=4096, npz=None):
     import torch
     lib = _load()
     if lib.nb_g1_upload(None, None):
@@ -53,8 +62,8 @@ def run(worlds=4096):
     lib.nb_g1_sizes(sizes)
     p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    for cfg in ("forward", "vjp"):
-        s = synthetic.config_states(cfg, B=worlds)
+    for cfg in (("npz",) if npz else ()) + ("forward", "vjp"):
+        s = _npz_states(npz, worlds) if cfg == "npz" else synthetic.config_states(cfg, B=worlds)
         t = [torch.from_numpy(np.ascontiguousarray(s[k])).cuda() for k in KEYS]
         B = t[0].shape[0]
         out = [torch.empty((B, 36), device="cuda"), torch.empty((B, 35), device="cuda"),
@@ -70,7 +79,8 @@ def run(worlds=4096):
         v = _read(lib)
         ws = v[20]
         tot = sum(v[k] for k, _ in FWD)
-        print(f"== forward, configuration {'2' if cfg == 'forward' else '3'}, B = {B}: {tot / ws:.0f} cycles per "
+        what = {"npz": npz, "forward": "configuration 2", "vjp": "configuration 3"}[cfg]
+        print(f"== forward, {what}, B = {B}: {tot / ws:.0f} cycles per "
               f"world-substep; {v[16] / ws:.2f} Newton iterations, {v[17] / max(v[16], 1):.2f} line-search "
               f"evaluations per iteration, {v[18] / ws:.1f} contacts, {v[19] / ws:.1f} rows per world-substep")
         for k, name in FWD:
@@ -94,7 +104,9 @@ def run(worlds=4096):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--worlds", type=int, default=4096)
-    run(ap.parse_args(argv).worlds)
+    ap.add_argument("--npz", default=None, help="also profile the forward on these states (e.g. a corpus)")
+    a = ap.parse_args(argv)
+    run(a.worlds, a.npz)
 
 
 if __name__ == "__main__":

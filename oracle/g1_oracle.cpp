@@ -69,6 +69,34 @@ template <class T> struct Contact {
   V3<T> pos, frame[3];
 };
 
+// The adjoint's gradient modes other than the exact derivative (reference g1_engine/adjoint.py:38-57, the clamp
+// options DK_ADJ_CLAMP_KV; g1_engine/adjoint_contact.py:76-90, the self-contact normal option DK_ADJ_NORMAL and the
+// near-parallel capsule rule DK_ADJ_PARALLEL) are exact derivatives of a surrogate step that holds some quantities at
+// their values on the base trajectory (the unperturbed step); central differences of the surrogate around the base
+// state therefore check them. Per substep of the base trajectory, ModeBase keeps: the dofs whose actuator force is
+// clamped, their input velocity and unclamped PD force, and for every contact of the sphere core (sphere-sphere,
+// sphere-capsule, capsule-capsule) its normal, centre distance nu and segment parameters. The surrogate:
+//  - clamp_kv 1 (exact): a clamped dof's force is its bound; 0: the bound minus kv (v - v_base) (the damping
+//    derivative kept); 2: the bound plus w (f - f_base), w = exp(-max((|f_base| - lim) / lim, 0) / soft) (soft <= 0:
+//    w = 0), f the unclamped PD force;
+//  - normal 0: exact; otherwise the core's normal is n_base + s (n - n_base), s = 0 (1: frozen), nu_base /
+//    max(nu_base, 1e-3) (2), nu_base < 1e-3 ? 0 : 1 (3), with the contact point and frame built from it; and a
+//    capsule-capsule contact with both segment parameters free on axes with sin^2 < 1.2e-3 keeps the base's
+//    parameters.
+struct ModeContact { int pair, slot; double n[3], nu, x1, x2; bool hold; };
+struct ModeBase {
+  unsigned long long clamp = 0;
+  double v[NV] = {}, f[NV] = {};
+  std::vector<ModeContact> con;
+};
+struct Mode {
+  int clamp_kv = 1, normal = 0;
+  double soft = 0;
+  bool record = false;        // the base pass: fill base[k]; else apply the surrogate with base[k]
+  ModeBase* base = nullptr;   // (nsub)
+  int k = 0;                  // the current substep
+};
+
 // one world's working state for one substep
 template <class T> struct World {
   // inputs / state
@@ -88,6 +116,7 @@ template <class T> struct World {
   int nrow;
   T J[NEFC][NV], D[NEFC], aref[NEFC];
   int unsupported;
+  Mode* mode = nullptr;  // a gradient mode's base pass or surrogate (test infrastructure), or none
 };
 
 template <class T> bool is_ancestor_dof(int dof, int body) {  // dof belongs to body or to one of its ancestors
@@ -213,9 +242,31 @@ template <class T> void dynamics(World<T>& w) {
   for (int i = 0; i < NV; i++) {
     T act = 0;
     if (i >= 6) {
-      act = T(g1_dof_kp[i]) * (w.ctrl[i - 6] - w.qpos[i + 1]) - T(g1_dof_kv[i]) * w.qvel[i];
-      T lim = T(g1_dof_frclim[i]);
-      act = std::min(std::max(act, -lim), lim);
+      const T f = T(g1_dof_kp[i]) * (w.ctrl[i - 6] - w.qpos[i + 1]) - T(g1_dof_kv[i]) * w.qvel[i];
+      const T lim = T(g1_dof_frclim[i]);
+      act = std::min(std::max(f, -lim), lim);
+      if (w.mode) {
+        ModeBase& b = w.mode->base[w.mode->k];
+        const unsigned long long bit = 1ull << i;
+        if (w.mode->record) {
+          b.v[i] = double(w.qvel[i]);
+          b.f[i] = double(f);
+          if (act <= -lim || act >= lim) b.clamp |= bit;
+        } else if (b.clamp & bit) {  // the base's clamp holds
+          const T bound = b.f[i] > 0 ? lim : -lim;
+          if (w.mode->clamp_kv == 0) {
+            act = bound - T(g1_dof_kv[i]) * (w.qvel[i] - T(b.v[i]));
+          } else if (w.mode->clamp_kv == 2) {
+            const double o = std::max((std::fabs(b.f[i]) - double(lim)) / double(lim), 0.0);
+            const T wt = w.mode->soft > 0 ? T(std::exp(-o / w.mode->soft)) : T(0);
+            act = bound + wt * (f - T(b.f[i]));
+          } else {
+            act = bound;
+          }
+        } else {
+          act = f;  // the base's unclamped zone holds
+        }
+      }
     }
     w.qfrc_smooth[i] = act - bias[i];
   }
@@ -281,7 +332,42 @@ template <class T> void sphere_sphere(const V3<T>& p1, T r1, const V3<T>& p2, T 
   *pos = p1 + (r1 + T(0.5) * *dist) * *n;
 }
 
-template <class T> void collide(int pair, const GeomPose<T>* gp, std::vector<Contact<T>>& out, int* unsup) {
+// A contact of the sphere core between the centres c1 = p1 + x1 a1 (radius r1) and c2 = p2 + x2 a2 (r2) of pair /
+// slot, pushed when dist < 0; returns dist. With a gradient mode (Mode, above): the base pass records the contact,
+// the surrogate pass holds what the mode holds. hold_ok: both segment parameters free on near-parallel axes.
+template <class T> T core_contact(std::vector<Contact<T>>& out, Mode* mode, int pair, int slot, const V3<T>& p1,
+                                  const V3<T>& a1, T x1, T r1, const V3<T>& p2, const V3<T>& a2, T x2, T r2,
+                                  bool hold_ok) {
+  const ModeContact* bc = nullptr;
+  if (mode && !mode->record)
+    for (const ModeContact& c : mode->base[mode->k].con)
+      if (c.pair == pair && c.slot == slot) { bc = &c; break; }
+  if (bc && bc->hold) { x1 = T(bc->x1); x2 = T(bc->x2); }
+  const V3<T> c1 = p1 + x1 * a1, c2 = p2 + x2 * a2;
+  T dist; V3<T> pos, n, fr[3];
+  sphere_sphere(c1, r1, c2, r2, &dist, &pos, &n);
+  if (bc && mode->normal != 0) {
+    const double nu = bc->nu;
+    const T sc = mode->normal == 1 ? T(0) : (mode->normal == 2 ? T(nu / std::max(nu, 1e-3)) : T(nu < 1e-3 ? 0 : 1));
+    const V3<T> n0 = v3(T(bc->n[0]), T(bc->n[1]), T(bc->n[2]));
+    n = n0 + sc * (n - n0);
+    pos = c1 + (r1 + T(0.5) * dist) * n;
+  }
+  make_frame(n, fr);
+  if (dist < 0) {
+    push(out, pair, slot, dist, pos, fr);
+    if (mode && mode->record) {
+      const V3<T> d = c2 - c1;
+      mode->base[mode->k].con.push_back(ModeContact{pair, slot, {double(n[0]), double(n[1]), double(n[2])},
+                                                    double(std::sqrt(dot(d, d))), double(x1), double(x2),
+                                                    mode->normal != 0 && hold_ok});
+    }
+  }
+  return dist;
+}
+
+template <class T> void collide(int pair, const GeomPose<T>* gp, std::vector<Contact<T>>& out, int* unsup,
+                                Mode* mode) {
   int g1 = g1_pair_g1[pair], g2 = g1_pair_g2[pair], t1 = g1_geom_type[g1], t2 = g1_geom_type[g2];
   const V3<T> p1 = gp[g1].p, p2 = gp[g2].p;
   const double* s1 = g1_geom_size + 3 * g1;
@@ -317,11 +403,9 @@ template <class T> void collide(int pair, const GeomPose<T>* gp, std::vector<Con
   V3<T> dif = p2 - p1;
   T rb = T(g1_geom_rbound[g1]) + T(g1_geom_rbound[g2]);
   if (dot(dif, dif) > rb * rb) return;  // bounding spheres apart: no contact at zero margin
+  const V3<T> zero = v3<T>(0, 0, 0);
   if (t1 == SPHERE && t2 == SPHERE) {
-    T dist; V3<T> pos, n, fr[3];
-    sphere_sphere(p1, T(s1[0]), p2, T(s2[0]), &dist, &pos, &n);
-    make_frame(n, fr);
-    if (dist < 0) push(out, pair, 0, dist, pos, fr);
+    core_contact(out, mode, pair, 0, p1, zero, T(0), T(s1[0]), p2, zero, T(0), T(s2[0]), false);
     return;
   }
   if (t1 == SPHERE && t2 == CAPSULE) {  // closest point of the segment, MuJoCo Warp's regularised parameter
@@ -330,34 +414,28 @@ template <class T> void collide(int pair, const GeomPose<T>* gp, std::vector<Con
     V3<T> a = p2 - hl * ax, ab = (T(2) * hl) * ax, ap = p1 - a;
     T gam = dot(ab, ab) + T(1e-6);
     T t = std::min(std::max(dot(ap, ab) / gam, T(0)), T(1));
-    V3<T> pt = a + t * ab;
-    T dist; V3<T> pos, n, fr[3];
-    sphere_sphere(p1, T(s1[0]), pt, T(s2[0]), &dist, &pos, &n);
-    make_frame(n, fr);
-    if (dist < 0) push(out, pair, 0, dist, pos, fr);
+    core_contact(out, mode, pair, 0, p1, zero, T(0), T(s1[0]), a, ab, t, T(s2[0]), false);
     return;
   }
   if (t1 == CAPSULE && t2 == CAPSULE) {
     V3<T> a1 = T(s1[1]) * zaxis(gp[g1].q), a2 = T(s2[1]) * zaxis(gp[g2].q), d = p1 - p2;
     T ma = dot(a1, a1), mb = -dot(a1, a2), mc = dot(a2, a2), u = -dot(a1, d), v = dot(a2, d);
     T det = ma * mc - mb * mb;
-    auto contact_at = [&](T x1, T x2, T* dist, V3<T>* pos, V3<T>* n) {
-      sphere_sphere(p1 + x1 * a1, T(s1[0]), p2 + x2 * a2, T(s2[0]), dist, pos, n);
-    };
     if (std::fabs(det) >= T(1e-15)) {  // else parallel: the segments' end candidates
       T x1 = (mc * u - mb * v) / det, x2 = (ma * v - mb * u) / det;
-      if (x1 > 1) { x1 = 1; x2 = (v - mb) / mc; }
-      else if (x1 < -1) { x1 = -1; x2 = (v + mb) / mc; }
+      bool free1 = true, free2 = true;  // not set by a clamp of the cascade
+      if (x1 > 1) { x1 = 1; free1 = false; x2 = (v - mb) / mc; }
+      else if (x1 < -1) { x1 = -1; free1 = false; x2 = (v + mb) / mc; }
       if (x2 > 1 || x2 < -1) {
         bool hi = x2 > 1;
         x2 = hi ? T(1) : T(-1);
+        free2 = false;
         T raw = hi ? (u - mb) / ma : (u + mb) / ma;
+        free1 = raw > -1 && raw < 1;
         x1 = std::min(std::max(raw, T(-1)), T(1));
       }
-      T dist; V3<T> pos, n, fr[3];
-      contact_at(x1, x2, &dist, &pos, &n);
-      make_frame(n, fr);
-      if (dist < 0) push(out, pair, 0, dist, pos, fr);
+      core_contact(out, mode, pair, 0, p1, a1, x1, T(s1[0]), p2, a2, x2, T(s2[0]),
+                   free1 && free2 && det < T(1.2e-3) * ma * mc);
     } else {
       int cnt = 0;
       for (int e = 0; e < 4 && cnt < 2; e++) {
@@ -371,13 +449,7 @@ template <class T> void collide(int pair, const GeomPose<T>* gp, std::vector<Con
           T raw = e == 2 ? (u - mb) / ma : (u + mb) / ma;
           x1 = std::min(std::max(raw, T(-1)), T(1));
         }
-        T dist; V3<T> pos, n, fr[3];
-        contact_at(x1, x2, &dist, &pos, &n);
-        if (dist <= 0) {
-          cnt++;
-          make_frame(n, fr);
-          if (dist < 0) push(out, pair, e, dist, pos, fr);
-        }
+        if (core_contact(out, mode, pair, e, p1, a1, x1, T(s1[0]), p2, a2, x2, T(s2[0]), false) <= 0) cnt++;
       }
     }
     return;
@@ -393,7 +465,7 @@ template <class T> void collision(World<T>& w) {
     gp[g].q = qmul(w.xq[b], mq4<T>(g1_geom_quat + 4 * g));
   }
   std::vector<Contact<T>> all;
-  for (int p = 0; p < NPAIR; p++) collide(p, gp, all, &w.unsupported);
+  for (int p = 0; p < NPAIR; p++) collide(p, gp, all, &w.unsupported, w.mode);
   w.ncon_raw = (int)all.size();
   if (w.ncon_raw > MAXCON) { w.unsupported |= 4; all.resize(MAXCON); }
   for (auto& c : all) c.mu = g1_pair_foot[c.pair] ? w.fric : T(g1_pair_mu[c.pair]);
@@ -676,9 +748,121 @@ void step_world(int iw, const double* qpos, const double* qvel, const double* wa
   delete w;
 }
 
+// One world's control step from float64 inputs (qpos 36, qvel 35, warm 35, ctrl 29, fric, com 3) under a gradient
+// mode's base pass or surrogate: (qpos', qvel') into out (71)
+template <class T>
+void mode_step(const double* q, const double* v, const double* warm, const double* u, double fric, const double* com,
+               int iterations, int nsub, double tol, Mode* mode, double* out) {
+  World<T>* w = new World<T>();
+  T c[NU];
+  for (int i = 0; i < NQ; i++) w->qpos[i] = T(q[i]);
+  for (int i = 0; i < NV; i++) { w->qvel[i] = T(v[i]); w->qacc[i] = T(warm[i]); }
+  for (int i = 0; i < NU; i++) c[i] = T(u[i]);
+  w->ctrl = c;
+  w->fric = T(fric);
+  w->com = v3(T(com[0]), T(com[1]), T(com[2]));
+  w->unsupported = 0;
+  w->mode = mode;
+  for (int k = 0; k < nsub; k++) {
+    mode->k = k;
+    substep(*w, iterations, T(tol), nullptr);
+  }
+  for (int i = 0; i < NQ; i++) out[i] = double(w->qpos[i]);
+  for (int i = 0; i < NV; i++) out[NQ + i] = double(w->qvel[i]);
+  delete w;
+}
+
+// qpos moved along the tangent dq (35): root position, root rotation vector in the local frame, hinge angles
+void integrate_qpos(const double* q, const double* dq, double* out) {
+  for (int i = 0; i < NQ; i++) out[i] = q[i];
+  for (int k = 0; k < 3; k++) out[k] += dq[k];
+  const double ang = std::sqrt(dq[3] * dq[3] + dq[4] * dq[4] + dq[5] * dq[5]);
+  double qn = std::sqrt(q[3] * q[3] + q[4] * q[4] + q[5] * q[5] + q[6] * q[6]);
+  Q4<double> quat{q[3] / qn, q[4] / qn, q[5] / qn, q[6] / qn}, dquat{1, 0, 0, 0};
+  if (ang > 0) {
+    const double sn = std::sin(ang / 2) / ang;
+    dquat = Q4<double>{std::cos(ang / 2), sn * dq[3], sn * dq[4], sn * dq[5]};
+  }
+  const Q4<double> o = qmul(quat, dquat);
+  out[3] = o.w; out[4] = o.x; out[5] = o.y; out[6] = o.z;
+  for (int i = 6; i < NV; i++) out[i + 1] += dq[i];
+}
+
 }  // namespace
 
 extern "C" {
+
+// Central differences (step h) of a gradient mode's surrogate step (Mode, above: clamp_kv 0..2 with soft, normal
+// 0..3), float64: J (nw, 71, 99) = d(qpos' in qpos form 36, qvel' 35) / d(qpos tangent 35, qvel 35, ctrl 29) at the
+// inputs, the base pass (which records what the mode holds) run once per world. Test infrastructure: the check of the
+// analytic adjoint's modes.
+int g1_oracle_fd_jacobian_mode(int nw, const double* qpos, const double* qvel, const double* warm, const double* ctrl,
+                               const double* fric, const double* com, int iterations, int nsub, double tol,
+                               int clamp_kv, int normal, double soft, double h, int nthreads, double* J) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3)
+    return 1;
+  constexpr int NO = NQ + NV, NI = 2 * NV + NU;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads > 0 ? nthreads : omp_get_max_threads())
+  for (int iw = 0; iw < nw; iw++) {
+    const double *q = qpos + (size_t)iw * NQ, *v = qvel + (size_t)iw * NV, *wm = warm + (size_t)iw * NV;
+    const double *u = ctrl + (size_t)iw * NU, *cm = com + 3 * (size_t)iw;
+    std::vector<ModeBase> base(nsub);
+    Mode mode;
+    mode.clamp_kv = clamp_kv; mode.normal = normal; mode.soft = soft; mode.base = base.data();
+    double out[NO], plus[NO], minus[NO], qq[NQ], vv[NV], uu[NU], dq[NV];
+    mode.record = true;
+    mode_step<double>(q, v, wm, u, fric[iw], cm, iterations, nsub, tol, &mode, out);
+    mode.record = false;
+    for (int j = 0; j < NI; j++) {
+      for (int sgn = 0; sgn < 2; sgn++) {
+        const double d = sgn ? -h : h;
+        for (int i = 0; i < NQ; i++) qq[i] = q[i];
+        for (int i = 0; i < NV; i++) vv[i] = v[i];
+        for (int i = 0; i < NU; i++) uu[i] = u[i];
+        if (j < NV) {
+          for (int i = 0; i < NV; i++) dq[i] = i == j ? d : 0.0;
+          integrate_qpos(q, dq, qq);
+        } else if (j < 2 * NV) {
+          vv[j - NV] += d;
+        } else {
+          uu[j - 2 * NV] += d;
+        }
+        mode_step<double>(qq, vv, wm, uu, fric[iw], cm, iterations, nsub, tol, &mode, sgn ? minus : plus);
+      }
+      for (int o = 0; o < NO; o++) J[((size_t)iw * NO + o) * NI + j] = (plus[o] - minus[o]) / (2 * h);
+    }
+  }
+  return 0;
+}
+
+// The base trajectory's smallest sphere-core centre distance nu over all substeps' contacts, per world (1e300 when
+// it has none) with that contact's pair (-1: none), and how many capsule contacts the near-parallel rule holds:
+// which states exercise the normal options. Test infrastructure.
+int g1_oracle_core_stats(int nw, const double* qpos, const double* qvel, const double* warm, const double* ctrl,
+                         const double* fric, const double* com, int iterations, int nsub, double* min_nu,
+                         int* nholds, int* min_pair) {
+  if (nw < 0 || nsub < 1 || nsub > 32) return 1;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int iw = 0; iw < nw; iw++) {
+    std::vector<ModeBase> base(nsub);
+    Mode mode;
+    mode.normal = 3; mode.base = base.data(); mode.record = true;
+    double out[NQ + NV];
+    mode_step<double>(qpos + (size_t)iw * NQ, qvel + (size_t)iw * NV, warm + (size_t)iw * NV, ctrl + (size_t)iw * NU,
+                      fric[iw], com + 3 * (size_t)iw, iterations, nsub, 1e-8, &mode, out);
+    double m = 1e300;
+    int nh = 0, mp = -1;
+    for (const ModeBase& b : base)
+      for (const ModeContact& c : b.con) {
+        if (c.nu < m) { m = c.nu; mp = c.pair; }
+        nh += c.hold;
+      }
+    min_nu[iw] = m;
+    nholds[iw] = nh;
+    if (min_pair) min_pair[iw] = mp;
+  }
+  return 0;
+}
 
 // One control step of nw worlds (row-major float64 arrays, as the C-ABI's float32 ones): nsub substeps of the
 // reference's algorithm, Newton capped at `iterations` with tolerance `tol` (the model's 1e-8 by default).

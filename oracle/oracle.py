@@ -33,6 +33,11 @@ def lib():
         d, i = ctypes.c_void_p, ctypes.c_int
         _lib.g1_oracle_step.argtypes = [i, d, d, d, d, d, d, i, i, ctypes.c_double, i, i, d, d, d, d, d, d]
         _lib.g1_oracle_step.restype = i
+        _lib.g1_oracle_fd_jacobian_mode.argtypes = [i] + [d] * 6 + [i, i, ctypes.c_double, i, i, ctypes.c_double,
+                                                                    ctypes.c_double, i, d]
+        _lib.g1_oracle_fd_jacobian_mode.restype = i
+        _lib.g1_oracle_core_stats.argtypes = [i] + [d] * 6 + [i, i, d, d, d]
+        _lib.g1_oracle_core_stats.restype = i
         _lib.g1_oracle_matrices.argtypes = [i] + [d] * 10
         _lib.g1_oracle_matrices.restype = i
     return _lib
@@ -121,6 +126,37 @@ def fd_jacobian(qpos, qvel, warm, ctrl, friction, com, h=1e-6, iterations=2000, 
             outs.append(np.concatenate([oq, ov], 1))
         cols.append((outs[0] - outs[1]) / (2 * h))
     return np.stack(cols, 2)
+
+
+def fd_jacobian_mode(qpos, qvel, warm, ctrl, friction, com, clamp_kv=1, normal=0, soft=0.2, h=1e-6, iterations=2000,
+                     tol=1e-13, substeps=4, threads=0):
+    """Central-difference Jacobian (B, 71, 99) of the surrogate step of the adjoint's gradient mode (clamp_kv,
+    normal, soft) in the tangent basis, float64, converged solves: the derivative that mode's analytic VJP must give
+    (oracle/g1_oracle.cpp: Mode). clamp_kv=1, normal=0 is the plain step's Jacobian (fd_jacobian)."""
+    B = np.asarray(qpos).shape[0]
+    args = [_c(qpos, (B, NQ)), _c(qvel, (B, NV)), _c(warm, (B, NV)), _c(ctrl, (B, NU)), _c(friction, (B,)),
+            _c(com, (B, 3))]
+    J = np.zeros((B, NQ + NV, 2 * NV + NU))
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    rc = lib().g1_oracle_fd_jacobian_mode(B, *map(p, args), int(iterations), int(substeps), float(tol), int(clamp_kv),
+                                          int(normal), float(soft), float(h), int(threads), p(J))
+    if rc:
+        raise ValueError(f"g1_oracle_fd_jacobian_mode failed ({rc})")
+    return J
+
+
+def core_stats(qpos, qvel, warm, ctrl, friction, com, iterations=10, substeps=4):
+    """Per world of one step: the smallest centre distance nu (m) of a sphere-core (self) contact over the substeps
+    (1e300: none), the number of capsule contacts the near-parallel rule holds (normal option on), and the pair of
+    the smallest-nu contact (-1: none)."""
+    B = np.asarray(qpos).shape[0]
+    args = [_c(qpos, (B, NQ)), _c(qvel, (B, NV)), _c(warm, (B, NV)), _c(ctrl, (B, NU)), _c(friction, (B,)),
+            _c(com, (B, 3))]
+    nu, nh, pr = np.zeros(B), np.zeros(B, np.int32), np.zeros(B, np.int32)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    if lib().g1_oracle_core_stats(B, *map(p, args), int(iterations), int(substeps), p(nu), p(nh), p(pr)):
+        raise ValueError("g1_oracle_core_stats failed")
+    return nu, nh, pr
 
 
 def threads_available():

@@ -265,3 +265,84 @@ def test_nonfinite_inputs_are_flagged_not_fatal():
     assert torch.isfinite(v1[ok]).all() and torch.isfinite(gq[ok]).all()
     d = torch_ffi.read_diagnostics(reset=True)
     assert d["nonfinite_rows"] >= 1 and (int(binfo[2].item()) >> 16) & 7
+
+
+# every (clamp_kv, normal) gradient mode of nb_g1_adjoint against central differences of the float64 oracle's
+# surrogate step for that mode (oracle/g1_oracle.cpp: Mode, the derivative the mode defines): the reference's
+# clamped (G4), limit-row (G5) and self-contact (G6) gradient states, and states whose self contacts come within
+# 1 mm of degenerate (nu ~ 0.5 mm, tests/golden/mode_states.npz), where the normal options 2 and 3 differ from the
+# exact derivative. Gates: on the reference's states, the gradient check's p99 bounds per block on the relative
+# error per state; on the near-degenerate ones (max over states), NEAR_THRESHOLDS: there the contact normal n =
+# (c2 - c1) / nu is computed in float32 from centres ~1 m from the origin with nu ~ 5e-4 m, so it carries a relative
+# error ~ 1e-7 m / nu ~ 2e-4, which the contact's force and Hessian terms carry into the gradient. The exact normal
+# derivative (normal 0) there is 1 / nu-sensitive: reported, not gated.
+MODES = [(kv, n) for kv in (0, 1, 2) for n in (0, 1, 2, 3)]
+NEAR_THRESHOLDS = dict(qpos=5e-3, qvel=2e-3, ctrl=1e-3)
+
+
+@pytest.fixture(scope="module")
+def mode_cases(golden):
+    t = golden("truth_grad.npz")
+    pick = np.concatenate([np.flatnonzero(t[f"group_{g}"] & (t["model_flags"] == 0))[:n]
+                           for g, n in (("G4", 8), ("G5", 4), ("G6", 8))])
+    s = {k: t[k][pick] for k in KEYS}
+    s["cot_qpos"], s["cot_qvel"] = t["cot_qpos"][pick, 0], t["cot_qvel"][pick, 0]
+    m = golden("mode_states.npz")
+    rng = np.random.default_rng(5)
+    n = m["qpos"].shape[0]
+    cq, cv = rng.standard_normal((n, 36)).astype(np.float32), rng.standard_normal((n, 35)).astype(np.float32)
+    cq[:, 3:7] = 0.0
+    for k in KEYS:
+        s[k] = np.concatenate([s[k], m[k]])
+    s["cot_qpos"], s["cot_qvel"] = np.concatenate([s["cot_qpos"], cq]), np.concatenate([s["cot_qvel"], cv])
+    near = np.zeros(len(s["qpos"]), bool)
+    near[len(pick):] = True
+    return s, near
+
+
+def _mode_vjp(s, clamp_kv, normal):
+    torch = _cuda()
+    from nablaengine_b200 import torch_ffi
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda() for k in KEYS]
+    tape = torch_ffi.forward(*t, iterations=50, tape=True)[4]
+    cq = torch.from_numpy(np.ascontiguousarray(s["cot_qpos"], np.float32)).cuda()
+    cv = torch.from_numpy(np.ascontiguousarray(s["cot_qvel"], np.float32)).cuda()
+    gq, gv, gu, info = torch_ffi.backward(tape, t[4], t[5], cq, cv, clamp_kv=clamp_kv, normal=normal,
+                                          ctrl=t[3] if clamp_kv == 2 else None)
+    return np.concatenate([qpos_tangent(gq.cpu().numpy(), s["qpos"]), gv.cpu().numpy(), gu.cpu().numpy()], 1)
+
+
+@pytest.mark.parametrize("clamp_kv,normal", MODES)
+def test_every_gradient_mode_against_the_oracle_surrogate(mode_cases, clamp_kv, normal):
+    import oracle
+    s, near = mode_cases
+    J = oracle.fd_jacobian_mode(*(s[k] for k in KEYS), clamp_kv=clamp_kv, normal=normal, soft=0.2)
+    cot = np.concatenate([s["cot_qpos"], s["cot_qvel"]], 1).astype(np.float64)
+    fd = np.einsum("bi,bij->bj", cot, J)
+    g = _mode_vjp(s, clamp_kv, normal)
+    lines = []
+    for name, sl in BLOCKS.items():
+        e = np.linalg.norm(g[:, sl] - fd[:, sl], axis=1) / np.maximum(np.linalg.norm(fd[:, sl], axis=1), 1e-9)
+        lines.append(f"({clamp_kv}, {normal}) {name}: reference states p99 {np.quantile(e[~near], 0.99):.2e}, "
+                     f"near-degenerate states max {e[near].max():.2e}")
+        assert np.quantile(e[~near], 0.99) <= THRESHOLDS[name], "\n".join(lines)
+        if normal != 0:
+            assert e[near].max() <= NEAR_THRESHOLDS[name], "\n".join(lines)
+    print("\n".join(lines))
+
+
+def test_gradient_modes_differ_where_they_should(mode_cases):
+    """The options change the gradient only where they act: the clamp options on states with a clamped actuator
+    (G4), the options 2 and 3 only near a degenerate self contact (and there only where that contact carries a force:
+    a contact whose rows are all inactive adds nothing to the gradient)."""
+    s, near = mode_cases
+    base = _mode_vjp(s, 1, 0)
+    g4 = np.zeros(len(near), bool)
+    g4[:8] = True
+    for kv in (0, 2):
+        d = np.abs(_mode_vjp(s, kv, 0) - base).max(1)
+        assert (d[g4] > 0).any()
+    for n in (2, 3):
+        d = np.abs(_mode_vjp(s, 1, n) - base).max(1)
+        print(f"normal {n}: gradient changed on {int((d[near] > 0).sum())} of {int(near.sum())} near-degenerate states")
+        assert (d[near] > 0).any() and (d[~near] == 0).all()

@@ -102,3 +102,19 @@ def test_oracle_fd_jacobian_matches_mujoco_jacobian_truth(golden):
         err = np.maximum(e, floor) / nt
         assert np.median(err) < 1e-5, (sl, err)
         assert err.max() < 1e-4, (sl, err)
+
+
+def test_mode_surrogate_exact_mode_is_the_plain_step(golden):
+    """The gradient-mode surrogate in the exact mode (clamp_kv=1, normal=0) is the plain step: its central
+    differences equal fd_jacobian's bitwise; the frozen normal (normal=1) changes only states with self contacts."""
+    g = golden("truth_grad.npz")
+    keys = INPUTS
+    idx = np.concatenate([np.flatnonzero(g["group_G0"])[:2], np.flatnonzero(g["group_G6"])[:2]])
+    x = [g[k][idx] for k in keys]
+    J0 = oracle.fd_jacobian(*x, iterations=200)
+    J1 = oracle.fd_jacobian_mode(*x, clamp_kv=1, normal=0, iterations=200)
+    assert np.array_equal(J0, J1)
+    nu, _, _ = oracle.core_stats(*x)
+    Jf = oracle.fd_jacobian_mode(*x, clamp_kv=1, normal=1, iterations=200)
+    changed = np.abs(Jf - J1).reshape(len(idx), -1).max(1) > 0
+    assert changed.tolist() == (nu < 1e299).tolist()

@@ -13,7 +13,7 @@
 namespace nbg1 {
 
 #ifndef NB_WPB
-#define NB_WPB 14
+#define NB_WPB 15
 #endif
 #ifndef NB_LOCKSTEP
 #define NB_LOCKSTEP 1
@@ -90,8 +90,8 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
       const bool v = c < s.ncon;
       o[0] = v ? (float)s.con_pair[c] : -1.f;
       o[1] = v ? s.con_dist[c] : 0.f;
-      for (int k = 0; k < 3; k++) {  // (con_pos is kept relative to the root origin X[1])
-        o[2 + k] = v ? s.con_pos[c][k] + s.X[1][k] : 0.f;
+      for (int k = 0; k < 3; k++) {  // (con_pos is kept relative to the root origin O)
+        o[2 + k] = v ? s.con_pos[c][k] + s.O[k] : 0.f;
         o[5 + k] = v ? s.con_fr[c][k] : 0.f;
       }
     }

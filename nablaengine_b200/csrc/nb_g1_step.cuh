@@ -84,25 +84,24 @@ __device__ unsigned long long g_prof[NPROF];
 struct __align__(16) World {
   float M[NTRIP], L[NTRIP];            // mass matrix (with armature), factor scratch (16-byte aligned)
   float qpos[NQ], qvel[NV], qacc[NV], ctrl[NU], com[3], fric;
-  float X[NB][3];                      // body positions (Q: orientations, until collision)
+  float O[3];                          // the root origin (body 1's position): the moments' reference point
   float dw[NV][3], dv[NV][3];          // dof motion about O: angular axis, velocity of the point O
   float qsm[NV], qacc0[NV], Ma[NV], grad[NV], p[NV], dinv[NV + 1];  // p: the Newton direction, then a_adv
-  union {
-    float BV[NB][6];                   // body spatial motion at O (angular, linear) for a generalised vector: rows_jv
-    struct { float K[21], P[KDOF][6]; unsigned char dof[KDOF]; } hs;  // Hessian assembly
-  };
+  struct { float K[21], P[KDOF][6]; unsigned char dof[KDOF]; } hs;  // Hessian assembly
   int ngroup, nls, nfact, pad3_;        // groups; line-search evaluations, factorisations (work counters)
   float ncost;                          // Newton state between iterations: cost, iterations, converged, same zones
   int nit_cur, ndone, nsame;
   unsigned clamp_lo, clamp_hi;          // actuator force at its limit (dof bits), for the tape
   int ncon, ncon_raw, nefc, nlim, unsup, ncand, nit, pad_;
+  unsigned long long lim_mask;          // dofs with a limit row (rows 0 .. nlim - 1 in dof order)
   union {
     struct {  // from kinematics to the geom poses at the start of collision
-      float Q[NB][4];                   // body orientations
+      float Q[NB][4], X[NB][3];         // body orientations and positions
       struct { float om[NB][3], al[NB][3], ao[NB][3], wr[NB][6], I[NB][10]; } sm;  // smooth phase
     };
     struct {  // collision on
-      unsigned long long grp_mask[WCON];  // contacts of group g (same body pair) as bits
+      unsigned char grp_first[WCON + 1];  // the groups' members: grp_mem[grp_first[g] .. grp_first[g + 1]),
+      unsigned char grp_mem[WCON];        // in contact order (group g: the contacts between one body pair)
       int con_pair[WCON];
       unsigned char con_slot[WCON], con_row0[WCON], con_nrow[WCON];
       unsigned short con_bb[WCON];        // the contact's bodies b1 | b2 << 8 (contact_setup on)
@@ -114,7 +113,6 @@ struct __align__(16) World {
         float wr[WCON][6];  // the contact wrench at O (moment, force)
         struct { int key[WCON]; unsigned char lead[WCON], grp[WCON]; } g;  // contact_setup: the groups
       } cs;
-      short lim_row[NV];                  // the dof's limit row, or -1
       union {
         struct {  // make_rows on
           float efc_D[WROWS];
@@ -133,9 +131,10 @@ struct __align__(16) World {
 #endif
 };
 
-// collision computes the geom poses from Q into col, then writes the contacts (over Q): Q must not share col's space
-static_assert(offsetof(World, Q) + sizeof(World::Q) <= offsetof(World, col) ||
-              offsetof(World, col) + sizeof(World::col) <= offsetof(World, Q), "Q and col overlap");
+// collision computes the geom poses from Q and X into col, then writes the contacts (over Q and X): Q and X must not
+// share col's space
+static_assert(offsetof(World, Q) + sizeof(World::Q) <= offsetof(World, col) &&
+              offsetof(World, X) + sizeof(World::X) <= offsetof(World, col), "Q, X and col overlap");
 
 // ---- small vector helpers --------------------------------------------------------------------------------------
 __device__ __forceinline__ void qmul(const float* a, const float* b, float* o) {
@@ -174,14 +173,6 @@ __device__ __forceinline__ float ld(const float* p) { return __ldg(p); }
 __device__ __forceinline__ int ldi(const int* p) { return __ldg(p); }
 
 // M(i, j) of a symmetric matrix stored as its packed lower triangle
-// index of the (k + 1)-th set bit of m, or -1
-__device__ __forceinline__ int nth_bit(unsigned long long m, int k) {
-  const unsigned lo = (unsigned)m, hi = (unsigned)(m >> 32);
-  const int nlo = __popc(lo);
-  if (k < nlo) return (int)__fns(lo, 0, k + 1);
-  k -= nlo;
-  return k < __popc(hi) ? 32 + (int)__fns(hi, 0, k + 1) : -1;
-}
 __device__ __forceinline__ float sym(const float* A, int i, int j) { return j <= i ? A[TRI(i, j)] : A[TRI(j, i)]; }
 
 // ---- smooth dynamics ---------------------------------------------------------------------------------------------
@@ -203,7 +194,7 @@ __device__ __noinline__ void kinematics(World& s, int lane) {
         float wl[3] = {s.qvel[3], s.qvel[4], s.qvel[5]}, om[3];
         qrot(s.Q[1], wl, om);
         for (int k = 0; k < 3; k++) {
-          s.X[1][k] = s.qpos[k];
+          s.X[1][k] = s.O[k] = s.qpos[k];
           s.sm.om[1][k] = om[k];
           s.sm.al[1][k] = 0.f;
           s.sm.ao[1][k] = 0.f;
@@ -253,7 +244,7 @@ __device__ __noinline__ void kinematics(World& s, int lane) {
 
 // the dofs' motion vectors about O = the root origin (lane = dof)
 __device__ __noinline__ void dof_motion(World& s, int lane) {
-  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  const float O[3] = {s.O[0], s.O[1], s.O[2]};
   for (int i = lane; i < NV; i += 32) {
     float w[3] = {0.f, 0.f, 0.f}, v[3] = {0.f, 0.f, 0.f};
     if (i < 3) {
@@ -278,7 +269,7 @@ __device__ __noinline__ void dof_motion(World& s, int lane) {
 // subtrees (leaves first)
 __device__ __noinline__ void body_terms(World& s, int lane) {
   const int b = lane;
-  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  const float O[3] = {s.O[0], s.O[1], s.O[2]};
   if (b >= 1 && b < NB) {
     float ip[3] = {ld(g1_body_ipos + 3 * b), ld(g1_body_ipos + 3 * b + 1), ld(g1_body_ipos + 3 * b + 2)};
     if (b == G1_TORSO)
@@ -986,7 +977,7 @@ __device__ __noinline__ void collision(World& s, int lane) {
 // one wrench
 __device__ __noinline__ void contact_setup(World& s, int lane) {
   const int ncon = uni(s.ncon);
-  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  const float O[3] = {s.O[0], s.O[1], s.O[2]};
   __syncwarp();
   for (int c = lane; c < ncon; c += 32) {
     const int pr = s.con_pair[c];
@@ -1022,22 +1013,39 @@ __device__ __noinline__ void contact_setup(World& s, int lane) {
   }
   for (int c = lane; c < ncon; c += 32) s.cs.g.grp[c] = s.cs.g.grp[s.cs.g.lead[c]];
   __syncwarp();
-  for (int g = lane; g < ngroup; g += 32) {
-    unsigned long long m = 0ull;
-    for (int c = 0; c < ncon; c++)
-      if (s.cs.g.grp[c] == g) m |= 1ull << c;
-    s.grp_mask[g] = m;
+  // the member lists: group g's size (lane g), an exclusive prefix sum over the groups, then its members in order
+  int carry = 0;
+  for (int g0 = 0; g0 < ngroup; g0 += 32) {
+    const int g = g0 + lane;
+    int n = 0;
+    if (g < ngroup)
+      for (int c = 0; c < ncon; c++) n += s.cs.g.grp[c] == g;
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (g < ngroup) {
+      int k = carry + incl - n;
+      s.grp_first[g] = (unsigned char)k;
+      for (int c = 0; c < ncon; c++)
+        if (s.cs.g.grp[c] == g) s.grp_mem[k++] = (unsigned char)c;
+    }
+    carry += __shfl_sync(FULL, incl, 31);
   }
-  if (lane == 0) s.ngroup = ngroup;
+  if (lane == 0) { s.grp_first[ngroup] = (unsigned char)ncon; s.ngroup = ngroup; }
   __syncwarp();
 }
 
 // ---- constraint rows -----------------------------------------------------------------------------------------------
-// body spatial motion at O for the generalised vector v (lane = body: a sum over its ancestor dofs)
-__device__ __noinline__ void body_motion(World& s, const float* v, int lane) {
-  // own contribution of body b (lane): its hinge's v_d (dw, dv); the root: its 6 dofs (translations e_k, rotations
-  // about O); then the sums over the ancestors by pointer jumping (ceil(log2(depth + 1)) = 4 rounds: add the value
-  // held by the current ancestor pointer, then jump the pointer; the world body holds 0 and points to itself)
+// J_d v of every contact's frame rows for the generalised vector v, into cs.jd. First the bodies' spatial motions at
+// O (lane = body, kept in registers): its own contribution, the hinge's v_d (dw, dv), or for the root its 6 dofs
+// (translations e_k, rotations about O), then the sums over the ancestors by pointer jumping (ceil(log2(depth + 1))
+// = 4 rounds: add the value held by the current ancestor pointer, then jump the pointer; the world body holds 0 and
+// points to itself). Then per contact (lane = contact) the two bodies' motions by shuffles from their lanes, and the
+// relative velocity at the contact point along the frame rows.
+__device__ __noinline__ void contact_jv(World& s, const float* v, int lane) {
   static_assert(MAXD < 16, "4 pointer-jumping rounds");
   float a[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   int par = 0;
@@ -1058,24 +1066,22 @@ __device__ __noinline__ void body_motion(World& s, const float* v, int lane) {
     for (int k = 0; k < 6; k++) a[k] += __shfl_sync(FULL, a[k], par);
     par = __shfl_sync(FULL, par, par);
   }
-  if (lane < NB)
-    for (int k = 0; k < 6; k++) s.BV[lane][k] = a[k];
-  __syncwarp();
-}
-
-// J_d v of every contact's frame rows (after body_motion(v))
-__device__ __noinline__ void contact_jv(World& s, int lane) {
-  const int ncon = s.ncon;
-  for (int c = lane; c < ncon; c += 32) {
-    const int bb = s.con_bb[c], b1 = bb & 255, b2 = bb >> 8;
-    float dV[6], u[3];
-    for (int k = 0; k < 6; k++) dV[k] = s.BV[b2][k] - s.BV[b1][k];
-    // the relative velocity at the contact point: v_O + w x (pos - O); frame row d: row . that
-    cross(dV, s.con_pos[c], u);
-    for (int k = 0; k < 3; k++) u[k] += dV[3 + k];
-    float fr[9];
-    frame_rows(s, c, fr);
-    for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(fr + 3 * d, u);
+  const int ncon = uni(s.ncon);
+  for (int c0 = 0; c0 < ncon; c0 += 32) {
+    const int c = c0 + lane;
+    const bool valid = c < ncon;
+    const int bb = valid ? s.con_bb[c] : 0, b1 = bb & 255, b2 = bb >> 8;
+    float dV[6];
+#pragma unroll
+    for (int k = 0; k < 6; k++) dV[k] = __shfl_sync(FULL, a[k], b2) - __shfl_sync(FULL, a[k], b1);
+    if (valid) {
+      // the relative velocity at the contact point: v_O + w x (pos - O); frame row d: row . that
+      float u[3], fr[9];
+      cross(dV, s.con_pos[c], u);
+      for (int k = 0; k < 3; k++) u[k] += dV[3 + k];
+      frame_rows(s, c, fr);
+      for (int d = 0; d < 3; d++) s.cs.jd[c][d] = dot3(fr + 3 * d, u);
+    }
   }
   __syncwarp();
 }
@@ -1083,8 +1089,7 @@ __device__ __noinline__ void contact_jv(World& s, int lane) {
 // J v of every row into registers: row r = lane + 32 t into o[t], 0 past the row count (contact rows from cs.jd,
 // limit rows from v)
 __device__ __forceinline__ void rows_jv(World& s, const float* v, float (&o)[ROWS_PER_LANE], int lane) {
-  body_motion(s, v, lane);
-  contact_jv(s, lane);
+  contact_jv(s, v, lane);
   const int nefc = s.nefc;
 #pragma unroll
   for (int t = 0; t < ROWS_PER_LANE; t++) {
@@ -1123,9 +1128,8 @@ __device__ __noinline__ void impedance(const float* solref, const float* solimp,
 __device__ __noinline__ void make_rows(World& s, int lane) {
   const float h = G1_TIMESTEP;
   const unsigned below = (1u << lane) - 1u;
-  for (int i = lane; i < NV; i += 32) s.lim_row[i] = -1;
-  __syncwarp();
   int nlim = 0;
+  unsigned long long lmask = 0ull;
   for (int i0 = 0; i0 < NV; i0 += 32) {
     const int i = i0 + lane;
     float dlo = 1.f, dhi = 1.f;
@@ -1136,6 +1140,7 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
     }
     const bool on = fminf(dlo, dhi) < 0.f;
     const unsigned bal = __ballot_sync(FULL, on);
+    lmask |= (unsigned long long)bal << i0;
     if (on) {
       const int r = nlim + __popc(bal & below);
       const float pos = fminf(dlo, dhi), sg = dlo < dhi ? 1.f : -1.f;
@@ -1146,15 +1151,13 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
       impedance(sr, si, pos, h, &k, &b, &imp);
       const float R = fmaxf(1e-15f, ld(g1_dof_invweight0 + i) * (1.f - imp) / imp);
       s.efc_kind[r] = ROW_LIMIT; s.efc_a[r] = (short)i; s.efc_b[r] = (signed char)sg;
-      s.lim_row[i] = (short)r;
       s.efc_D[r] = 1.f / R;
       s.efc_jar[r] = -b * (sg * s.qvel[i]) - k * imp * pos;  // aref until newton_begin
     }
     nlim += __popc(bal);
   }
   // contact rows need J qvel
-  body_motion(s, s.qvel, lane);
-  contact_jv(s, lane);
+  contact_jv(s, s.qvel, lane);
   const int ncon = uni(s.ncon);
   int r0 = nlim;
   for (int c0 = 0; c0 < ncon; c0 += 32) {
@@ -1200,6 +1203,7 @@ __device__ __noinline__ void make_rows(World& s, int lane) {
   }
   if (lane == 0) {
     s.nlim = nlim;
+    s.lim_mask = lmask;
     s.nefc = min(r0, WROWS);
     if (r0 > WROWS) s.unsup |= ROW_OVERFLOW;
   }
@@ -1254,23 +1258,18 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
     const int g = g0 + lane / 6, e = lane % 6;
     float acc = 0.f;
     const bool on = lane < 30 && g < ngroup;
-    if (on) {
-      unsigned long long m = s.grp_mask[g];
-      while (m) {
-        const int c = __ffsll((long long)m) - 1;
-        m &= m - 1ull;
-        acc += s.cs.wr[c][e];
-      }
-    }
+    if (on)
+      for (int k = s.grp_first[g]; k < s.grp_first[g + 1]; k++) acc += s.cs.wr[s.grp_mem[k]][e];
     __syncwarp();
-    if (on) s.cs.wr[__ffsll((long long)s.grp_mask[g]) - 1][e] = acc;
+    if (on) s.cs.wr[s.grp_mem[s.grp_first[g]]][e] = acc;
     __syncwarp();
   }
   // lane l: dof 3 + l (dofs 3..34 in one pass); dofs 0..2 (the root translations, motion e_k) get the linear force
   // of the groups whose support holds them (every lane accumulates those three sums)
   const int i = lane + 3;
   float jtf = 0.f, ft[3] = {0.f, 0.f, 0.f};
-  const int lr = s.lim_row[i];
+  const unsigned long long lmask = s.lim_mask;  // the dof's limit row: its rank among the dofs with one
+  const int lr = (lmask >> i) & 1ull ? __popcll(lmask & ((1ull << i) - 1ull)) : -1;
   if (lr >= 0) {
     const float x = s.efc_jar[lr];
     if (x < 0.f) jtf = s.efc_b[lr] * (-s.efc_D[lr] * x);
@@ -1279,7 +1278,7 @@ __device__ __noinline__ float2 newton_grad(World& s, int lane, float extra) {
   const unsigned long long bit = 1ull << i;
 #pragma unroll 1
   for (int g = 0; g < ngroup; g++) {
-    const int c = __ffsll((long long)s.grp_mask[g]) - 1;
+    const int c = s.grp_mem[s.grp_first[g]];  // the group's first contact holds its sum
     unsigned long long m1, m2;
     body_masks(s.con_bb[c], &m1, &m2);
     const float* W = s.cs.wr[c];
@@ -1364,7 +1363,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
   bool xbranch = false;  // a group on two branches of the tree (H fills outside M's pattern)
 #endif
   for (int g = 0; g < ngroup; g++) {
-    const unsigned long long gm = s.grp_mask[g];
+    const int first = s.grp_first[g], nmem = s.grp_first[g + 1] - first;
     // K = sum of D a a' over the group's quadratic rows, a = ((pos - O) x u, u) with u = n +- mu t_k the row's
     // direction: lane 4 m + t holds the 21 products (upper triangle of 6 x 6, row order) of row t of the group's
     // member m (eight members at a time), and a transposing reduction leaves entry kslot on each lane
@@ -1372,10 +1371,10 @@ __device__ __noinline__ void hessian(World& s, int lane) {
 #pragma unroll
     for (int e = 0; e < 21; e++) v[e] = 0.f;
     bool any = false;
-    const int nmem = __popcll(gm);
 #pragma unroll 1
     for (int base = 0; base < nmem; base += 8) {
-      const int c = nth_bit(gm, base + (lane >> 2)), t = lane & 3;
+      const int m = base + (lane >> 2), t = lane & 3;
+      const int c = m < nmem ? s.grp_mem[first + m] : -1;
       if (c < 0 || t >= s.con_nrow[c]) continue;
       const int r = s.con_row0[c] + t;
       if (!(s.efc_jar[r] < 0.f)) continue;
@@ -1404,7 +1403,7 @@ __device__ __noinline__ void hessian(World& s, int lane) {
     kred_level<2, 1>(v, lane);
     if (kslot >= 0) s.hs.K[kslot] = v[0];
     __syncwarp();
-    const int lead = __ffsll((long long)gm) - 1;
+    const int lead = s.grp_mem[first];
     unsigned long long m1, m2;
     body_masks(s.con_bb[lead], &m1, &m2);
     const unsigned long long sup = m1 | m2;

@@ -91,9 +91,9 @@ class Clocks:
 
 
 # DRAM bytes (read + write) per world of one forward launch: ncu `dram__bytes_read.sum + dram__bytes_write.sum` of
-# k_forward on 1480 configuration-2 worlds with the world order (one wave; the capture command is in
+# k_forward on 2220 configuration-2 worlds with the world order (one wave; the capture command is in
 # profiles/k_forward.md), divided by the worlds; the inputs and outputs of the step, nothing re-read
-FORWARD_DRAM_BYTES_PER_WORLD = 847
+FORWARD_DRAM_BYTES_PER_WORLD = 702
 
 
 def cpu_baseline(seconds=10.0, corpus_seconds=6.0):
@@ -450,10 +450,13 @@ def main():
     e1.record(st)
     torch.cuda.synchronize()
     e2e_total = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    per_rank = [total.clone() for _ in range(world)]
     if world > 1:
+        dist.all_gather(per_rank, total)
         dist.all_reduce(total, op=dist.ReduceOp.MAX)
         dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
         dist.all_reduce(fg_ms, op=dist.ReduceOp.MAX)
+    per_rank_ms = [t.item() / a.steps for t in per_rank]
     t_s, e2e_s = total.item() / 1e3, e2e_total.item() / 1e3
     value = world * B * a.steps / t_s
     e2e_value = world * B * a.steps / e2e_s
@@ -505,6 +508,7 @@ def main():
                      "ms_per_step": fg_ms[3].item(), "worlds_per_gpu": jac["B"], "gpu_launches_per_step": 3,
                      "l2": "flushed between timed steps"},
         "kernel_ms": {"median": statistics.median(kern_ms), "min": min(kern_ms), "max": max(kern_ms)},
+        "per_rank_ms_per_step": per_rank_ms,
     }
     if corpus is not None:
         out["corpus"] = corpus

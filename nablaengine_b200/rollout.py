@@ -93,30 +93,39 @@ def main(argv=None):
     inp = rollout_inputs(a.worlds, a.steps, rank, dev)
     inp["worlds_total"] = a.worlds * world
     bptt(inp)  # warm-up (allocator, first launches)
-    times, vec = [], None
+    reduce_stats(*bptt(inp))
+    times, red, vec = [], [], None
     for _ in range(a.repeats):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         loss, g = bptt(inp)
-        vec = reduce_stats(loss, g)
         e1.record()
+        vec = reduce_stats(loss, g)
+        e2.record()
         torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    # per rank the median and the slowest of the repeats, then the maximum over ranks of each
-    t = torch.tensor([sorted(times)[len(times) // 2], max(times)], dtype=torch.float64, device=dev)
+        times.append(e0.elapsed_time(e2))
+        red.append(e1.elapsed_time(e2))
+    # per rank: the median and the slowest rollout, and the median all-reduce (with its wait for the slowest rank);
+    # gathered, then the maximum over ranks of the rollout times
+    mine = torch.tensor([sorted(times)[len(times) // 2], max(times), sorted(red)[len(red) // 2]], dtype=torch.float64,
+                        device=dev)
+    per = [mine.clone() for _ in range(world)]
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_gather(per, mine)
         dist.destroy_process_group()
+    per = torch.stack(per).cpu()
+    med, slow = per[:, 0].max().item(), per[:, 1].max().item()
     if rank == 0:
         v = vec.cpu().tolist()
         print(json.dumps({"metric": "BPTT rollout world-steps/s (fwd+grad)", "n_gpus": world,
                           "worlds_per_gpu": a.worlds,
-                          "steps": a.steps, "repeats": a.repeats, "ms_per_rollout": t[0].item(),
-                          "ms_per_rollout_slowest": t[1].item(),
-                          "value": world * a.worlds * a.steps / (t[0].item() / 1e3), "unit": "world-steps/s",
+                          "steps": a.steps, "repeats": a.repeats, "ms_per_rollout": med,
+                          "ms_per_rollout_slowest": slow,
+                          "per_rank_ms_median": per[:, 0].tolist(), "per_rank_allreduce_ms": per[:, 2].tolist(),
+                          "value": world * a.worlds * a.steps / (med / 1e3), "unit": "world-steps/s",
                           "loss": v[0], "ctrl_grad_norm": v[1] ** 0.5, "rows": v[2], "nonfinite_rows": v[3],
                           "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9}), flush=True)
 

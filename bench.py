@@ -7,10 +7,11 @@ One JSON line on rank 0. A "step" is one control step (4 x 5 ms substeps, Newton
 4096 worlds of BASELINE configuration 2 (seeded synthetic states of the benchmark distribution; rank r uses seed
 1 + r). `value` is device-timed (CUDA events on the launching stream, inputs resident in HBM, an L2 flush between
 steps outside the timed events, max over ranks); `e2e` is the same metric through the public torch API with the
-inputs copied from pinned host memory and the outputs copied back inside the timed region. `roofline` counts the
-step's algorithmic FP32 FLOPs from the kernel's own work counters (nablaengine_b200/flops.py) over the measured kernel
-time; `cpu_baseline` times the float64 CPU oracle (the reference's CPU path, MuJoCo C, is not installed on the box) on
-a bounded sample with all host threads. Under torchrun every rank runs its own 4096 worlds (weak scaling, no
+inputs copied from pinned host memory and the outputs copied back inside the timed region (double-buffered copy
+streams overlapping the copies with the neighbouring steps' compute). `roofline` counts the step's algorithmic FP32
+FLOPs from the kernel's own work counters (nablaengine_b200/flops.py) over the measured kernel time; `cpu_baseline`
+times the float64 CPU oracle (the reference's CPU path, MuJoCo C, is not installed on the box) on a bounded sample
+with all host threads. Under torchrun every rank runs its own 4096 worlds (weak scaling, no
 collective inside the step).
 
 --impl reference: the reference's CPU implementation of the path on the box's host cores (MuJoCo is not installed, so
@@ -426,27 +427,47 @@ def main():
                          device=dev)
     corpus = measure_corpus(dev) if world == 1 and not a.no_corpus else None
 
-    # end to end through the public API: pinned host inputs in, host outputs back, every step
+    # end to end through the public API: pinned host inputs in, host outputs back, every step; the copies run on
+    # their own streams, double-buffered, so step i + 1's inputs cross while step i computes and step i's outputs
+    # come back while step i + 1 computes (every byte of every step still crosses inside the timed region)
     host = [t.cpu().pin_memory() for t in x]
     hout = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = sum(t.numel() * t.element_size() for t in hout)
+    h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dbuf = [[torch.empty_like(t) for t in x] for _ in range(2)]
 
-    def e2e_step():
-        dx = [h.to(dev, non_blocking=True) for h in host]
-        r = torch_ffi.forward(*dx, iterations=ITERATIONS, substeps=SUBSTEPS)
-        for h, o in zip(hout, r):
-            h.copy_(o, non_blocking=True)
+    def e2e_run(n):
+        h2d_stream.wait_stream(st)
+        freed = [None, None]  # per input buffer: the step that read it is done
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(h2d_stream):
+                if freed[b] is not None:
+                    h2d_stream.wait_event(freed[b])
+                for d, h in zip(dbuf[b], host):
+                    d.copy_(h, non_blocking=True)
+                arrived = torch.cuda.Event()
+                arrived.record(h2d_stream)
+            st.wait_event(arrived)
+            r = torch_ffi.forward(*dbuf[b], iterations=ITERATIONS, substeps=SUBSTEPS)
+            freed[b] = torch.cuda.Event()
+            freed[b].record(st)
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(freed[b])
+                for h, o in zip(hout, r):
+                    h.copy_(o, non_blocking=True)
+                    o.record_stream(d2h_stream)
+        st.wait_stream(d2h_stream)
+        st.wait_stream(h2d_stream)
 
-    for _ in range(2):
-        e2e_step()
+    e2e_run(2)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for _ in range(a.steps):
-        e2e_step()
+    e2e_run(a.steps)
     e1.record(st)
     torch.cuda.synchronize()
     e2e_total = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)

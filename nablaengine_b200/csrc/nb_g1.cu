@@ -139,15 +139,20 @@ __global__ void __launch_bounds__(ORD_THREADS) k_order(int nw, const float* __re
 }
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
-// worlds per block of k_adjoint: 10 x 21.9 KB, one block per SM. The worlds meet at a block barrier before every
-// substep, so the SM's warps run the same code together (one instruction stream; measured at B = 4096: 1.06 ms
-// against 1.14 ms with one world per block and no barrier)
+// Worlds per block of k_adjoint: up to AWPB (13 x 16.6 KB, one block per SM). The worlds meet at a block barrier
+// before every substep, so the SM's warps run the same code together (one instruction stream; measured at B = 4096:
+// 1.06 ms against 1.14 ms with one world per block and no barrier). The launch spreads the worlds evenly over whole
+// waves: as many waves as AWPB per SM needs, and per block the fewest worlds that fill them (a block's time grows
+// with its worlds: at B = 4096, 3 waves of 10 worlds ran in 0.588 ms, 2.1 waves of 13 in 0.681 ms, configuration 3).
+// Two instances: blocks of up to AWPB_SMALL worlds run the one compiled for that many (more registers per thread:
+// 0.588 against 0.605 ms for the same 10-world blocks in the AWPB instance), larger blocks the AWPB one.
 #ifndef NB_AWPB
-#define NB_AWPB 10
+#define NB_AWPB 13
 #endif
-constexpr int AWPB = NB_AWPB;
+constexpr int AWPB = NB_AWPB, AWPB_SMALL = 10;
 struct AdjBlock { AWorld s; Adj a; };
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
+static_assert(ASMEM <= 227 * 1024, "one adjoint block per SM");
 
 // The starting cotangent of one adjoint over nsub records tw (the world's first record): the output cotangent is
 // (gq, gv) (qpos form, in any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel')
@@ -209,7 +214,8 @@ __device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int ns
 
 // tape: nw * nsub records; gq_out (B,36) / gv_out (B,35): cotangents of qpos' / qvel'; outputs gq_in (B,36) (qpos
 // form), gv_in (B,35), gctrl (B,29), info (B,) (replay mismatch bits); ctrl: the step's setpoints (clamp_kv 2 only)
-__global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const float* __restrict__ tape,
+template <int MAXW>  // the most worlds a block of this instance takes (its register budget follows)
+__global__ void __launch_bounds__(MAXW * 32) k_adjoint(int nw, int nsub, const float* __restrict__ tape,
                                                        const float* __restrict__ fric, const float* __restrict__ com,
                                                        const float* __restrict__ gq_out,
                                                        const float* __restrict__ gv_out, float* __restrict__ gq_in,
@@ -218,7 +224,7 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
                                                        float clamp_soft, int clamp_kv, int normal) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int w = blockIdx.x * AWPB + warp;
+  int w = blockIdx.x * (int)(blockDim.x >> 5) + warp;  // (blockDim.x / 32 <= AWPB worlds per block)
   const bool active = w < nw;  // inactive warps replay world 0 for the barriers and write nothing
   if (!active) w = 0;
   AdjBlock& blk = reinterpret_cast<AdjBlock*>(smem)[warp];
@@ -258,7 +264,7 @@ __global__ void __launch_bounds__(AWPB * 32) k_adjoint(int nw, int nsub, const f
 constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = NB_JR, JBLK = (JROWS + JR - 1) / JR;
 struct JacRecord {  // what the rows share per record
   AWorld s;
-  float LH[NTRI], dinvH[NV + 1];
+  float LQ[NTRI], dinvQ[NV + 1], LH[NTRI], dinvH[NV + 1];
   AdjShared W;
 };
 struct JacBlock {
@@ -285,12 +291,12 @@ __global__ void __launch_bounds__((JR + 1) * 32) k_jacobian(int nw, int nsub, co
   // while the rows work on record k (one barrier per record)
   auto prepare = [&](int k) {
     JacRecord& R = jb.rec[k & 1];
-    adj_record(R.s, R.W, tw + (size_t)k * REC_WORDS, R.LH, R.dinvH, lane);
+    adj_record(R.s, R.W, tw + (size_t)k * REC_WORDS, R.LQ, R.dinvQ, R.LH, R.dinvH, lane);
     adj_replay(R.s, R.W, lane);
   };
   if (helper) {
     for (int q = 0; q < 2; q++) {
-      for (int e = lane; e < NTRI; e += 32) jb.rec[q].s.L[e] = 0.f;  // L_Q's entries outside its pattern
+      for (int e = lane; e < NTRI; e += 32) jb.rec[q].LQ[e] = 0.f;  // L_Q's entries outside its pattern
       if (lane == 0) jb.rec[q].s.fric = fric[w];
       if (lane < 3) jb.rec[q].s.com[lane] = com[w64 * 3 + lane];
       for (int i = lane; i < NU; i += 32) jb.rec[q].W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
@@ -307,7 +313,7 @@ __global__ void __launch_bounds__((JR + 1) * 32) k_jacobian(int nw, int nsub, co
     } else if (active) {
       JacRecord& R = jb.rec[k & 1];
       const float* rec = tw + (size_t)k * REC_WORDS;
-      adj_row_solve(R.s, R.W, A, rec, R.LH, R.dinvH, lane);
+      adj_row_solve(R.s, R.W, A, rec, R.LQ, R.dinvQ, R.LH, R.dinvH, lane);
       flags |= adj_row_rest(R.s, R.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
     }
   }
@@ -448,6 +454,20 @@ using namespace nbg1;
 static size_t g_prof_smem = 0;  // profile builds: a larger dynamic shared-memory size per block (lower occupancy)
 #endif
 
+// the SM count of each device (nb_g1_upload records it; 148 until then)
+static int g_sms[64];
+static int device_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || g_sms[dev] <= 0) return 148;
+  return g_sms[dev];
+}
+// k_adjoint's worlds per block for nw worlds: the waves AWPB per SM needs, filled evenly
+static int adjoint_worlds_per_block(int nw) {
+  const long long sms = device_sms(), waves = (nw + sms * AWPB - 1) / (sms * AWPB);
+  const long long wpb = (nw + sms * waves - 1) / (sms * waves);
+  return (int)std::max(1ll, std::min<long long>(AWPB, wpb));
+}
+
 extern "C" {
 
 void nb_g1_sizes(long long out[8]) {
@@ -460,10 +480,18 @@ long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : ((long long)nw * (long
 int nb_g1_upload(const float* consts, cudaStream_t stream) {
   (void)consts;
   (void)stream;
-  // the model is compiled in; the per-device work is the kernels' shared-memory opt-in (above 48 KB)
-  cudaError_t e = cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
+  // the model is compiled in; the per-device work is the kernels' shared-memory opt-in (above 48 KB) and the SM count
+  int dev = 0, nsm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev >= 0 && dev < 64) g_sms[dev] = nsm;
+  e = cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_adjoint, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+    e = cudaFuncSetAttribute(k_adjoint<AWPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_adjoint<AWPB_SMALL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(AdjBlock) * AWPB_SMALL));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)JSMEM);
   return (int)e;
@@ -501,7 +529,7 @@ int nb_g1_launch(int dev, long long out[8]) {
   if ((e = cudaSetDevice(dev)) != cudaSuccess) return (int)e;
   e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fb, k_forward, WPB * 32, SMEM);
-  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ab, k_adjoint, AWPB * 32, ASMEM);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ab, k_adjoint<AWPB>, AWPB * 32, ASMEM);
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&jb, k_jacobian, (JR + 1) * 32, JSMEM);
   const cudaError_t e2 = cudaSetDevice(old);
   if (e == cudaSuccess) e = e2;
@@ -557,9 +585,12 @@ int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, cons
   if (!tape || !friction || !com || !gq_out || !gv_out || !gq_in || !gv_in || !gctrl || !info)
     return (int)cudaErrorInvalidValue;
   if (clamp_kv == 2 && !ctrl) return (int)cudaErrorInvalidValue;
-  const int blocks = (nw + AWPB - 1) / AWPB;
-  k_adjoint<<<blocks, AWPB * 32, ASMEM, stream>>>(nw, nsub, tape, friction, com, gq_out, gv_out, gq_in, gv_in, gctrl,
-                                                  info, ctrl, clamp_soft, clamp_kv, normal);
+  const int wpb = adjoint_worlds_per_block(nw);
+  const int blocks = (nw + wpb - 1) / wpb;
+  auto kernel = wpb <= AWPB_SMALL ? k_adjoint<AWPB_SMALL> : k_adjoint<AWPB>;
+  kernel<<<blocks, wpb * 32, sizeof(AdjBlock) * wpb, stream>>>(nw, nsub, tape, friction, com, gq_out, gv_out, gq_in,
+                                                               gv_in, gctrl, info, ctrl, clamp_soft, clamp_kv,
+                                                               normal);
   return (int)cudaGetLastError();
 }
 

@@ -36,32 +36,41 @@ enum : int { ADJ_REPLAY_MISMATCH = 1 << 13 };
 struct __align__(16) AWorld {
   float qpos[NQ], qvel[NV], qacc[NV], com[3], fric;
   float Q[NB][4], X[NB][3];            // body poses
-  float L[NTRI], dinv[NV + 1];         // the tape's factor being solved with
-  struct { struct { float gx[NG][3], gq[NG][4]; } col; } u;  // geom poses
   int ncon, nefc;
   int con_pair[MAXCON];
   unsigned char con_slot[MAXCON], con_row0[MAXCON], con_nrow[MAXCON], con_pad[MAXCON];
 };
+struct GeomPoses { float gx[NG][3], gq[NG][4]; };
 
+// The adjoint's per-world state (k_adjoint: one cotangent per world). Its scratch overlaps by phase: the factor being
+// solved with (the solves, first), the replayed geom poses and the motions of a* and v with the contact batch (the
+// replay and the contacts), and the sweep's subtree sums and parent cotangents (last); each phase writes its part
+// after the previous owner of that space is done with it.
 struct __align__(16) Adj {
   float lam[NV], y[NV], xa[NV], aadv[NV], vb[NV], qb[NV], ub[NU], qout[NV], tmp2[NV], u[NU];
   float ql[NV];                       // direct tangent cotangents (integrator, limits, actuators)
   float om[NB][3], alA[NB][3], aoA[NB][3], alB[NB][3], aoB[NB][3];  // replayed velocities / accelerations
-  float VL[NB][6], VY[NB][6], VA[NB][6], VV[NB][6];                   // body motions at the origin
+  float VL[NB][6], VY[NB][6];         // body motions at the origin of lambda and y
   float dep[NB][24];                  // per body: G_lambda, G_a, G_v (wrenches at the origin), pose wrench
-  float up[NB][18];                   // to the parent: its om, alA, aoA, alB, aoB cotangents and the relative-position
-                                      // force rbar (applied as -rbar at the parent's origin)
-  union {
-    float sub[NB][36];                // subtree sums: W_A, W_B, G_lambda, G_a, G_v, P (6 each) (the sweep)
-    struct {
-      float cw[32][30];               // a batch of 32 contacts' wrenches (the contact phase, before the sweep)
-      int cbody[32];                  // their bodies: b1 | b2 << 8
-    };
-  };
   float ax[NV][3];                    // dof axes (world)
+  float dinv[NV + 1];                 // the factor's inverse diagonal (L_Q's, then L_H's)
   unsigned clamp_lo, clamp_hi;
   unsigned zone[NEFC / 32];           // the record's zone bits (row r quadratic: bit r & 31 of word r / 32)
   int nlim_tape, flags, normal, pad_;  // normal: the self-contact normal derivative option (0..3)
+  union {
+    float L[NTRIP];                   // the solves: L_Q (tree-block order), then L_H
+    struct {                          // the replay and the contacts
+      float cw[32][30];               // a batch of 32 contacts' wrenches
+      int cbody[32];                  // their bodies: b1 | b2 << 8
+      float VA[NB][6], VV[NB][6];     // body motions at the origin of a* and v
+      GeomPoses col;                  // geom poses
+    };
+    struct {                          // the sweep
+      float sub[NB][36];              // subtree sums: W_A, W_B, G_lambda, G_a, G_v, P (6 each)
+      float up[NB][18];               // to the parent: its om, alA, aoA, alB, aoB cotangents and the relative-position
+                                      // force rbar (applied as -rbar at the parent's origin)
+    };
+  };
 #ifdef NB_PROFILE
   long long prof_t;
 #endif
@@ -70,6 +79,7 @@ struct __align__(16) Adj {
 // The Jacobian's split of Adj: what the rows (cotangents) of one world share per record, and each row's own state
 struct __align__(16) AdjShared {
   float xa[NV], aadv[NV], u[NU];
+  GeomPoses col;                      // geom poses
   float om[NB][3], alA[NB][3], aoA[NB][3], alB[NB][3], aoB[NB][3];
   float VA[NB][6], VV[NB][6];
   float ax[NV][3];
@@ -305,7 +315,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const fl
     const int dim = ldi(g1_pair_dim + pr);
     const float mu = dim != 3 ? 0.f : (ldi(g1_pair_foot + pr) ? s.fric : ld(g1_pair_mu + pr));
     float p1[3], p2[3];
-    for (int k = 0; k < 3; k++) { p1[k] = s.u.col.gx[g1][k]; p2[k] = s.u.col.gx[g2][k]; }
+    for (int k = 0; k < 3; k++) { p1[k] = W.col.gx[g1][k]; p2[k] = W.col.gx[g2][k]; }
     const float r1 = ld(g1_geom_size + 3 * g1), r2 = ld(g1_geom_size + 3 * g2);
     // geometry: the two sphere-core points (v1 on body 1, v2 on body 2), or the plane case
     float dist = 0.f, pos[3], fr[9], nrm[3], v1[3], v2[3], ax[3] = {0.f, 0.f, 0.f}, proj = 0.f;
@@ -317,9 +327,9 @@ __device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const fl
     float ma = 1.f, mb = 0.f, mc = 1.f, x1 = 0.f, x2 = 0.f;
     bool fr1 = false, fr2 = false;
     if (plane) {
-      zaxis(s.u.col.gq[g1], nrm);
+      zaxis(W.col.gq[g1], nrm);
       if (t2 == 3) {
-        zaxis(s.u.col.gq[g2], ax);
+        zaxis(W.col.gq[g2], ax);
         const float hl = ld(g1_geom_size + 3 * g2 + 1);
         for (int k = 0; k < 3; k++) v2[k] = slot == 0 ? p2[k] + hl * ax[k] : p2[k] - hl * ax[k];
         const float na = dot3(nrm, ax);
@@ -344,7 +354,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const fl
         for (int k = 0; k < 3; k++) { v1[k] = p1[k]; v2[k] = p2[k]; }
       } else if (t1 == 2 && t2 == 3) {
         const float hl = ld(g1_geom_size + 3 * g2 + 1);
-        zaxis(s.u.col.gq[g2], axu);
+        zaxis(W.col.gq[g2], axu);
         for (int k = 0; k < 3; k++) { sa[k] = p2[k] - axu[k] * hl; sb[k] = 2.f * hl * axu[k]; sd[k] = p1[k] - sa[k]; }
         ma = dot3(sb, sb) + 1e-6f;
         const float raw = dot3(sd, sb) / ma;
@@ -353,8 +363,8 @@ __device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const fl
         for (int k = 0; k < 3; k++) { v1[k] = p1[k]; v2[k] = sa[k] + x2 * sb[k]; }
       } else {
         const float hl1 = ld(g1_geom_size + 3 * g1 + 1), hl2 = ld(g1_geom_size + 3 * g2 + 1);
-        zaxis(s.u.col.gq[g1], sa);
-        zaxis(s.u.col.gq[g2], sb);
+        zaxis(W.col.gq[g1], sa);
+        zaxis(W.col.gq[g2], sb);
         for (int k = 0; k < 3; k++) { sa[k] *= hl1; sb[k] *= hl2; sd[k] = p1[k] - p2[k]; }
         ma = dot3(sa, sa); mb = -dot3(sa, sb); mc = dot3(sb, sb);
         const float uu = -dot3(sa, sd), vv = dot3(sb, sd);
@@ -927,14 +937,23 @@ __device__ __forceinline__ void copy_factor_tb(float* dst, const float* src, int
 }
 
 // One substep of the adjoint from its tape record rec. What every cotangent of the record shares: adj_record (the
-// record's state into s and W; with LH given also both factors: L_Q into s.L / s.dinv, L_H into LH / dinvH) and
+// record's state into s and W; with the factors' buffers given also both factors: L_Q into LQ / dinvQ, L_H into
+// LH / dinvH) and
 // adj_replay (the replayed poses, velocities and accelerations, the motions of a* and v, the geom poses and contact
 // rows). One cotangent, A.qout / A.vb in (the substep output's tangent and velocity cotangents), out the input's
-// (A.qout, A.vb), A.ub accumulating the ctrl gradient: adj_row_solve (the integrator and both solves; without LH it
-// copies each factor into s.L just before its solve) and adj_row_rest. block_sync: every warp of the block calls adj_row together; a block barrier before the limit
+// (A.qout, A.vb), A.ub accumulating the ctrl gradient: adj_row_solve (the integrator and both solves; without the
+// factors' buffers it copies each factor into the state's own scratch just before its solve) and adj_row_rest. block_sync: every warp of the block calls adj_row together; a block barrier before the limit
 // rows and the sweep re-aligns the worlds after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
+// the solve scratch of a cotangent's state: k_adjoint's Adj holds its own (the factor is copied in just before each
+// solve); the Jacobian's rows (AdjRow) solve with their record's factors, held once per block
+__device__ __forceinline__ float* solve_scratch(Adj& A) { return A.L; }
+__device__ __forceinline__ float* solve_scratch_dinv(Adj& A) { return A.dinv; }
+__device__ __forceinline__ float* solve_scratch(AdjRow&) { return nullptr; }
+__device__ __forceinline__ float* solve_scratch_dinv(AdjRow&) { return nullptr; }
+
 template <class SH>
-__device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, float* LH, float* dinvH, int lane) {
+__device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, float* LQ, float* dinvQ, float* LH,
+                                           float* dinvH, int lane) {
   for (int i = lane; i < NQ; i += 32) s.qpos[i] = rec[T_QPOS + i];
   for (int i = lane; i < NV; i += 32) {
     s.qvel[i] = rec[T_QVEL + i];
@@ -957,9 +976,9 @@ __device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, f
     s.con_slot[c] = (unsigned char)(e >> 9);
   }
   if (LH) {
-    copy_factor_tb(s.L, rec + T_LQ, lane, false);  // (s.L holds L_Q only: zeroed once)
+    copy_factor_tb(LQ, rec + T_LQ, lane, false);  // (LQ holds L_Q only: zeroed once)
     copy_factor(LH, rec + T_LH, lane);
-    for (int i = lane; i < NV; i += 32) { s.dinv[i] = rec[T_DINVQ + i]; dinvH[i] = rec[T_DINVH + i]; }
+    for (int i = lane; i < NV; i += 32) { dinvQ[i] = rec[T_DINVQ + i]; dinvH[i] = rec[T_DINVH + i]; }
   }
   __syncwarp();
 }
@@ -978,8 +997,8 @@ __device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
                          ld(g1_geom_quat + 4 * g + 3)};
     float t[3];
     qrot(s.Q[b], gp, t);
-    for (int k = 0; k < 3; k++) s.u.col.gx[g][k] = s.X[b][k] + t[k];
-    qmul(s.Q[b], gq, s.u.col.gq[g]);
+    for (int k = 0; k < 3; k++) W.col.gx[g][k] = s.X[b][k] + t[k];
+    qmul(s.Q[b], gq, W.col.gq[g]);
   }
   {
     const int ncon = s.ncon;
@@ -1004,8 +1023,8 @@ __device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
 }
 
 template <class SH, class RW>
-__device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, const float* rec, const float* LH,
-                                              const float* dinvH, int lane) {
+__device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, const float* rec, const float* LQ,
+                                              const float* dinvQ, const float* LH, const float* dinvH, int lane) {
   const float h = G1_TIMESTEP;
   for (int i = lane; i < NV; i += 32) A.ql[i] = 0.f;
   __syncwarp();
@@ -1052,21 +1071,23 @@ __device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, con
   }
   PROF(A, 0);
   // y = (M + h kv)^-1 abar_adv with L_Q; abar* = abar_adv - h kv y
-  if (!LH) {
-    copy_factor_tb(s.L, rec + T_LQ, lane, true);
-    for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVQ + i];
+  float* L = solve_scratch(A);  // (without the record's factors: each copied here just before its solve)
+  float* dinv = solve_scratch_dinv(A);
+  if (!LQ) {
+    copy_factor_tb(L, rec + T_LQ, lane, true);
+    for (int i = lane; i < NV; i += 32) dinv[i] = rec[T_DINVQ + i];
   }
   for (int i = lane; i < NV; i += 32) A.lam[i] = A.y[i];
   __syncwarp();
-  chol_solve<true>(s.L, s.dinv, A.y, lane);  // L_Q is in tree-block order
+  chol_solve<true>(LQ ? LQ : L, LQ ? dinvQ : dinv, A.y, lane);  // L_Q is in tree-block order
   for (int i = lane; i < NV; i += 32) A.lam[i] -= h * ld(g1_dof_kv + i) * A.y[i];
   // A2: lambda = H^-1 abar* with L_H
   if (!LH) {
     __syncwarp();
-    copy_factor(s.L, rec + T_LH, lane);
-    for (int i = lane; i < NV; i += 32) s.dinv[i] = rec[T_DINVH + i];
+    copy_factor(L, rec + T_LH, lane);
+    for (int i = lane; i < NV; i += 32) dinv[i] = rec[T_DINVH + i];
     __syncwarp();
-    chol_solve(s.L, s.dinv, A.lam, lane);
+    chol_solve(L, dinv, A.lam, lane);
   } else {
     __syncwarp();
     chol_solve(LH, dinvH, A.lam, lane);
@@ -1126,8 +1147,8 @@ __device__ __forceinline__ int adj_row_rest(AWorld& s, const SH& W, RW& A, const
 // the adjoint's substep (one cotangent per world): both parts in one warp, the factors copied as they are needed
 __device__ __forceinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
                                            float (*cw)[30], int lane, bool block_sync = false) {
-  adj_record(s, A, rec, nullptr, nullptr, lane);
-  adj_row_solve(s, A, A, rec, nullptr, nullptr, lane);
+  adj_record(s, A, rec, nullptr, nullptr, nullptr, nullptr, lane);
+  adj_row_solve(s, A, A, rec, nullptr, nullptr, nullptr, nullptr, lane);
   adj_replay(s, A, lane);
   return adj_row_rest(s, A, A, rec, clamp_kv, clamp_soft, cw, lane, block_sync);
 }

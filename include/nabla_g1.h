@@ -72,9 +72,10 @@ int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, cons
 /* The full step Jacobian from a tape: jac (B,71,99) float32, row r = d(output r) / d(inputs) with the outputs
  * qpos' (36, qpos form) then qvel' (35) and the inputs in the tangent basis: qpos tangent (35: root position, root
  * rotation vector in the local frame, hinges), qvel (35), ctrl (29); info (B,) int32: the replay flags ORed over the
- * rows. Arguments otherwise as nb_g1_adjoint; one launch (one warp per world and row). No counterpart in the
- * reference's ABI: its Jacobian is 71 calls of `<pfx>_adjoint` with unit cotangents plus the qpos-to-tangent map
- * (scripts/paper_bench/ours.py:99-110, benchmarks/bench/adapters/base.py:254-277); row r here equals that row. */
+ * rows. Arguments otherwise as nb_g1_adjoint; one launch (one block per world, one lane per tangent-basis cotangent
+ * of the output). No counterpart in the reference's ABI: its Jacobian is 71 calls of `<pfx>_adjoint` with unit
+ * cotangents plus the qpos-to-tangent map (scripts/paper_bench/ours.py:99-110, benchmarks/bench/adapters/base.py:
+ * 254-277); row r here equals that row within float32 rounding (the same VJP, its operations in another order). */
 int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
                    float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal);
 
@@ -116,8 +117,8 @@ int nb_g1_last_forward(cudaStream_t stream, int nw, const int* info, unsigned* r
 
 /* The launch shapes on device dev (after nb_g1_upload on it): out[8] = [the forward's dynamic shared memory per
  * block (bytes), the forward's resident worlds per SM, the adjoint's shared memory per block, its resident worlds per
- * SM, the Jacobian's shared memory per block, its resident output rows per SM, the device's SM count, 0]; a world or
- * row count of 0 means the kernel does not fit the device. Restores the caller's current device. Replaces
+ * SM, the Jacobian's shared memory per block, its resident cotangents (Jacobian rows in flight) per SM, the device's
+ * SM count, 0]; a world or row count of 0 means the kernel does not fit the device. Restores the caller's current device. Replaces
  * `int <pfx>_launch(int dev, long long* o)` (src/nablaengine/jax_ffi.py:243-253: the adjoint's shared memory and
  * resident worlds per SM). */
 int nb_g1_launch(int dev, long long out[8]);

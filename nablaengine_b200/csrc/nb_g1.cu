@@ -9,6 +9,7 @@
 #include "nb_g1_step.cuh"
 #include "nb_g1_adjoint.cuh"
 #include "nb_g1_kin.cuh"
+#include "nb_g1_jac.cuh"
 
 namespace nbg1 {
 
@@ -253,75 +254,77 @@ __global__ void __launch_bounds__(MAXW * 32) k_adjoint(int nw, int nsub, const f
 }
 
 // The step Jacobian (B, 71, 99): row r = the VJP of output r (qpos' in qpos form 0..35, qvel' 36..70) in the
-// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). A block holds JR rows of one world (one warp each, JBLK
-// blocks per world) and what the rows share per record (the record's state, both factors and the replay), prepared
-// by a helper warp one record ahead in a second buffer while the rows work on the current one. The rows keep only
-// their cotangents' state (AdjRow, 12.3 KB), so twelve fit an SM. info (B,): the replay flags ORed over the rows
-// (zeroed by the launcher).
-#ifndef NB_JR
-#define NB_JR 12
-#endif
-constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU, JR = NB_JR, JBLK = (JROWS + JR - 1) / JR;
-struct JacRecord {  // what the rows share per record
-  AWorld s;
-  float LQ[NTRI], dinvQ[NV + 1], LH[NTRI], dinvH[NV + 1];
-  AdjShared W;
-};
-struct JacBlock {
-  JacRecord rec[2];  // the record the rows are on and the next one, which the helper prepares meanwhile
-  AdjRow r[JR];
-};
-constexpr size_t JSMEM = sizeof(JacBlock);
-static_assert(JSMEM <= 227 * 1024, "one Jacobian block per SM");
-__global__ void __launch_bounds__((JR + 1) * 32) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
-                                                            const float* __restrict__ fric,
-                                                            const float* __restrict__ com, float* __restrict__ jac,
-                                                            int* __restrict__ info, const float* __restrict__ ctrl,
-                                                            float clamp_soft, int clamp_kv, int normal) {
+// tangent columns (qpos tangent 35 | qvel 35 | ctrl 29). One block per world, one lane per right-hand side (the 70
+// tangent-basis cotangents of the output; nb_g1_jac.cuh), the record's shared terms prepared once per record by the
+// block. info (B,): the replay flags (zeroed by the launcher).
+constexpr int JROWS = NQ + NV, JCOLS = 2 * NV + NU;
+constexpr size_t JSMEM = sizeof(JBlock);
+static_assert(2 * (JSMEM + 1024) <= 228 * 1024, "two Jacobian blocks per SM");
+__global__ void __launch_bounds__(JTHREADS, 2) k_jacobian(int nw, int nsub, const float* __restrict__ tape,
+                                                          const float* __restrict__ fric,
+                                                          const float* __restrict__ com, float* __restrict__ jac,
+                                                          int* __restrict__ info, const float* __restrict__ ctrl,
+                                                          float clamp_soft, int clamp_kv, int normal) {
   extern __shared__ __align__(16) unsigned char smem[];
-  JacBlock& jb = *reinterpret_cast<JacBlock*>(smem);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool helper = warp == JR;
-  const int w = blockIdx.x / JBLK, row = (blockIdx.x % JBLK) * JR + warp;
-  const bool active = !helper && row < JROWS;  // (the last block's spare row stays for the barriers)
+  __shared__ float qcoef[12];  // the quaternion rows: row 3 + c = sum_k qcoef[3 c + k] (rotation cotangent k)
+  JBlock& B = *reinterpret_cast<JBlock*>(smem);
+  const int t = threadIdx.x, w = blockIdx.x;
   const size_t w64 = (size_t)w;
   const float* tw = tape + w64 * nsub * REC_WORDS;
-  AdjRow& A = jb.r[helper ? 0 : warp];
-  // the helper loads and replays record k into rec[k & 1]: the last record before the loop, then record k - 1
-  // while the rows work on record k (one barrier per record)
-  auto prepare = [&](int k) {
-    JacRecord& R = jb.rec[k & 1];
-    adj_record(R.s, R.W, tw + (size_t)k * REC_WORDS, R.LQ, R.dinvQ, R.LH, R.dinvH, lane);
-    adj_replay(R.s, R.W, lane);
-  };
-  if (helper) {
-    for (int q = 0; q < 2; q++) {
-      for (int e = lane; e < NTRI; e += 32) jb.rec[q].LQ[e] = 0.f;  // L_Q's entries outside its pattern
-      if (lane == 0) jb.rec[q].s.fric = fric[w];
-      if (lane < 3) jb.rec[q].s.com[lane] = com[w64 * 3 + lane];
-      for (int i = lane; i < NU; i += 32) jb.rec[q].W.u[i] = ctrl ? ctrl[w64 * NU + i] : 0.f;
-    }
-    __syncwarp();
-    prepare(nsub - 1);
+  const int j = t < JNR ? t : JNR + (t & 1);  // the lane's right-hand side (spare lanes: the spare columns)
+  float* x = B.rhs + j;
+  for (int e = t; e < NTRIP; e += JTHREADS) B.R.LQ[e] = 0.f;  // L_Q's entries off its pattern
+  if (t == 0) B.R.flags = 0;
+  for (int i = 0; i < NV; i++) {
+    JX(JO_Q, i) = j < NV && i == j ? 1.f : 0.f;
+    JX(JO_V, i) = j >= NV && j < JNR && i == j - NV ? 1.f : 0.f;
   }
-  if (active) adj_row_init(A, tw, nsub, nullptr, nullptr, row, normal, lane);
-  int flags = 0;
+  for (int i = 0; i < NU; i++) JX(JO_U, i) = 0.f;
+  if (t == 0) {  // the output cotangent of a qpos' quaternion entry in the rotation tangent: 1/2 Im(q'* e_c) / |q'|^2
+    const float* last = tw + (size_t)(nsub - 1) * REC_WORDS;
+    const float h = G1_TIMESTEP;
+    float q[4] = {last[T_QPOS + 3], last[T_QPOS + 4], last[T_QPOS + 5], last[T_QPOS + 6]};
+    const float wv[3] = {last[T_QVEL + 3] + h * last[T_AADV + 3], last[T_QVEL + 4] + h * last[T_AADV + 4],
+                         last[T_QVEL + 5] + h * last[T_AADV + 5]};
+    const float nwv = sqrtf(dot3(wv, wv));
+    if (nwv > 0.f) {
+      float sa, ca;
+      sincosf(0.5f * h * nwv, &sa, &ca);
+      const float dq[4] = {ca, sa * wv[0] / nwv, sa * wv[1] / nwv, sa * wv[2] / nwv};
+      float o[4];
+      qmul(q, dq, o);
+      const float on = sqrtf(o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3]);
+      for (int k = 0; k < 4; k++) q[k] = o[k] / on;
+    }
+    const float qc[4] = {q[0], -q[1], -q[2], -q[3]};
+    const float n2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3];
+    for (int c = 0; c < 4; c++) {
+      const float g[4] = {c == 0 ? 1.f : 0.f, c == 1 ? 1.f : 0.f, c == 2 ? 1.f : 0.f, c == 3 ? 1.f : 0.f};
+      float m[4];
+      qmul(qc, g, m);
+      for (int k = 0; k < 3; k++) qcoef[3 * c + k] = 0.5f * m[1 + k] / n2;
+    }
+  }
   for (int k = nsub - 1; k >= 0; k--) {
-    __syncthreads();  // record k is ready, and every row is done with record k + 1's buffer (the helper's next)
-    if (helper) {
-      if (k > 0) prepare(k - 1);
-    } else if (active) {
-      JacRecord& R = jb.rec[k & 1];
-      const float* rec = tw + (size_t)k * REC_WORDS;
-      adj_row_solve(R.s, R.W, A, rec, R.LQ, R.dinvQ, R.LH, R.dinvH, lane);
-      flags |= adj_row_rest(R.s, R.W, A, rec, clamp_kv, clamp_soft, A.cw, lane, false);
-    }
+    __syncthreads();  // (the previous record's cotangents are done with the shared terms and lambda / y)
+    jac_prep(B, tw + (size_t)k * REC_WORDS, fric + w, com + 3 * w64, ctrl ? ctrl + w64 * NU : nullptr, clamp_soft,
+             clamp_kv, normal, t);
+    jac_rhs_solves(B.R, x);
+    jac_rhs_sweep(B.R, x);
   }
-  if (!active) return;
-  float* out = jac + (w64 * JROWS + row) * JCOLS;
-  for (int i = lane; i < NV; i += 32) { out[i] = A.qout[i]; out[NV + i] = A.vb[i]; }
-  for (int i = lane; i < NU; i += 32) out[2 * NV + i] = A.ub[i];
-  if (lane == 0 && flags) atomicOr(info + w, flags);
+  __syncthreads();
+  float* out = jac + w64 * JROWS * JCOLS;
+  for (int e = t; e < JROWS * JCOLS; e += JTHREADS) {
+    const int r = e / JCOLS, c = e - r * JCOLS;
+    const float* row = B.rhs + (c < NV ? JO_Q + c : (c < 2 * NV ? JO_V + c - NV : JO_U + c - 2 * NV)) * JS;
+    float v;
+    if (r < 3) v = row[r];
+    else if (r < 7) v = qcoef[3 * (r - 3)] * row[3] + qcoef[3 * (r - 3) + 1] * row[4] + qcoef[3 * (r - 3) + 2] * row[5];
+    else if (r < NQ) v = row[r - 1];
+    else v = row[NV + r - NQ];
+    out[e] = v;
+  }
+  if (t == 0 && B.R.flags) atomicOr(info + w, B.R.flags);
 }
 // ---- diagnostics: device counters (uint64, DIAG order of the Python layer) added by one small kernel per call ------
 enum : int {
@@ -477,6 +480,25 @@ void nb_g1_sizes(long long out[8]) {
 
 long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : ((long long)nw * (long long)sizeof(int) + 15) / 16 * 16; }
 
+// k_jacobian's leaf-to-root pass visits bodies NB - 1 .. 1 and parks at most one hand-over at a time: every parent
+// precedes its children, and a body whose parent is not visited next hands over to the parent already parked, if any
+static bool jac_tree_ok() {
+  int parent[NB];
+  if (cudaMemcpyFromSymbol(parent, g1_body_parent, sizeof(parent)) != cudaSuccess) return false;
+  int parked = -1;
+  for (int b = NB - 1; b >= 1; b--) {
+    if (parked == b) parked = -1;
+    if (b < 2) continue;
+    const int p = parent[b];
+    if (p < 1 || p >= b) return false;
+    if (p != b - 1) {
+      if (parked != -1 && parked != p) return false;
+      parked = p;
+    }
+  }
+  return parked == -1;
+}
+
 int nb_g1_upload(const float* consts, cudaStream_t stream) {
   (void)consts;
   (void)stream;
@@ -494,6 +516,7 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
                              (int)(sizeof(AdjBlock) * AWPB_SMALL));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_jacobian, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)JSMEM);
+  if (e == cudaSuccess && !jac_tree_ok()) e = cudaErrorInvalidValue;
   return (int)e;
 }
 
@@ -530,12 +553,12 @@ int nb_g1_launch(int dev, long long out[8]) {
   e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fb, k_forward, WPB * 32, SMEM);
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ab, k_adjoint<AWPB>, AWPB * 32, ASMEM);
-  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&jb, k_jacobian, (JR + 1) * 32, JSMEM);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&jb, k_jacobian, JTHREADS, JSMEM);
   const cudaError_t e2 = cudaSetDevice(old);
   if (e == cudaSuccess) e = e2;
   if (e != cudaSuccess) return (int)e;
   const long long v[8] = {(long long)SMEM, (long long)fb * WPB, (long long)ASMEM, (long long)ab * AWPB,
-                          (long long)JSMEM, (long long)jb * JR, nsm, 0};
+                          (long long)JSMEM, (long long)jb * JNR, nsm, 0};
   for (int i = 0; i < 8; i++) out[i] = v[i];
   return 0;
 }
@@ -570,9 +593,8 @@ int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, con
   if (clamp_kv == 2 && !ctrl) return (int)cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(info, 0, sizeof(int) * (size_t)nw, stream);
   if (e != cudaSuccess) return (int)e;
-  const unsigned jblocks = (unsigned)((long long)nw * JBLK);
-  k_jacobian<<<jblocks, (JR + 1) * 32, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl,
-                                                                 clamp_soft, clamp_kv, normal);
+  k_jacobian<<<(unsigned)nw, JTHREADS, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl, clamp_soft,
+                                                         clamp_kv, normal);
   return (int)cudaGetLastError();
 }
 

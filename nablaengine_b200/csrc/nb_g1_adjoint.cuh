@@ -76,7 +76,7 @@ struct __align__(16) Adj {
 #endif
 };
 
-// The Jacobian's split of Adj: what the rows (cotangents) of one world share per record, and each row's own state
+// What every cotangent of a record shares (the Jacobian's preparation: its per-record replay beside AWorld)
 struct __align__(16) AdjShared {
   float xa[NV], aadv[NV], u[NU];
   GeomPoses col;                      // geom poses
@@ -86,23 +86,6 @@ struct __align__(16) AdjShared {
   unsigned clamp_lo, clamp_hi;
   unsigned zone[NEFC / 32];
   int nlim_tape, pad_[3];
-};
-struct __align__(16) AdjRow {
-  float lam[NV], y[NV], vb[NV], qb[NV], ub[NU], qout[NV], tmp2[NV], ql[NV];
-  float VL[NB][6], VY[NB][6];
-  float dep[NB][24];
-  float up[NB][18];
-  union {
-    float sub[NB][36];
-    struct {
-      float cw[32][30];
-      int cbody[32];
-    };
-  };
-  int flags, normal, pad_[2];
-#ifdef NB_PROFILE
-  long long prof_t;
-#endif
 };
 
 // ---- replay ---------------------------------------------------------------------------------------------------------
@@ -296,18 +279,19 @@ __device__ __forceinline__ void impedance_d(const float* solimp, float pos, floa
 }
 
 // ---- the rows' terms ------------------------------------------------------------------------------------------------
-// Contacts (lane = contact): replay the tape's contact (pair, slot) from the geom poses, its rows' forces at the
-// tape's zones, the cotangents of J x for x = lambda, a*, v as forces at the contact point (deposited as wrenches on
-// the two bodies) and the geometry's pose wrenches. Returns the replay mismatch flag of this lane.
-template <class SH, class RW>
-__device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const float* rec, float (*cw)[30], int c0,
-                                        int lane) {
-  const int ncon = s.ncon;
-  const int c = c0 + lane;
-  float out[30];
-  for (int k = 0; k < 30; k++) out[k] = 0.f;
+// One contact's terms (one thread, no warp operations): replay the tape's contact (pair, slot) from the geom poses,
+// its rows' forces at the tape's zones, the cotangents of J x for x = lambda, a*, v as forces at the contact point
+// (wrenches at the origin, deposited on the two bodies) and the geometry's pose wrenches. Everything but lambda's
+// part is the same for every cotangent and is computed once; the terms of lambda are linear in its relative motion
+// between the two bodies, dV = V^lambda(b2) - V^lambda(b1) (angular, linear at the origin), and are evaluated NEVAL
+// times: dvl(e, b1, b2, dV) gives the e-th dV, put(e, out, b) takes out[30]: G(lambda), G(a*), G(v) (out[0..17], G as
+// deposited on body 2: G(lambda) does not depend on dV, and G(v) is b G(a*) up to rounding, b the rows' damping),
+// the pose wrenches of body 2 (out[18..23]) and body 1 (out[24..29]; zero for a plane). Returns the replay mismatch
+// flag (the replayed distance is not negative).
+template <int NEVAL, class SH, class DV, class PUT>
+__device__ __forceinline__ int contact_terms(const AWorld& s, const SH& W, int c, int normal, DV dvl, PUT put) {
   int mismatch = 0;
-  if (c < ncon) {
+  {
     const int pr = s.con_pair[c], slot = s.con_slot[c];
     const int g1 = ldi(g1_pair_g1 + pr), g2 = ldi(g1_pair_g2 + pr);
     const int t1 = ldi(g1_geom_type + g1), t2 = ldi(g1_geom_type + g2);
@@ -383,7 +367,7 @@ __device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const fl
             x1 = fminf(fmaxf(raw, -1.f), 1.f);
           }
           // both free on near-parallel axes, with a normal option: both held (sin^2 of the angle < 1.2e-3)
-          if (A.normal != 0 && fr1 && fr2 && det < 1.2e-3f * ma * mc) fr1 = fr2 = false;
+          if (normal != 0 && fr1 && fr2 && det < 1.2e-3f * ma * mc) fr1 = fr2 = false;
         } else if (slot < 2) {
           x1 = slot == 0 ? 1.f : -1.f;
           const float raw = slot == 0 ? (vv - mb) / mc : (vv + mb) / mc;
@@ -413,152 +397,210 @@ __device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const fl
     impedance_d(si, dist, &imp, &dimp);
     const float R = fmaxf(1e-15f, iw * (1.f - imp) / imp), D = 1.f / R;
     const float dD = R > 1e-15f ? D * D * iw / (imp * imp) : 0.f;  // dD / dimp = 1 / (iw (1 - imp)^2)
-    // relative point velocities u(x) = dV_lin + dW x pos for x = lambda, a*, v; jd_d(x) = fr_d . u(x)
-    float u[3][3], jd[3][3];
-    for (int m = 0; m < 3; m++) {
-      const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? W.VA : W.VV);
+    // the motions of a* (m = 1) and v (m = 2) at the contact point: u = dV_lin + dW x pos, jd_d = fr_d . u; the
+    // rows' Bt = J_t a + b J_t v + k imp dist and Abar = -D Bt, the cotangent of J_t lambda, which gives G(lambda)
+    float u[3][3], jd[3][3], dW[3][3];
+    for (int m = 1; m < 3; m++) {
+      const float(*B)[6] = m == 1 ? W.VA : W.VV;
       float dV[6], t[3];
       for (int k = 0; k < 6; k++) dV[k] = B[b2][k] - B[b1][k];
       cross(dV, pos, t);
-      for (int k = 0; k < 3; k++) u[m][k] = dV[3 + k] + t[k];
+      for (int k = 0; k < 3; k++) { u[m][k] = dV[3 + k] + t[k]; dW[m][k] = dV[k]; }
       for (int dd = 0; dd < 3; dd++) jd[m][dd] = dot3(fr + 3 * dd, u[m]);
     }
-    // psi_c = -D sum_t (J_t lambda) (J_t a + b J_t v + k imp dist) over the tape's quadratic rows
+    // psi_c = -D sum_t (J_t lambda) (J_t a + b J_t v + k imp dist) over the tape's quadratic rows (at most 4)
     const int r0 = s.con_row0[c], nr = s.con_nrow[c];
-    float jdb[3][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
-    float Dbar = 0.f, kterm_bar = 0.f;
     const float kterm = kk * imp * dist;
-    for (int t = 0; t < nr; t++) {
+    float jdb0[3] = {0.f, 0.f, 0.f}, Bt[4] = {0.f, 0.f, 0.f, 0.f};
+    unsigned quad = 0u;  // bit t: row r0 + t is quadratic
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      if (t >= nr) break;
       const int r = r0 + t;
       if (!((W.zone[r >> 5] >> (r & 31)) & 1u)) continue;
+      quad |= 1u << t;
       const float sg = (t & 1) ? -1.f : 1.f;
       const int kd = 1 + (t >> 1);
       const float w1 = dim == 3 ? sg * mu : 0.f;
-      const float Jl = jd[0][0] + w1 * jd[0][kd], Ja = jd[1][0] + w1 * jd[1][kd], Jv = jd[2][0] + w1 * jd[2][kd];
-      const float Bt = Ja + bb * Jv + kterm;
-      const float Abar = -D * Bt, Bbar = -D * Jl;
-      Dbar -= Jl * Bt;
-      kterm_bar += Bbar;
-      // J_t x = jd_0(x) + w1 jd_kd(x)
-      const float xb[3] = {Abar, Bbar, bb * Bbar};
-      for (int m = 0; m < 3; m++) {
-        jdb[m][0] += xb[m];
-        if (dim == 3) jdb[m][kd] += w1 * xb[m];
-      }
+      const float Ja = jd[1][0] + w1 * jd[1][kd], Jv = jd[2][0] + w1 * jd[2][kd];
+      Bt[t] = Ja + bb * Jv + kterm;
+      const float Abar = -D * Bt[t];
+      jdb0[0] += Abar;
+      if (dim == 3) jdb0[kd] += w1 * Abar;
     }
-    // back through jd = fr . u: ubar(x), frame cotangents, pos cotangent
-    float frb[9], pb[3] = {0.f, 0.f, 0.f};
-    for (int k = 0; k < 9; k++) frb[k] = 0.f;
-    for (int m = 0; m < 3; m++) {
-      float ub[3] = {0.f, 0.f, 0.f};
+    float out[30];
+    {
+      float ub0[3] = {0.f, 0.f, 0.f}, t[3];
       for (int dd = 0; dd < 3; dd++)
-        for (int k = 0; k < 3; k++) { ub[k] += jdb[m][dd] * fr[3 * dd + k]; frb[3 * dd + k] += jdb[m][dd] * u[m][k]; }
-      // u = dV_lin + dW x pos: the wrench (pos x ubar, ubar); pos gets ubar x dW
-      const float(*B)[6] = m == 0 ? A.VL : (m == 1 ? W.VA : W.VV);
-      float dW[3], t[3];
-      for (int k = 0; k < 3; k++) dW[k] = B[b2][k] - B[b1][k];
-      cross(ub, dW, t);
-      for (int k = 0; k < 3; k++) pb[k] += t[k];
-      cross(pos, ub, t);
-      for (int k = 0; k < 3; k++) { out[6 * m + k] = t[k]; out[6 * m + 3 + k] = ub[k]; }
+        for (int k = 0; k < 3; k++) ub0[k] += jdb0[dd] * fr[3 * dd + k];
+      cross(pos, ub0, t);
+      for (int k = 0; k < 3; k++) { out[k] = t[k]; out[3 + k] = ub0[k]; }
     }
-    // dist: through imp (D, k imp dist)
-    const float distb = kterm_bar * kk * (imp + dimp * dist) + Dbar * dD * dimp;
-    // geometry VJP -> pose forces at v1 (body 1) and v2 (body 2) and moments
-    float v1b[3] = {0.f, 0.f, 0.f}, v2b[3] = {0.f, 0.f, 0.f}, m2[3] = {0.f, 0.f, 0.f};
-    if (plane) {
-      // pos = v2 - n (r2 + dist / 2), dist = n . v2 - n . p1 - r2 (plane fixed: the world)
-      const float np = dot3(nrm, pb);
-      for (int k = 0; k < 3; k++) v2b[k] = pb[k] - 0.5f * nrm[k] * np + nrm[k] * distb;
-      if (t2 == 3 && proj >= 0.5f) {  // frame along the axis projected on the plane
-        float bbv[3], t[3];
-        cross(frb + 6, nrm, t);
-        for (int k = 0; k < 3; k++) bbv[k] = frb[3 + k] + t[k];
-        const float* bvec = fr + 3;
-        const float bd = dot3(bvec, bbv);
-        float pjb[3];
-        for (int k = 0; k < 3; k++) pjb[k] = (bbv[k] - bvec[k] * bd) / proj;
-        const float npj = dot3(nrm, pjb);
-        float axb[3];
-        for (int k = 0; k < 3; k++) axb[k] = pjb[k] - nrm[k] * npj;
-        cross(ax, axb, m2);  // a body direction: moment ax x axbar
+#pragma unroll 1
+    for (int e = 0; e < NEVAL; e++) {
+      // lambda's terms: u(lambda) from dV; the rows' Bbar = -D J_t lambda (the cotangent of J_t a; b Bbar of J_t v),
+      // the cotangents of D and of k imp dist
+      {
+        float dVl[6], t[3];
+        dvl(e, b1, b2, dVl);
+        cross(dVl, pos, t);
+        for (int k = 0; k < 3; k++) { u[0][k] = dVl[3 + k] + t[k]; dW[0][k] = dVl[k]; }
+        for (int dd = 0; dd < 3; dd++) jd[0][dd] = dot3(fr + 3 * dd, u[0]);
       }
-    } else {
-      // pos = v1 + n (r1 + dist / 2), dist = |v2 - v1| - r1 - r2, n = (v2 - v1) / |v2 - v1|, frame = make_frame(n)
-      float nb[3];
-      const float hp = r1 + 0.5f * dist;
-      for (int k = 0; k < 3; k++) nb[k] = hp * pb[k];
-      const float distb2 = distb + 0.5f * dot3(nrm, pb);
-      make_frame_vjp(nrm, frb, nb);
-      float dirb[3];
-      const float dd = dist + r1 + r2;
-      // kappa(dd) of the normal derivative kappa (I - n n'): 0 exact 1/dd, 1 frozen frame, 2 1/max(dd, eps),
-      // 3 frozen below eps (strict <), eps = 1e-3 m
-      const int nopt = A.normal;
-      const float kap =
-          nopt == 1 ? 0.f : (nopt == 2 ? 1.f / fmaxf(dd, 1e-3f) : (nopt == 3 && dd < 1e-3f ? 0.f : 1.f / dd));
-      const float nnb = dot3(nrm, nb);
-      for (int k = 0; k < 3; k++) dirb[k] = nrm[k] * distb2 + kap * (nb[k] - nrm[k] * nnb);
-      for (int k = 0; k < 3; k++) { v1b[k] = pb[k] - dirb[k]; v2b[k] = dirb[k]; }
-    }
-    float t[3];
-    if (plane) {
-      cross(v2, v2b, t);
-      for (int k = 0; k < 3; k++) { out[18 + k] = t[k] + m2[k]; out[21 + k] = v2b[k]; }
-    } else {
-      // the core points back to the geoms: forces P1 at p1, P2 at p2 and moments m1, m2 of the axes' cotangents,
-      // through the free segment parameters
-      float P1[3], P2[3], m1[3] = {0.f, 0.f, 0.f};
-      if (t1 == 2 && t2 == 2) {
-        for (int k = 0; k < 3; k++) { P1[k] = v1b[k]; P2[k] = v2b[k]; }
-      } else if (t1 == 2) {  // sphere-capsule: v2 = sa + x2 sb, x2 = (sd . sb) / ma, sd = p1 - sa
-        const float hl = ld(g1_geom_size + 3 * g2 + 1);
-        const float xb = fr2 ? dot3(v2b, sb) : 0.f, sdb = dot3(sd, sb);
-        float sdbar[3], sbb[3], sab[3];
-        for (int k = 0; k < 3; k++) {
-          sdbar[k] = xb * sb[k] / ma;
-          sbb[k] = x2 * v2b[k] + xb * sd[k] / ma - 2.f * xb * sdb * sb[k] / (ma * ma);
-          sab[k] = v2b[k] - sdbar[k];
-          P1[k] = v1b[k] + sdbar[k];
-          P2[k] = sab[k];
+      float jdb[3][3] = {{jdb0[0], jdb0[1], jdb0[2]}, {0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
+      float Dbar = 0.f, kterm_bar = 0.f;
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        if (!((quad >> t) & 1u)) continue;
+        const float sg = (t & 1) ? -1.f : 1.f;
+        const int kd = 1 + (t >> 1);
+        const float w1 = dim == 3 ? sg * mu : 0.f;
+        const float Jl = jd[0][0] + w1 * jd[0][kd];
+        const float Bbar = -D * Jl;
+        Dbar -= Jl * Bt[t];
+        kterm_bar += Bbar;
+        jdb[1][0] += Bbar;
+        jdb[2][0] += bb * Bbar;
+        if (dim == 3) {
+          jdb[1][kd] += w1 * Bbar;
+          jdb[2][kd] += w1 * (bb * Bbar);
         }
-        float axb[3];
-        for (int k = 0; k < 3; k++) axb[k] = -hl * sab[k] + 2.f * hl * sbb[k];
-        cross(axu, axb, m2);
-      } else {  // capsule-capsule: v1 = p1 + sa x1, v2 = p2 + sb x2
-        const float xb1 = fr1 ? dot3(v1b, sa) : 0.f, xb2 = fr2 ? dot3(v2b, sb) : 0.f;
-        float ub = 0.f, vb = 0.f, mab = 0.f, mbb = 0.f, mcb = 0.f;
-        if (fr1 && fr2) {
-          const float det = ma * mc - mb * mb;
-          const float z1 = (mc * xb1 - mb * xb2) / det, z2 = (ma * xb2 - mb * xb1) / det;
-          ub = z1; vb = z2; mab = -z1 * x1; mbb = -(z1 * x2 + z2 * x1); mcb = -z2 * x2;
-        } else if (fr2) {  // x2 = (vv - mb x1) / mc
-          vb = xb2 / mc; mbb = -x1 * xb2 / mc; mcb = -x2 * xb2 / mc;
-        } else if (fr1) {  // x1 = (uu - mb x2) / ma
-          ub = xb1 / ma; mbb = -x2 * xb1 / ma; mab = -x1 * xb1 / ma;
-        }
-        float sab[3], sbb[3], sdb[3];
-        for (int k = 0; k < 3; k++) {
-          sab[k] = x1 * v1b[k] + 2.f * mab * sa[k] - mbb * sb[k] - ub * sd[k];
-          sbb[k] = x2 * v2b[k] - mbb * sa[k] + 2.f * mcb * sb[k] + vb * sd[k];
-          sdb[k] = -ub * sa[k] + vb * sb[k];
-          P1[k] = v1b[k] + sdb[k];
-          P2[k] = v2b[k] - sdb[k];
-        }
-        cross(sa, sab, m1);  // the half-axes are body directions scaled by their half lengths
-        cross(sb, sbb, m2);
       }
-      cross(p2, P2, t);
-      for (int k = 0; k < 3; k++) { out[18 + k] = t[k] + m2[k]; out[21 + k] = P2[k]; }
-      cross(p1, P1, t);
-      for (int k = 0; k < 3; k++) { out[24 + k] = t[k] + m1[k]; out[27 + k] = P1[k]; }
+      // back through jd = fr . u: ubar(x), frame cotangents, pos cotangent
+      float frb[9], pb[3] = {0.f, 0.f, 0.f};
+      for (int k = 0; k < 9; k++) frb[k] = 0.f;
+      for (int m = 0; m < 3; m++) {
+        float ub[3] = {0.f, 0.f, 0.f}, t[3];
+        for (int dd = 0; dd < 3; dd++)
+          for (int k = 0; k < 3; k++) { ub[k] += jdb[m][dd] * fr[3 * dd + k]; frb[3 * dd + k] += jdb[m][dd] * u[m][k]; }
+        // u = dV_lin + dW x pos: the wrench (pos x ubar, ubar); pos gets ubar x dW
+        cross(ub, dW[m], t);
+        for (int k = 0; k < 3; k++) pb[k] += t[k];
+        if (m > 0) {
+          cross(pos, ub, t);
+          for (int k = 0; k < 3; k++) { out[6 * m + k] = t[k]; out[6 * m + 3 + k] = ub[k]; }
+        }
+      }
+      for (int k = 18; k < 30; k++) out[k] = 0.f;
+      // dist: through imp (D, k imp dist)
+      const float distb = kterm_bar * kk * (imp + dimp * dist) + Dbar * dD * dimp;
+      // geometry VJP -> pose forces at v1 (body 1) and v2 (body 2) and moments
+      float v1b[3] = {0.f, 0.f, 0.f}, v2b[3] = {0.f, 0.f, 0.f}, m2[3] = {0.f, 0.f, 0.f};
+      if (plane) {
+        // pos = v2 - n (r2 + dist / 2), dist = n . v2 - n . p1 - r2 (plane fixed: the world)
+        const float np = dot3(nrm, pb);
+        for (int k = 0; k < 3; k++) v2b[k] = pb[k] - 0.5f * nrm[k] * np + nrm[k] * distb;
+        if (t2 == 3 && proj >= 0.5f) {  // frame along the axis projected on the plane
+          float bbv[3], t[3];
+          cross(frb + 6, nrm, t);
+          for (int k = 0; k < 3; k++) bbv[k] = frb[3 + k] + t[k];
+          const float* bvec = fr + 3;
+          const float bd = dot3(bvec, bbv);
+          float pjb[3];
+          for (int k = 0; k < 3; k++) pjb[k] = (bbv[k] - bvec[k] * bd) / proj;
+          const float npj = dot3(nrm, pjb);
+          float axb[3];
+          for (int k = 0; k < 3; k++) axb[k] = pjb[k] - nrm[k] * npj;
+          cross(ax, axb, m2);  // a body direction: moment ax x axbar
+        }
+      } else {
+        // pos = v1 + n (r1 + dist / 2), dist = |v2 - v1| - r1 - r2, n = (v2 - v1) / |v2 - v1|, frame = make_frame(n)
+        float nb[3];
+        const float hp = r1 + 0.5f * dist;
+        for (int k = 0; k < 3; k++) nb[k] = hp * pb[k];
+        const float distb2 = distb + 0.5f * dot3(nrm, pb);
+        make_frame_vjp(nrm, frb, nb);
+        float dirb[3];
+        const float dd = dist + r1 + r2;
+        // kappa(dd) of the normal derivative kappa (I - n n'): 0 exact 1/dd, 1 frozen frame, 2 1/max(dd, eps),
+        // 3 frozen below eps (strict <), eps = 1e-3 m
+        const int nopt = normal;
+        const float kap =
+            nopt == 1 ? 0.f : (nopt == 2 ? 1.f / fmaxf(dd, 1e-3f) : (nopt == 3 && dd < 1e-3f ? 0.f : 1.f / dd));
+        const float nnb = dot3(nrm, nb);
+        for (int k = 0; k < 3; k++) dirb[k] = nrm[k] * distb2 + kap * (nb[k] - nrm[k] * nnb);
+        for (int k = 0; k < 3; k++) { v1b[k] = pb[k] - dirb[k]; v2b[k] = dirb[k]; }
+      }
+      float t[3];
+      if (plane) {
+        cross(v2, v2b, t);
+        for (int k = 0; k < 3; k++) { out[18 + k] = t[k] + m2[k]; out[21 + k] = v2b[k]; }
+      } else {
+        // the core points back to the geoms: forces P1 at p1, P2 at p2 and moments m1, m2 of the axes' cotangents,
+        // through the free segment parameters
+        float P1[3], P2[3], m1[3] = {0.f, 0.f, 0.f};
+        if (t1 == 2 && t2 == 2) {
+          for (int k = 0; k < 3; k++) { P1[k] = v1b[k]; P2[k] = v2b[k]; }
+        } else if (t1 == 2) {  // sphere-capsule: v2 = sa + x2 sb, x2 = (sd . sb) / ma, sd = p1 - sa
+          const float hl = ld(g1_geom_size + 3 * g2 + 1);
+          const float xb = fr2 ? dot3(v2b, sb) : 0.f, sdb = dot3(sd, sb);
+          float sdbar[3], sbb[3], sab[3];
+          for (int k = 0; k < 3; k++) {
+            sdbar[k] = xb * sb[k] / ma;
+            sbb[k] = x2 * v2b[k] + xb * sd[k] / ma - 2.f * xb * sdb * sb[k] / (ma * ma);
+            sab[k] = v2b[k] - sdbar[k];
+            P1[k] = v1b[k] + sdbar[k];
+            P2[k] = sab[k];
+          }
+          float axb[3];
+          for (int k = 0; k < 3; k++) axb[k] = -hl * sab[k] + 2.f * hl * sbb[k];
+          cross(axu, axb, m2);
+        } else {  // capsule-capsule: v1 = p1 + sa x1, v2 = p2 + sb x2
+          const float xb1 = fr1 ? dot3(v1b, sa) : 0.f, xb2 = fr2 ? dot3(v2b, sb) : 0.f;
+          float ub = 0.f, vb = 0.f, mab = 0.f, mbb = 0.f, mcb = 0.f;
+          if (fr1 && fr2) {
+            const float det = ma * mc - mb * mb;
+            const float z1 = (mc * xb1 - mb * xb2) / det, z2 = (ma * xb2 - mb * xb1) / det;
+            ub = z1; vb = z2; mab = -z1 * x1; mbb = -(z1 * x2 + z2 * x1); mcb = -z2 * x2;
+          } else if (fr2) {  // x2 = (vv - mb x1) / mc
+            vb = xb2 / mc; mbb = -x1 * xb2 / mc; mcb = -x2 * xb2 / mc;
+          } else if (fr1) {  // x1 = (uu - mb x2) / ma
+            ub = xb1 / ma; mbb = -x2 * xb1 / ma; mab = -x1 * xb1 / ma;
+          }
+          float sab[3], sbb[3], sdb[3];
+          for (int k = 0; k < 3; k++) {
+            sab[k] = x1 * v1b[k] + 2.f * mab * sa[k] - mbb * sb[k] - ub * sd[k];
+            sbb[k] = x2 * v2b[k] - mbb * sa[k] + 2.f * mcb * sb[k] + vb * sd[k];
+            sdb[k] = -ub * sa[k] + vb * sb[k];
+            P1[k] = v1b[k] + sdb[k];
+            P2[k] = v2b[k] - sdb[k];
+          }
+          cross(sa, sab, m1);  // the half-axes are body directions scaled by their half lengths
+          cross(sb, sbb, m2);
+        }
+        cross(p2, P2, t);
+        for (int k = 0; k < 3; k++) { out[18 + k] = t[k] + m2[k]; out[21 + k] = P2[k]; }
+        cross(p1, P1, t);
+        for (int k = 0; k < 3; k++) { out[24 + k] = t[k] + m1[k]; out[27 + k] = P1[k]; }
+      }
+      put(e, (const float*)out, bb);
     }
   }
-  for (int k = 0; k < 30; k++) cw[lane][k] = out[k];
-  if (c < ncon) {
+  return mismatch;
+}
+
+// Contacts (lane = contact): one batch of 32 contacts' terms for the cotangent of A (the motion of lambda in A.VL)
+// into cw, their bodies into A.cbody. Returns the replay mismatch flag of this lane.
+template <class SH, class RW>
+__device__ __noinline__ int adj_contacts(AWorld& s, const SH& W, RW& A, const float* rec, float (*cw)[30], int c0,
+                                        int lane) {
+  const int c = c0 + lane;
+  float out[30];
+  for (int k = 0; k < 30; k++) out[k] = 0.f;
+  int mismatch = 0;
+  if (c < s.ncon) {
+    mismatch = contact_terms<1>(
+        s, W, c, A.normal,
+        [&](int, int b1, int b2, float* dV) {
+          for (int k = 0; k < 6; k++) dV[k] = A.VL[b2][k] - A.VL[b1][k];
+        },
+        [&](int, const float* o, float) {
+          for (int k = 0; k < 30; k++) out[k] = o[k];
+        });
     const int pr = s.con_pair[c];
     A.cbody[lane] = ldi(g1_geom_body + ldi(g1_pair_g1 + pr)) | ldi(g1_geom_body + ldi(g1_pair_g2 + pr)) << 8;
   }
+  for (int k = 0; k < 30; k++) cw[lane][k] = out[k];
   __syncwarp();
   return mismatch;
 }
@@ -945,11 +987,9 @@ __device__ __forceinline__ void copy_factor_tb(float* dst, const float* src, int
 // factors' buffers it copies each factor into the state's own scratch just before its solve) and adj_row_rest. block_sync: every warp of the block calls adj_row together; a block barrier before the limit
 // rows and the sweep re-aligns the worlds after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
 // the solve scratch of a cotangent's state: k_adjoint's Adj holds its own (the factor is copied in just before each
-// solve); the Jacobian's rows (AdjRow) solve with their record's factors, held once per block
+// solve)
 __device__ __forceinline__ float* solve_scratch(Adj& A) { return A.L; }
 __device__ __forceinline__ float* solve_scratch_dinv(Adj& A) { return A.dinv; }
-__device__ __forceinline__ float* solve_scratch(AdjRow&) { return nullptr; }
-__device__ __forceinline__ float* solve_scratch_dinv(AdjRow&) { return nullptr; }
 
 template <class SH>
 __device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, float* LQ, float* dinvQ, float* LH,

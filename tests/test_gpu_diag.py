@@ -79,7 +79,7 @@ def test_launch_info():
     d = torch_ffi.launch_info(0)
     props = torch.cuda.get_device_properties(0)
     assert d["sms"] == props.multi_processor_count
-    assert d["forward_worlds_per_sm"] >= 10 and d["adjoint_worlds_per_sm"] >= 10 and d["jacobian_rows_per_sm"] >= 12
+    assert d["forward_worlds_per_sm"] >= 10 and d["adjoint_worlds_per_sm"] >= 10 and d["jacobian_rows_per_sm"] >= 2 * 70
     for k in ("forward_smem_bytes", "adjoint_smem_bytes", "jacobian_smem_bytes"):
         assert 0 < d[k] <= 227 * 1024
     out = (ctypes.c_longlong * 8)()

@@ -65,6 +65,43 @@ def test_jacobian_matches_oracle_fd_on_synthetic_states():
         assert np.median(e) <= BOUND[name], (name, e)
 
 
+# The Jacobian kernel carries the 70 tangent-basis cotangents of a world on the lanes of one block and backward one
+# cotangent on a warp: the same mathematics in another order of float32 operations (and the quaternion rows as
+# combinations of the rotation cotangents). Per (world, row): the relative difference over the 99 tangent columns.
+ROW_TOL = {"median": 2e-5, "p99": 2e-3, "max": 3e-2}
+
+
+def _backward_rows(torch_ffi, torch, tape, t, rows, **kw):
+    """(B, len(rows), 99) float64: backward's VJP of each row's unit cotangent in the Jacobian's tangent columns."""
+    B = t[0].shape[0]
+    xi = t[0][:, 3:7].double()
+    out = []
+    for r in rows:
+        cq, cv = torch.zeros(B, 36, device="cuda"), torch.zeros(B, 35, device="cuda")
+        if r < 36:
+            cq[:, r] = 1.0
+        else:
+            cv[:, r - 36] = 1.0
+        gq, gv, gu, _ = torch_ffi.backward(tape, t[4], t[5], cq, cv, **kw)
+        # the qpos block: qpos form -> tangent, 1/2 Im(xi* (x) g) / |xi|^2
+        g = gq.double()
+        w, x, y, z = xi.unbind(1)
+        a, b, c, e = g[:, 3:7].unbind(1)
+        rot = 0.5 * torch.stack([w * b - x * a - y * e + z * c, w * c + x * e - y * a - z * b,
+                                 w * e - x * c + y * b - z * a], 1) / (xi * xi).sum(1, keepdim=True)
+        out.append(torch.cat([g[:, :3], rot, g[:, 7:], gv.double(), gu.double()], 1))
+    return torch.stack(out, 1)
+
+
+def _assert_rows_close(J, ref):
+    num = (J.double() - ref).norm(dim=2)
+    rel = (num / ref.norm(dim=2).clamp_min(1e-9)).flatten().cpu().numpy()
+    stats = {"median": float(np.median(rel)), "p99": float(np.percentile(rel, 99)), "max": float(rel.max())}
+    print(stats)
+    for k, bound in ROW_TOL.items():
+        assert stats[k] <= bound, (k, stats)
+
+
 def test_jacobian_rows_equal_the_vjp_of_unit_cotangents(golden):
     torch = _cuda()
     from nablaengine_b200 import torch_ffi
@@ -72,25 +109,9 @@ def test_jacobian_rows_equal_the_vjp_of_unit_cotangents(golden):
     t = [torch.from_numpy(np.ascontiguousarray(d[k], np.float32)).cuda() for k in KEYS]
     tape = torch_ffi.forward(*t, tape=True)[4]
     J = torch_ffi.jacobian(tape, t[4], t[5], clamp_kv=0, normal=3)[0]
-    B = J.shape[0]
-    xi = t[0][:, 3:7].double()
-    for r in (0, 4, 12, 40, 70):
-        cq, cv = torch.zeros(B, 36, device="cuda"), torch.zeros(B, 35, device="cuda")
-        if r < 36:
-            cq[:, r] = 1.0
-        else:
-            cv[:, r - 36] = 1.0
-        gq, gv, gu, _ = torch_ffi.backward(tape, t[4], t[5], cq, cv)
-        assert torch.equal(J[:, r, 35:70], gv) and torch.equal(J[:, r, 70:], gu)
-        # the qpos block: qpos form -> tangent, 1/2 Im(xi* (x) g) / |xi|^2
-        g = gq.double()
-        w, x, y, z = xi.unbind(1)
-        a, b, c, e = g[:, 3:7].unbind(1)
-        rot = 0.5 * torch.stack([w * b - x * a - y * e + z * c, w * c + x * e - y * a - z * b,
-                                 w * e - x * c + y * b - z * a], 1) / (xi * xi).sum(1, keepdim=True)
-        tan = torch.cat([g[:, :3], rot, g[:, 7:]], 1)
-        err = (J[:, r, :35].double() - tan).norm(dim=1) / tan.norm(dim=1).clamp_min(1e-9)
-        assert float(err.max()) < 1e-5, (r, err)
+    rows = (0, 4, 12, 40, 70)
+    ref = _backward_rows(torch_ffi, torch, tape, t, rows, clamp_kv=0, normal=3)
+    _assert_rows_close(J[:, list(rows)], ref)
 
 
 def test_jacobian_argument_errors(golden):
@@ -107,10 +128,10 @@ def test_jacobian_argument_errors(golden):
     assert J.shape == (0, 71, 99)
 
 
-@pytest.mark.parametrize("substeps", [1, 3])
-def test_jacobian_rows_equal_backward_ragged_batch(substeps):
-    """A batch of 37 worlds (no multiple of anything in the launch) with an odd number of records: every row of the
-    Jacobian equals backward's VJP of its unit cotangent bit for bit in the qvel and ctrl columns."""
+@pytest.mark.parametrize("substeps,clamp_kv,normal", [(1, 1, 0), (3, 1, 0), (4, 2, 2), (4, 0, 1)])
+def test_jacobian_rows_equal_backward_ragged_batch(substeps, clamp_kv, normal):
+    """A batch of 37 worlds (no multiple of anything in the launch), odd numbers of records and the gradient modes:
+    every row of the Jacobian equals backward's VJP of its unit cotangent within ROW_TOL."""
     torch = _cuda()
     from nablaengine_b200 import synthetic, torch_ffi
     s = synthetic.config_states("vjp", B=37)
@@ -118,13 +139,9 @@ def test_jacobian_rows_equal_backward_ragged_batch(substeps):
     t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda()
          for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
     tape = torch_ffi.forward(*t, substeps=substeps, tape=True)[4]
-    J = torch_ffi.jacobian(tape, t[4], t[5], substeps=substeps)[0]
-    B = J.shape[0]
-    for r in range(71):
-        cq, cv = torch.zeros(B, 36, device="cuda"), torch.zeros(B, 35, device="cuda")
-        if r < 36:
-            cq[:, r] = 1.0
-        else:
-            cv[:, r - 36] = 1.0
-        gq, gv, gu, _ = torch_ffi.backward(tape, t[4], t[5], cq, cv, substeps=substeps, clamp_kv=1, normal=0)
-        assert torch.equal(J[:, r, 35:70], gv) and torch.equal(J[:, r, 70:], gu), r
+    mode = dict(substeps=substeps, clamp_kv=clamp_kv, normal=normal)
+    if clamp_kv == 2:
+        mode.update(ctrl=t[3], clamp_soft=0.2)
+    J = torch_ffi.jacobian(tape, t[4], t[5], **mode)[0]
+    ref = _backward_rows(torch_ffi, torch, tape, t, range(71), **mode)
+    _assert_rows_close(J, ref)

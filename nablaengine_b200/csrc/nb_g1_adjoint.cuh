@@ -1023,13 +1023,9 @@ __device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, f
   __syncwarp();
 }
 
+// the geom poses from the replayed body poses (lane = geom)
 template <class SH>
-__device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
-  // the replay: poses and both channels; the motions of a* and v
-  adj_replay_kin(s, W, lane);
-  adj_motion(s, W, s.qacc, W.VA, lane);
-  adj_motion(s, W, s.qvel, W.VV, lane);
-  // geom poses; the contacts' rows: the same numbering as the forward (limit rows first)
+__device__ __forceinline__ void adj_replay_geoms(const AWorld& s, SH& W, int lane) {
   for (int g = lane; g < NG; g += 32) {
     const int b = ldi(g1_geom_body + g);
     const float gp[3] = {ld(g1_geom_pos + 3 * g), ld(g1_geom_pos + 3 * g + 1), ld(g1_geom_pos + 3 * g + 2)};
@@ -1040,25 +1036,38 @@ __device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
     for (int k = 0; k < 3; k++) W.col.gx[g][k] = s.X[b][k] + t[k];
     qmul(s.Q[b], gq, W.col.gq[g]);
   }
-  {
-    const int ncon = s.ncon;
-    int r0 = W.nlim_tape;
-    for (int c0 = 0; c0 < ncon; c0 += 32) {
-      const int c = c0 + lane;
-      const int want = c < ncon ? (ldi(g1_pair_dim + s.con_pair[c]) == 3 ? 4 : 1) : 0;
-      int incl = want;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(FULL, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int first = r0 + incl - want;
-      if (c < ncon) {
-        s.con_row0[c] = (unsigned char)min(first, 255);
-        s.con_nrow[c] = (unsigned char)max(0, min(want, NEFC - first));
-      }
-      r0 += __shfl_sync(FULL, incl, 31);
+}
+
+// the contacts' rows: the same numbering as the forward (limit rows first; lane = contact)
+template <class SH>
+__device__ __forceinline__ void adj_replay_rows(AWorld& s, const SH& W, int lane) {
+  const int ncon = s.ncon;
+  int r0 = W.nlim_tape;
+  for (int c0 = 0; c0 < ncon; c0 += 32) {
+    const int c = c0 + lane;
+    const int want = c < ncon ? (ldi(g1_pair_dim + s.con_pair[c]) == 3 ? 4 : 1) : 0;
+    int incl = want;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(FULL, incl, o);
+      if (lane >= o) incl += t;
     }
+    const int first = r0 + incl - want;
+    if (c < ncon) {
+      s.con_row0[c] = (unsigned char)min(first, 255);
+      s.con_nrow[c] = (unsigned char)max(0, min(want, NEFC - first));
+    }
+    r0 += __shfl_sync(FULL, incl, 31);
   }
+}
+
+template <class SH>
+__device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
+  // the replay: poses and both channels; the motions of a* and v; the geom poses and the contacts' rows
+  adj_replay_kin(s, W, lane);
+  adj_motion(s, W, s.qacc, W.VA, lane);
+  adj_motion(s, W, s.qvel, W.VV, lane);
+  adj_replay_geoms(s, W, lane);
+  adj_replay_rows(s, W, lane);
   __syncwarp();
 }
 

@@ -212,27 +212,30 @@ __device__ __forceinline__ void jac_prep_lists(JRec& R, const AWorld& s, int lan
   }
 }
 
-// thread t < ncon: contact t's matrices, from its terms at the 6 unit dV
-__device__ __forceinline__ void jac_prep_contact(JRec& R, const AWorld& s, const AdjShared& W, int normal, int t) {
-  JCon& C = R.con[t];
-  const int mism = contact_terms<6>(
-      s, W, t, normal,
+// item i < 3 ncon: contact i / 3's matrix columns 2 (i % 3) and 2 (i % 3) + 1, from its terms at those unit dV (the
+// contact's cotangent-independent part is computed by each of its three items)
+__device__ __forceinline__ void jac_prep_contact(JRec& R, const AWorld& s, const AdjShared& W, int normal, int i) {
+  const int c = i / 3, e0 = 2 * (i - 3 * c);
+  JCon& C = R.con[c];
+  const int mism = contact_terms<2>(
+      s, W, c, normal,
       [&](int e, int b1, int b2, float* dV) {
-        for (int k = 0; k < 6; k++) dV[k] = k == e ? 1.f : 0.f;
-        if (e == 0) { C.b1 = b1; C.b2 = b2; }
+        for (int k = 0; k < 6; k++) dV[k] = k == e0 + e ? 1.f : 0.f;
+        if (e0 + e == 0) { C.b1 = b1; C.b2 = b2; }
       },
       [&](int e, const float* o, float bb) {
+        const int col = e0 + e;
         for (int k = 0; k < 6; k++) {
-          C.Ga[6 * k + e] = o[6 + k];
-          C.P2[6 * k + e] = o[18 + k];
-          C.P1[6 * k + e] = o[24 + k];
+          C.Ga[6 * k + col] = o[6 + k];
+          C.P2[6 * k + col] = o[18 + k];
+          C.P1[6 * k + col] = o[24 + k];
         }
-        if (e == 0) {
+        if (col == 0) {
           for (int k = 0; k < 6; k++) C.GL[k] = o[k];
           C.bb = bb;
         }
       });
-  if (mism) atomicOr(&R.flags, ADJ_REPLAY_MISMATCH);
+  if (mism && e0 == 0) atomicOr(&R.flags, ADJ_REPLAY_MISMATCH);
 }
 
 // thread b in 1..NB-1: body b's cotangent-independent terms (the own terms of both ID channels, as adj_sweep)
@@ -344,16 +347,30 @@ __device__ __forceinline__ void jac_prep_sums(JRec& R, int lane) {
 __device__ __forceinline__ void jac_prep(JBlock& B, const float* rec, const float* fric_w, const float* com_w,
                                          const float* ctrl_w, float clamp_soft, int clamp_kv, int normal, int t) {
   JRec& R = B.R;
+  AWorld& s = B.prep.s;
+  AdjShared& W = B.prep.W;
   const int warp = t >> 5, lane = t & 31;
   jac_prep_state(B, rec, fric_w, com_w, ctrl_w, t);
   __syncthreads();
-  if (warp == 0) adj_replay(B.prep.s, B.prep.W, lane);
-  else if (warp == 1) jac_prep_dofs(R, B.prep.s, B.prep.W, clamp_soft, clamp_kv, lane);
-  else jac_prep_lists(R, B.prep.s, lane);
+  if (warp == 0) adj_replay_kin(s, W, lane);
+  else if (warp == 1) jac_prep_dofs(R, s, W, clamp_soft, clamp_kv, lane);
+  else {
+    jac_prep_lists(R, s, lane);
+    adj_replay_rows(s, W, lane);
+  }
   __syncthreads();
-  if (t < R.ncon) jac_prep_contact(R, B.prep.s, B.prep.W, normal, t);
-  if (t >= 1 && t < NB) jac_prep_body(R, B.prep.s, B.prep.W, t);
-  if (t >= 32 && t < 32 + NV) jac_prep_dof_motion(R, B.prep.s, B.prep.W, t - 32);
+  if (warp == 0) {
+    adj_replay_geoms(s, W, lane);
+    jac_prep_dof_motion(R, s, W, lane);
+    if (lane < NV - 32) jac_prep_dof_motion(R, s, W, 32 + lane);
+  } else if (warp == 1) {
+    adj_motion(s, W, s.qacc, W.VA, lane);
+    if (lane >= 1 && lane < NB) jac_prep_body(R, s, W, lane);
+  } else {
+    adj_motion(s, W, s.qvel, W.VV, lane);
+  }
+  __syncthreads();
+  for (int i = t; i < 3 * R.ncon; i += JTHREADS) jac_prep_contact(R, s, W, normal, i);
   __syncthreads();
   if (warp == 0) jac_prep_sums(R, lane);
   __syncthreads();

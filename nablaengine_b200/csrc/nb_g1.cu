@@ -140,20 +140,21 @@ __global__ void __launch_bounds__(ORD_THREADS) k_order(int nw, const float* __re
 }
 
 // ---- the adjoint ------------------------------------------------------------------------------------------------
-// Worlds per block of k_adjoint: up to AWPB (13 x 16.6 KB, one block per SM). The worlds meet at a block barrier
+// Worlds per block of k_adjoint: up to AWPB (14 x 16.2 KB, one block per SM). The worlds meet at a block barrier
 // before every substep, so the SM's warps run the same code together (one instruction stream; measured at B = 4096:
 // 1.06 ms against 1.14 ms with one world per block and no barrier). The launch spreads the worlds evenly over whole
 // waves: as many waves as AWPB per SM needs, and per block the fewest worlds that fill them (a block's time grows
-// with its worlds: at B = 4096, 3 waves of 10 worlds ran in 0.588 ms, 2.1 waves of 13 in 0.681 ms, configuration 3).
-// Two instances: blocks of up to AWPB_SMALL worlds run the one compiled for that many (more registers per thread:
-// 0.588 against 0.605 ms for the same 10-world blocks in the AWPB instance), larger blocks the AWPB one.
+// with its worlds, but less than in proportion: at B = 4096 on configuration 3, 3 waves of 10 worlds ran in 0.588
+// ms, 2.1 waves of 13 in 0.681 ms, 2 waves of 14 in 0.479 ms). Two instances: blocks of up to AWPB_SMALL worlds run
+// the one compiled for that many (more registers per thread: 0.588 against 0.605 ms for the same 10-world blocks in
+// the 13-world instance), larger blocks the AWPB one.
 #ifndef NB_AWPB
-#define NB_AWPB 13
+#define NB_AWPB 14
 #endif
 constexpr int AWPB = NB_AWPB, AWPB_SMALL = 10;
 struct AdjBlock { AWorld s; Adj a; };
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
-static_assert(ASMEM <= 227 * 1024, "one adjoint block per SM");
+static_assert(ASMEM <= 227 * 1024 && ASMEM + 1024 <= 228 * 1024, "one adjoint block of AWPB worlds per SM");
 
 // The starting cotangent of one adjoint over nsub records tw (the world's first record): the output cotangent is
 // (gq, gv) (qpos form, in any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel')

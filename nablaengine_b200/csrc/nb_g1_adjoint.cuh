@@ -42,23 +42,26 @@ struct __align__(16) AWorld {
 };
 struct GeomPoses { float gx[NG][3], gq[NG][4]; };
 
-// The adjoint's per-world state (k_adjoint: one cotangent per world). Its scratch overlaps by phase: the factor being
-// solved with (the solves, first), the replayed geom poses and the motions of a* and v with the contact batch (the
+// The adjoint's per-world state (k_adjoint: one cotangent per world; with AWorld 16.2 KB, 14 per SM). Its scratch
+// overlaps by phase: the factor being solved with and its inverse diagonal (the solves, first), the replayed geom poses and the motions of a* and v with the contact batch (the
 // replay and the contacts), and the sweep's subtree sums and parent cotangents (last); each phase writes its part
 // after the previous owner of that space is done with it.
 struct __align__(16) Adj {
-  float lam[NV], y[NV], xa[NV], aadv[NV], vb[NV], qb[NV], ub[NU], qout[NV], tmp2[NV], u[NU];
-  float ql[NV];                       // direct tangent cotangents (integrator, limits, actuators)
+  float lam[NV], y[NV], xa[NV], aadv[NV], vb[NV], qb[NV], ub[NU], u[NU];
+  float qout[NV];                     // the tangent cotangent: the output's, then (from the integrator on) the input's
+                                      // direct terms (integrator, limits, actuators), the sweep's added at the end
   float om[NB][3], alA[NB][3], aoA[NB][3], alB[NB][3], aoB[NB][3];  // replayed velocities / accelerations
   float VL[NB][6], VY[NB][6];         // body motions at the origin of lambda and y
   float dep[NB][24];                  // per body: G_lambda, G_a, G_v (wrenches at the origin), pose wrench
   float ax[NV][3];                    // dof axes (world)
-  float dinv[NV + 1];                 // the factor's inverse diagonal (L_Q's, then L_H's)
   unsigned clamp_lo, clamp_hi;
   unsigned zone[NEFC / 32];           // the record's zone bits (row r quadratic: bit r & 31 of word r / 32)
   int nlim_tape, flags, normal, pad_;  // normal: the self-contact normal derivative option (0..3)
   union {
-    float L[NTRIP];                   // the solves: L_Q (tree-block order), then L_H
+    struct {                          // the solves: L_Q (tree-block order), then L_H, with its inverse diagonal
+      float L[NTRIP];
+      float dinv[NV + 1];
+    };
     struct {                          // the replay and the contacts
       float cw[32][30];               // a batch of 32 contacts' wrenches
       int cbody[32];                  // their bodies: b1 | b2 << 8
@@ -665,7 +668,7 @@ __device__ __noinline__ int adj_limits(AWorld& s, const SH& W, RW& A, const floa
         const float Bt = sg * a + bb * sg * v + kk * imp * pos;
         A.vb[i] += -D * bb * lam;
         const float dpos = -sg * lam * (dD * dimp * Bt + D * kk * (imp + dimp * pos));
-        A.ql[i] += sg * dpos;
+        A.qout[i] += sg * dpos;
       }
     }
     nlim += __popc(bal);
@@ -1075,24 +1078,18 @@ template <class SH, class RW>
 __device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, const float* rec, const float* LQ,
                                               const float* dinvQ, const float* LH, const float* dinvH, int lane) {
   const float h = G1_TIMESTEP;
-  for (int i = lane; i < NV; i += 32) A.ql[i] = 0.f;
-  __syncwarp();
   PROF_START(A);
-  // A1: the integrator. v' = v + h a_adv; root rotation: q' = q exp(h w' / 2)
+  // A1: the integrator. v' = v + h a_adv; root rotation: q' = q exp(h w' / 2). The input tangent gets qbar' (kept in
+  // qout), its rotation R(h w') qbar'_rot
   {
     for (int i = lane; i < NV; i += 32) {
-      const float vnew = s.qvel[i] + h * W.aadv[i];
-      A.tmp2[i] = vnew;
-    }
-    __syncwarp();
-    for (int i = lane; i < NV; i += 32) {
       float vt = A.vb[i];
-      if (i < 3 || i >= 6) { vt += h * A.qout[i]; A.ql[i] += A.qout[i]; }
+      if (i < 3 || i >= 6) vt += h * A.qout[i];
       A.y[i] = vt;  // (vbar'_tot; the rotation's part is added by lane 0 below)
     }
     __syncwarp();
     if (lane == 0) {
-      const float w[3] = {A.tmp2[3], A.tmp2[4], A.tmp2[5]};
+      const float w[3] = {s.qvel[3] + h * W.aadv[3], s.qvel[4] + h * W.aadv[4], s.qvel[5] + h * W.aadv[5]};
       const float tb[3] = {A.qout[3], A.qout[4], A.qout[5]};
       const float ph[3] = {h * w[0], h * w[1], h * w[2]};
       const float th = sqrtf(dot3(ph, ph));
@@ -1109,7 +1106,7 @@ __device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, con
       float sn = 0.f, omc = 0.f;
       if (th < 1e-3f) { sn = 1.f - th * th / 6.f; omc = 0.5f - th * th / 24.f; }
       else { float s_, c_; sincosf(th, &s_, &c_); sn = s_ / th; omc = (1.f - c_) / (th * th); }
-      for (int k = 0; k < 3; k++) A.ql[3 + k] += tb[k] + sn * pt[k] + omc * ppt[k];
+      for (int k = 0; k < 3; k++) A.qout[3 + k] = tb[k] + sn * pt[k] + omc * ppt[k];
     }
     __syncwarp();
     for (int i = lane; i < NV; i += 32) {
@@ -1176,7 +1173,7 @@ __device__ __forceinline__ int adj_row_rest(AWorld& s, const SH& W, RW& A, const
       const float o = fmaxf(0.f, (fabsf(f) - lim) / lim);
       wq = wv = __expf(-o / clamp_soft);
     }
-    A.ql[i] += -kp * lam * wq;
+    A.qout[i] += -kp * lam * wq;
     A.vb[i] += -kv * lam * wv;
     A.ub[i - 6] += kp * lam * wq;
   }
@@ -1188,7 +1185,7 @@ __device__ __forceinline__ int adj_row_rest(AWorld& s, const SH& W, RW& A, const
   adj_sweep(s, W, A, lane);
   PROF(A, 6);
   // A8: the input state's tangent cotangent
-  for (int i = lane; i < NV; i += 32) A.qout[i] = A.qb[i] + A.ql[i];
+  for (int i = lane; i < NV; i += 32) A.qout[i] = A.qb[i] + A.qout[i];
   __syncwarp();
   return flags;
 }

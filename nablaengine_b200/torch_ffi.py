@@ -575,8 +575,9 @@ def last_forward(nworld=None, device=None):
 
 
 def launch_info(device=None):
-    """The kernels' launch shapes on the device (nb_g1_launch): shared memory per block and resident worlds (or
-    Jacobian rows) per SM of the forward, the adjoint and the Jacobian, and the SM count."""
+    """The kernels' launch shapes on the device (nb_g1_launch): shared memory per block and resident worlds per SM
+    of the forward and the adjoint, the Jacobian's shared memory per block and resident cotangents (Jacobian rows in
+    flight, 70 per world) per SM, and the SM count."""
     index = _device_index(device)
     _device(index)
     out = (ctypes.c_longlong * 8)()

@@ -145,3 +145,23 @@ def test_jacobian_rows_equal_backward_ragged_batch(substeps, clamp_kv, normal):
     J = torch_ffi.jacobian(tape, t[4], t[5], **mode)[0]
     ref = _backward_rows(torch_ffi, torch, tape, t, range(71), **mode)
     _assert_rows_close(J, ref)
+
+
+def test_jacobian_many_contacts_and_long_steps():
+    """Worlds lowered into the floor (records of more than 32 contacts: the preparation's contact items take two
+    rounds of the block's threads) and a step of 9 substeps: every row equals backward's VJP within ROW_TOL."""
+    torch = _cuda()
+    from nablaengine_b200 import synthetic, torch_ffi
+    s = synthetic.config_states("vjp", B=24, seed_offset=7)
+    s["qpos"][:, 2] -= np.linspace(0.0, 0.45, 24, dtype=np.float32)
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda()
+         for k in ("qpos", "qvel", "warm", "ctrl", "friction", "com")]
+    out = torch_ffi.forward(*t, substeps=9, tape=True)
+    info, tape = out[3], out[4]
+    ncon = info[:, 1].cpu().numpy()
+    print("contacts of the last substep: max", int(ncon.max()), "worlds above 32:", int((ncon > 32).sum()))
+    assert (ncon > 32).sum() >= 3
+    J, jinfo = torch_ffi.jacobian(tape, t[4], t[5], substeps=9)
+    assert torch.isfinite(J).all()
+    ref = _backward_rows(torch_ffi, torch, tape, t, range(71), substeps=9, clamp_kv=1, normal=0)
+    _assert_rows_close(J, ref)

@@ -44,8 +44,9 @@ int nb_g1_upload(const float* consts, cudaStream_t stream);
  * rows of the last substep (<= 192), bits 1 unsupported geom pair / 4 contacts beyond 64 dropped / 16 rows beyond
  * 192 dropped, ORed over the substeps]. ocon (B,64,8) may be NULL: the last substep's contacts as (pair, dist,
  * pos[3], normal[3]), pair -1 past the count. tape (B, nsub, tape words) may be NULL: else the per-substep records
- * nb_g1_adjoint reads (the substep's input state, a*, a_adv, the Cholesky factors of the Newton Hessian and of
- * M + h kv, the contact table, the constraint zones, the actuator clamp masks, flags); the outputs are bitwise the
+ * nb_g1_adjoint reads (the substep's input state, a*, a_adv, the Cholesky factor of the Newton Hessian, the contact
+ * table, the constraint zones, the actuator clamp masks, flags, then the factor of M + h kv; nb_g1_forward_ex below
+ * writes the compact record without the last); the outputs are bitwise the
  * same with and without it. work: nb_g1_work_bytes(nw) bytes, overwritten, or NULL: with it the worlds are first
  * sorted by root height (lowest first, a small kernel before the step) so that worlds of similar cost share a
  * block; without it they run in index order, slower; the outputs are bitwise the same either way. nw == 0 is a
@@ -151,6 +152,29 @@ int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const fl
 int nb_g1_forward_noalloc(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
                           const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
                           float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape);
+
+/* The compact tape. nb_g1_tape_words(0) = the full record (the tape words of nb_g1_sizes, 1224), (1) = the compact
+ * record (848: the full record's first words, without the factor of M + h kv and its inverse diagonal, which the
+ * adjoint and the Jacobian then rebuild from the replayed poses: 31 % less tape, the reader's work grows by the
+ * rebuild). The _ex entries are nb_g1_forward / _adjoint / _jacobian / _diag_forward with the tape's record size
+ * (one of those two values) as a last argument; the plain entries take full records. Anything else returns
+ * cudaErrorInvalidValue. Outputs of the forward are bitwise the same for either record; the adjoint and the
+ * Jacobian from compact records equal those from full ones within float32 rounding. No counterpart in the
+ * reference's ABI (its tape is one fixed record, src/nablaengine/g1_engine/tape.py:27-43). */
+long long nb_g1_tape_words(int compact);
+int nb_g1_forward_ex(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                     const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                     float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape,
+                     void* work, int tape_words);
+int nb_g1_adjoint_ex(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction,
+                     const float* com, const float* gq_out, const float* gv_out, float* gq_in, float* gv_in,
+                     float* gctrl, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal,
+                     int tape_words);
+int nb_g1_jacobian_ex(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction,
+                      const float* com, float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv,
+                      int normal, int tape_words);
+int nb_g1_diag_forward_ex(cudaStream_t stream, unsigned long long* counters, int nw, int nsub, int iterations,
+                          const int* info, const float* tape, int tape_words);
 
 #ifdef __cplusplus
 }

@@ -13,8 +13,9 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "nabla_g1.h"
 EXPORTS = ("nb_g1_sizes", "nb_g1_work_bytes", "nb_g1_upload", "nb_g1_forward", "nb_g1_forward_stats",
            "nb_g1_adjoint", "nb_g1_jacobian", "nb_g1_kinematics", "nb_g1_kinematics_vjp", "nb_g1_diag_count",
            "nb_g1_diag_forward", "nb_g1_diag_backward", "nb_g1_forward_noalloc", "nb_g1_last_forward",
-           "nb_g1_launch")
-ABI_VERSION = 3
+           "nb_g1_launch", "nb_g1_tape_words", "nb_g1_forward_ex", "nb_g1_adjoint_ex", "nb_g1_jacobian_ex",
+           "nb_g1_diag_forward_ex")
+ABI_VERSION = 4
 NQ, NV, NU, NBODY, MAXCON, NEFC = 36, 35, 29, 31, 64, 192
 
 _LOCK = threading.Lock()
@@ -63,6 +64,15 @@ def load(path=None, build_if_missing=True):
         lib.nb_g1_diag_backward.argtypes, lib.nb_g1_diag_backward.restype = [vp, vp, i32] + [vp] * 6, i32
         lib.nb_g1_last_forward.argtypes, lib.nb_g1_last_forward.restype = [vp, i32, vp, vp, vp], i32
         lib.nb_g1_launch.argtypes, lib.nb_g1_launch.restype = [i32, vp], i32
+        lib.nb_g1_tape_words.argtypes, lib.nb_g1_tape_words.restype = [i32], i64
+        lib.nb_g1_forward_ex.argtypes = lib.nb_g1_forward.argtypes + [i32]
+        lib.nb_g1_forward_ex.restype = i32
+        lib.nb_g1_adjoint_ex.argtypes = lib.nb_g1_adjoint.argtypes + [i32]
+        lib.nb_g1_adjoint_ex.restype = i32
+        lib.nb_g1_jacobian_ex.argtypes = lib.nb_g1_jacobian.argtypes + [i32]
+        lib.nb_g1_jacobian_ex.restype = i32
+        lib.nb_g1_diag_forward_ex.argtypes = lib.nb_g1_diag_forward.argtypes + [i32]
+        lib.nb_g1_diag_forward_ex.restype = i32
         sizes = (ctypes.c_longlong * 8)()
         lib.nb_g1_sizes(sizes)
         want = (NQ, NV, NU, NBODY, MAXCON, NEFC)
@@ -76,3 +86,8 @@ def sizes():
     out = (ctypes.c_longlong * 8)()
     load().nb_g1_sizes(out)
     return list(out)
+
+
+def tape_words(compact=False):
+    """Words per world and substep of a tape record: full, or compact (no L_Q: rebuilt by the tape's readers)."""
+    return int(load().nb_g1_tape_words(1 if compact else 0))

@@ -29,7 +29,8 @@ constexpr int WPB = NB_WPB;  // worlds (warps) per block
 // transitions in step, each world's Newton iterations on their own): 3.81 ms against 3.84 at the same code, and
 // it needs the Newton loop to fit the instruction cache (~40 KB measured for 10 warps on separate paths).
 constexpr int TAPE_WORDS = REC_WORDS;
-constexpr long long ABI_VERSION = 3;  // 2: the tape's L_Q in tree-block order; 3: only its pattern's entries
+constexpr long long ABI_VERSION = 4;  // 2: the tape's L_Q in tree-block order; 3: only its pattern's entries; 4: L_Q
+                                      // at the record's end (the compact record: the first REC_COMPACT words)
 
 __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __restrict__ qpos,
                                                       const float* __restrict__ qvel, const float* __restrict__ warm,
@@ -38,7 +39,8 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
                                                       float* __restrict__ oq, float* __restrict__ ov,
                                                       float* __restrict__ ow, int* __restrict__ info,
                                                       float* __restrict__ ocon, int* __restrict__ stats,
-                                                      float* __restrict__ tape, const int* __restrict__ order) {
+                                                      float* __restrict__ tape, const int* __restrict__ order,
+                                                      int tape_words) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = blockIdx.x * WPB + warp;  // the warp's place in the world order (k_order), or its world index
@@ -56,7 +58,7 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
   if (lane == 0) { s.fric = fric[w64]; s.unsup = 0; s.nit = 0; }  // (w64: world 0 for an inactive warp)
   __syncwarp();
   for (int k = 0; k < nsub; k++) {
-    float* rec = tape && active ? tape + (w64 * nsub + k) * REC_WORDS : nullptr;
+    float* rec = tape && active ? tape + (w64 * nsub + k) * tape_words : nullptr;
     if (active) substep_pre(s, lane, rec);
 #if NB_LOCKSTEP < 0
     // each world iterates on its own; the block meets once, after every world's last iteration
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
 #else
     while (!uall(!active || s.ndone || s.nit_cur >= iterations)) newton_iter(s, lane);
 #endif
-    if (active) substep_post(s, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr, rec);
+    if (active) substep_post(s, lane, stats ? stats + (w64 * nsub + k) * 8 : nullptr, rec, tape_words == REC_WORDS);
   }
   if (!active) return;
   for (int i = lane; i < NQ; i += 32) oq[w64 * NQ + i] = s.qpos[i];
@@ -153,6 +155,7 @@ __global__ void __launch_bounds__(ORD_THREADS) k_order(int nw, const float* __re
 #endif
 constexpr int AWPB = NB_AWPB, AWPB_SMALL = 10;
 struct AdjBlock { AWorld s; Adj a; };
+static_assert(offsetof(AdjBlock, a) % 16 == 0 && sizeof(AdjBlock) % 16 == 0, "each world's Adj 16-byte aligned");
 constexpr size_t ASMEM = sizeof(AdjBlock) * AWPB;
 static_assert(ASMEM <= 227 * 1024 && ASMEM + 1024 <= 228 * 1024, "one adjoint block of AWPB worlds per SM");
 
@@ -160,8 +163,8 @@ static_assert(ASMEM <= 227 * 1024 && ASMEM + 1024 <= 228 * 1024, "one adjoint bl
 // (gq, gv) (qpos form, in any memory), or the unit vector of output row `unit` (0..70: qpos' in qpos form, then qvel')
 // when unit >= 0; into A.qout (dof tangent), A.vb, with A.ub cleared
 template <class RW>
-__device__ __noinline__ void adj_row_init(RW& A, const float* tw, int nsub, const float* gq, const float* gv, int unit,
-                                          int normal, int lane) {
+__device__ __noinline__ void adj_row_init(RW& A, const float* tw, int nsub, int rec_words, const float* gq,
+                                          const float* gv, int unit, int normal, int lane) {
   const float h = G1_TIMESTEP;
   if (lane == 0) A.normal = normal;
   auto cq = [&](int i) { return unit >= 0 ? (i == unit ? 1.f : 0.f) : gq[i]; };
@@ -170,7 +173,7 @@ __device__ __noinline__ void adj_row_init(RW& A, const float* tw, int nsub, cons
   for (int i = lane; i < NV; i += 32) A.vb[i] = cv(i);
   // the output cotangent in the dof tangent: the quaternion part at the output quaternion q' (re-integrated from the
   // last record): 1/2 Im(q'* gq) / |q'|^2
-  const float* last = tw + (size_t)(nsub - 1) * REC_WORDS;
+  const float* last = tw + (size_t)(nsub - 1) * rec_words;
   for (int i = lane; i < NV; i += 32)
     if (i < 3 || i >= 6) A.qout[i] = cq(i < 3 ? i : i + 1);
   if (lane == 0) {
@@ -199,17 +202,19 @@ __device__ __noinline__ void adj_row_init(RW& A, const float* tw, int nsub, cons
 
 // One world's adjoint (one warp): leaves the input cotangents in A.qout (dof tangent), A.vb, A.ub; returns the replay
 // flags. block_sync: a block barrier before every substep (every warp of the block calls this with the same nsub).
-__device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int nsub, float fric, const float* comw,
+__device__ __noinline__ int adj_world(AWorld& s, Adj& A, const float* tw, int nsub, int rec_words, float fric,
+                                      const float* comw,
                                       const float* ctrlw, const float* gq, const float* gv, int clamp_kv,
                                       float clamp_soft, int normal, int lane, bool block_sync) {
   if (lane == 0) s.fric = fric;
   if (lane < 3) s.com[lane] = comw[lane];
   for (int i = lane; i < NU; i += 32) A.u[i] = ctrlw ? ctrlw[i] : 0.f;
-  adj_row_init(A, tw, nsub, gq, gv, -1, normal, lane);
+  adj_row_init(A, tw, nsub, rec_words, gq, gv, -1, normal, lane);
   int flags = 0;
   for (int k = nsub - 1; k >= 0; k--) {
     if (block_sync) __syncthreads();  // (the same value on every thread of the block)
-    flags |= adj_substep(s, A, tw + (size_t)k * REC_WORDS, clamp_kv, clamp_soft, A.cw, lane, block_sync);
+    flags |= adj_substep(s, A, tw + (size_t)k * rec_words, rec_words == REC_WORDS, clamp_kv, clamp_soft, A.cw, lane,
+                         block_sync);
   }
   return flags;
 }
@@ -223,7 +228,7 @@ __global__ void __launch_bounds__(MAXW * 32) k_adjoint(int nw, int nsub, const f
                                                        const float* __restrict__ gv_out, float* __restrict__ gq_in,
                                                        float* __restrict__ gv_in, float* __restrict__ gctrl,
                                                        int* __restrict__ info, const float* __restrict__ ctrl,
-                                                       float clamp_soft, int clamp_kv, int normal) {
+                                                       float clamp_soft, int clamp_kv, int normal, int tape_words) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int w = blockIdx.x * (int)(blockDim.x >> 5) + warp;  // (blockDim.x / 32 <= AWPB worlds per block)
@@ -233,8 +238,8 @@ __global__ void __launch_bounds__(MAXW * 32) k_adjoint(int nw, int nsub, const f
   AWorld& s = blk.s;
   Adj& A = blk.a;
   const size_t w64 = (size_t)w;
-  const float* tw = tape + w64 * nsub * REC_WORDS;
-  const int flags = adj_world(s, A, tw, nsub, fric[w], com + w64 * 3, ctrl ? ctrl + w64 * NU : nullptr,
+  const float* tw = tape + w64 * nsub * tape_words;
+  const int flags = adj_world(s, A, tw, nsub, tape_words, fric[w], com + w64 * 3, ctrl ? ctrl + w64 * NU : nullptr,
                               gq_out + w64 * NQ, gv_out + w64 * NV, clamp_kv, clamp_soft, normal, lane, true);
   if (!active) return;
   // the input qpos gradient in qpos form: (q_lin, 2 xi (0, q_rot), q_hinge), xi the input quaternion
@@ -265,13 +270,13 @@ __global__ void __launch_bounds__(JTHREADS, 2) k_jacobian(int nw, int nsub, cons
                                                           const float* __restrict__ fric,
                                                           const float* __restrict__ com, float* __restrict__ jac,
                                                           int* __restrict__ info, const float* __restrict__ ctrl,
-                                                          float clamp_soft, int clamp_kv, int normal) {
+                                                          float clamp_soft, int clamp_kv, int normal, int tape_words) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float qcoef[12];  // the quaternion rows: row 3 + c = sum_k qcoef[3 c + k] (rotation cotangent k)
   JBlock& B = *reinterpret_cast<JBlock*>(smem);
   const int t = threadIdx.x, w = blockIdx.x;
   const size_t w64 = (size_t)w;
-  const float* tw = tape + w64 * nsub * REC_WORDS;
+  const float* tw = tape + w64 * nsub * tape_words;
   const int j = t < JNR ? t : JNR + (t & 1);  // the lane's right-hand side (spare lanes: the spare columns)
   float* x = B.rhs + j;
   for (int e = t; e < NTRIP; e += JTHREADS) B.R.LQ[e] = 0.f;  // L_Q's entries off its pattern
@@ -282,7 +287,7 @@ __global__ void __launch_bounds__(JTHREADS, 2) k_jacobian(int nw, int nsub, cons
   }
   for (int i = 0; i < NU; i++) JX(JO_U, i) = 0.f;
   if (t == 0) {  // the output cotangent of a qpos' quaternion entry in the rotation tangent: 1/2 Im(q'* e_c) / |q'|^2
-    const float* last = tw + (size_t)(nsub - 1) * REC_WORDS;
+    const float* last = tw + (size_t)(nsub - 1) * tape_words;
     const float h = G1_TIMESTEP;
     float q[4] = {last[T_QPOS + 3], last[T_QPOS + 4], last[T_QPOS + 5], last[T_QPOS + 6]};
     const float wv[3] = {last[T_QVEL + 3] + h * last[T_AADV + 3], last[T_QVEL + 4] + h * last[T_AADV + 4],
@@ -308,8 +313,8 @@ __global__ void __launch_bounds__(JTHREADS, 2) k_jacobian(int nw, int nsub, cons
   }
   for (int k = nsub - 1; k >= 0; k--) {
     __syncthreads();  // (the previous record's cotangents are done with the shared terms and lambda / y)
-    jac_prep(B, tw + (size_t)k * REC_WORDS, fric + w, com + 3 * w64, ctrl ? ctrl + w64 * NU : nullptr, clamp_soft,
-             clamp_kv, normal, t);
+    jac_prep(B, tw + (size_t)k * tape_words, tape_words == REC_WORDS, fric + w, com + 3 * w64,
+             ctrl ? ctrl + w64 * NU : nullptr, clamp_soft, clamp_kv, normal, t);
     jac_rhs_solves(B.R, x);
     jac_rhs_sweep(B.R, x);
   }
@@ -347,7 +352,7 @@ __device__ __forceinline__ bool finite_row(const float* x, int n) {
 }
 
 __global__ void k_diag_fwd(unsigned long long* d, int nw, int nsub, int iterations, const int* info,
-                           const float* tape) {
+                           const float* tape, int tape_words) {
   unsigned unsup = 0, lim = 0, oc = 0, orow = 0, refact = 0, nonconv = 0, sing = 0;
   const int stride = gridDim.x * blockDim.x;
   for (int w0 = blockIdx.x * blockDim.x; w0 < nw; w0 += stride) {  // whole warps stay in the loop
@@ -360,7 +365,7 @@ __global__ void k_diag_fwd(unsigned long long* d, int nw, int nsub, int iteratio
       lim += info[4 * w] >= iterations;
       if (tape)
         for (int k = 0; k < nsub; k++) {
-          const unsigned f = __float_as_uint(tape[((size_t)w * nsub + k) * REC_WORDS + T_FLAGS]);
+          const unsigned f = __float_as_uint(tape[((size_t)w * nsub + k) * tape_words + T_FLAGS]);
           refact += (f & TAPE_REFACT) != 0;
           nonconv += (f & TAPE_NONCONV) != 0;
           sing += (f & TAPE_SINGULAR) != 0;
@@ -459,6 +464,9 @@ static size_t g_prof_smem = 0;  // profile builds: a larger dynamic shared-memor
 #endif
 
 // the SM count of each device (nb_g1_upload records it; 148 until then)
+// a record size the tape entries take: the full record or the compact one
+static bool tape_words_ok(int w) { return w == REC_WORDS || w == REC_COMPACT; }
+
 static int g_sms[64];
 static int device_sms() {
   int dev = 0;
@@ -478,6 +486,8 @@ void nb_g1_sizes(long long out[8]) {
   const long long v[8] = {NQ, NV, NU, NB, MAXCON, NEFC, TAPE_WORDS, ABI_VERSION};
   for (int i = 0; i < 8; i++) out[i] = v[i];
 }
+
+long long nb_g1_tape_words(int compact) { return compact ? REC_COMPACT : REC_WORDS; }
 
 long long nb_g1_work_bytes(int nw) { return nw < 0 ? -1 : ((long long)nw * (long long)sizeof(int) + 15) / 16 * 16; }
 
@@ -521,12 +531,17 @@ int nb_g1_upload(const float* consts, cudaStream_t stream) {
   return (int)e;
 }
 
+int nb_g1_diag_forward_ex(cudaStream_t stream, unsigned long long* counters, int nw, int nsub, int iterations,
+                          const int* info, const float* tape, int tape_words) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || !tape_words_ok(tape_words)) return (int)cudaErrorInvalidValue;
+  if (!counters || (nw > 0 && !info)) return (int)cudaErrorInvalidValue;
+  k_diag_fwd<<<diag_grid(nw), 256, 0, stream>>>(counters, nw, nsub, iterations, info, tape, tape_words);
+  return (int)cudaGetLastError();
+}
+
 int nb_g1_diag_forward(cudaStream_t stream, unsigned long long* counters, int nw, int nsub, int iterations,
                        const int* info, const float* tape) {
-  if (nw < 0 || nsub < 1 || nsub > 32) return (int)cudaErrorInvalidValue;
-  if (!counters || (nw > 0 && !info)) return (int)cudaErrorInvalidValue;
-  k_diag_fwd<<<diag_grid(nw), 256, 0, stream>>>(counters, nw, nsub, iterations, info, tape);
-  return (int)cudaGetLastError();
+  return nb_g1_diag_forward_ex(stream, counters, nw, nsub, iterations, info, tape, REC_WORDS);
 }
 
 int nb_g1_diag_backward(cudaStream_t stream, unsigned long long* counters, int nw, const float* gq, const float* gv,
@@ -585,9 +600,11 @@ int nb_g1_kinematics_vjp(cudaStream_t stream, int nw, const float* qpos, const f
   return (int)cudaGetLastError();
 }
 
-int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
-                   float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal) {
-  if (nw < 0 || nsub < 1 || nsub > 32 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3)
+int nb_g1_jacobian_ex(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction,
+                      const float* com, float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv,
+                      int normal, int tape_words) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3 ||
+      !tape_words_ok(tape_words))
     return (int)cudaErrorInvalidValue;
   if (nw == 0) return 0;
   if (!tape || !friction || !com || !jac || !info) return (int)cudaErrorInvalidValue;
@@ -595,14 +612,22 @@ int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, con
   cudaError_t e = cudaMemsetAsync(info, 0, sizeof(int) * (size_t)nw, stream);
   if (e != cudaSuccess) return (int)e;
   k_jacobian<<<(unsigned)nw, JTHREADS, JSMEM, stream>>>(nw, nsub, tape, friction, com, jac, info, ctrl, clamp_soft,
-                                                         clamp_kv, normal);
+                                                         clamp_kv, normal, tape_words);
   return (int)cudaGetLastError();
 }
 
-int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
-                  const float* gq_out, const float* gv_out, float* gq_in, float* gv_in, float* gctrl, int* info,
-                  const float* ctrl, float clamp_soft, int clamp_kv, int normal) {
-  if (nw < 0 || nsub < 1 || nsub > 32 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3)
+int nb_g1_jacobian(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
+                   float* jac, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal) {
+  return nb_g1_jacobian_ex(stream, nw, nsub, tape, friction, com, jac, info, ctrl, clamp_soft, clamp_kv, normal,
+                           REC_WORDS);
+}
+
+int nb_g1_adjoint_ex(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction,
+                     const float* com, const float* gq_out, const float* gv_out, float* gq_in, float* gv_in,
+                     float* gctrl, int* info, const float* ctrl, float clamp_soft, int clamp_kv, int normal,
+                     int tape_words) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || clamp_kv < 0 || clamp_kv > 2 || normal < 0 || normal > 3 ||
+      !tape_words_ok(tape_words))
     return (int)cudaErrorInvalidValue;
   if (nw == 0) return 0;
   if (!tape || !friction || !com || !gq_out || !gv_out || !gq_in || !gv_in || !gctrl || !info)
@@ -613,15 +638,23 @@ int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, cons
   auto kernel = wpb <= AWPB_SMALL ? k_adjoint<AWPB_SMALL> : k_adjoint<AWPB>;
   kernel<<<blocks, wpb * 32, sizeof(AdjBlock) * wpb, stream>>>(nw, nsub, tape, friction, com, gq_out, gv_out, gq_in,
                                                                gv_in, gctrl, info, ctrl, clamp_soft, clamp_kv,
-                                                               normal);
+                                                               normal, tape_words);
   return (int)cudaGetLastError();
+}
+
+int nb_g1_adjoint(cudaStream_t stream, int nw, int nsub, const float* tape, const float* friction, const float* com,
+                  const float* gq_out, const float* gv_out, float* gq_in, float* gv_in, float* gctrl, int* info,
+                  const float* ctrl, float clamp_soft, int clamp_kv, int normal) {
+  return nb_g1_adjoint_ex(stream, nw, nsub, tape, friction, com, gq_out, gv_out, gq_in, gv_in, gctrl, info, ctrl,
+                          clamp_soft, clamp_kv, normal, REC_WORDS);
 }
 
 static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
                           const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
                           float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape,
-                          int* stats, int* order) {
-  if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0) return (int)cudaErrorInvalidValue;
+                          int* stats, int* order, int tape_words = REC_WORDS) {
+  if (nw < 0 || nsub < 1 || nsub > 32 || iterations < 0 || !tape_words_ok(tape_words))
+    return (int)cudaErrorInvalidValue;
   if (nw == 0) return 0;
   if (!qpos || !qvel || !warm || !ctrl || !friction || !com || !qpos_out || !qvel_out || !warm_out || !info)
     return (int)cudaErrorInvalidValue;
@@ -638,7 +671,7 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
     if (e != cudaSuccess) return (int)e;
   }
   k_forward<<<blocks, WPB * 32, smem, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
-                                                qvel_out, warm_out, info, ocon, stats, tape, order);
+                                                qvel_out, warm_out, info, ocon, stats, tape, order, tape_words);
   return (int)cudaGetLastError();
 }
 
@@ -647,6 +680,14 @@ int nb_g1_forward(cudaStream_t stream, int nw, const float* qpos, const float* q
                   float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape, void* work) {
   return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
                         warm_out, info, ocon, tape, nullptr, static_cast<int*>(work));
+}
+
+int nb_g1_forward_ex(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,
+                     const float* ctrl, const float* friction, const float* com, int iterations, int nsub,
+                     float* qpos_out, float* qvel_out, float* warm_out, int* info, float* ocon, float* tape,
+                     void* work, int tape_words) {
+  return launch_forward(stream, nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out, qvel_out,
+                        warm_out, info, ocon, tape, nullptr, static_cast<int*>(work), tape_words);
 }
 
 int nb_g1_forward_stats(cudaStream_t stream, int nw, const float* qpos, const float* qvel, const float* warm,

@@ -58,9 +58,12 @@ struct __align__(16) Adj {
   unsigned zone[NEFC / 32];           // the record's zone bits (row r quadratic: bit r & 31 of word r / 32)
   int nlim_tape, flags, normal, pad_;  // normal: the self-contact normal derivative option (0..3)
   union {
-    struct {                          // the solves: L_Q (tree-block order), then L_H, with its inverse diagonal
-      float L[NTRIP];
+    struct alignas(16) {              // the solves: L_Q (tree-block order), then L_H, with its inverse diagonal;
+      float L[NTRIP];                 // from a compact tape also M + h kv rebuilt for L_Q (adj_mass_factor); L and M
+                                      // are written as float4 (tb_factor, adj_mass_factor): 16-byte aligned
       float dinv[NV + 1];
+      float M[NTRIP];
+      float Ic[NB][10];
     };
     struct {                          // the replay and the contacts
       float cw[32][30];               // a batch of 32 contacts' wrenches
@@ -78,6 +81,8 @@ struct __align__(16) Adj {
   long long prof_t;
 #endif
 };
+static_assert(sizeof(AWorld) % 16 == 0 && offsetof(Adj, L) % 16 == 0 && offsetof(Adj, M) % 16 == 0,
+              "the solves' factor and mass-matrix scratch are written as float4");
 
 // What every cotangent of a record shares (the Jacobian's preparation: its per-record replay beside AWorld)
 struct __align__(16) AdjShared {
@@ -981,22 +986,15 @@ __device__ __forceinline__ void copy_factor_tb(float* dst, const float* src, int
     if (lane + 32 * q < NTB) dst[g_tb_index.e[lane + 32 * q]] = v[q];
 }
 
-// One substep of the adjoint from its tape record rec. What every cotangent of the record shares: adj_record (the
-// record's state into s and W; with the factors' buffers given also both factors: L_Q into LQ / dinvQ, L_H into
-// LH / dinvH) and
-// adj_replay (the replayed poses, velocities and accelerations, the motions of a* and v, the geom poses and contact
-// rows). One cotangent, A.qout / A.vb in (the substep output's tangent and velocity cotangents), out the input's
-// (A.qout, A.vb), A.ub accumulating the ctrl gradient: adj_row_solve (the integrator and both solves; without the
-// factors' buffers it copies each factor into the state's own scratch just before its solve) and adj_row_rest. block_sync: every warp of the block calls adj_row together; a block barrier before the limit
-// rows and the sweep re-aligns the worlds after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
-// the solve scratch of a cotangent's state: k_adjoint's Adj holds its own (the factor is copied in just before each
-// solve)
-__device__ __forceinline__ float* solve_scratch(Adj& A) { return A.L; }
-__device__ __forceinline__ float* solve_scratch_dinv(Adj& A) { return A.dinv; }
-
+// One substep of the adjoint from its tape record rec: adj_record (the record's state into s and W), the replay
+// (adj_replay: poses, velocities and accelerations, the motions of a* and v, the geom poses and contact rows), and for
+// the cotangent (A.qout / A.vb in: the substep output's tangent and velocity cotangents; out: the input's, A.ub
+// accumulating the ctrl gradient) adj_row_solve (the integrator and both solves, each factor copied into the state's
+// scratch just before its solve, L_Q rebuilt there from a compact record) and adj_row_rest. block_sync: every warp of
+// the block calls adj_substep together; a block barrier before the limit rows and the sweep re-aligns the worlds
+// after their contact loops (different lengths): 1.06 -> 1.02 ms at B = 4096
 template <class SH>
-__device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, float* LQ, float* dinvQ, float* LH,
-                                           float* dinvH, int lane) {
+__device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, int lane) {
   for (int i = lane; i < NQ; i += 32) s.qpos[i] = rec[T_QPOS + i];
   for (int i = lane; i < NV; i += 32) {
     s.qvel[i] = rec[T_QVEL + i];
@@ -1017,11 +1015,6 @@ __device__ __forceinline__ void adj_record(AWorld& s, SH& W, const float* rec, f
     const unsigned e = (__float_as_uint(rec[T_CON + c / 2]) >> (16 * (c & 1))) & 0xffffu;
     s.con_pair[c] = (int)(e & 511u);
     s.con_slot[c] = (unsigned char)(e >> 9);
-  }
-  if (LH) {
-    copy_factor_tb(LQ, rec + T_LQ, lane, false);  // (LQ holds L_Q only: zeroed once)
-    copy_factor(LH, rec + T_LH, lane);
-    for (int i = lane; i < NV; i += 32) { dinvQ[i] = rec[T_DINVQ + i]; dinvH[i] = rec[T_DINVH + i]; }
   }
   __syncwarp();
 }
@@ -1074,9 +1067,98 @@ __device__ __forceinline__ void adj_replay(AWorld& s, SH& W, int lane) {
   __syncwarp();
 }
 
+// L_Q from the replayed poses (the compact tape stores none): the forward's mass matrix (mass_and_force: each body's
+// spatial inertia about the pelvis origin O summed over its subtree, M_ij = s_j . I s_i over the ancestor dofs j of
+// dof i, the armature on the diagonal) and its tree-block factor with h kv, into L / dinv. M and Ic: scratch; lane =
+// body, then dof.
+template <class SH>
+__device__ __noinline__ void adj_mass_factor(const AWorld& s, const SH& W, float* M, float (*Ic)[10], float* L,
+                                             float* dinv, int lane) {
+  const float O[3] = {s.X[1][0], s.X[1][1], s.X[1][2]};
+  const int b = lane;
+  if (b >= 1 && b < NB) {
+    float ip[3] = {ld(g1_body_ipos + 3 * b), ld(g1_body_ipos + 3 * b + 1), ld(g1_body_ipos + 3 * b + 2)};
+    if (b == G1_TORSO)
+      for (int k = 0; k < 3; k++) ip[k] += s.com[k];
+    float c[3], qi[4], Rm[3][3];
+    qrot(s.Q[b], ip, c);
+    const float iq[4] = {ld(g1_body_iquat + 4 * b), ld(g1_body_iquat + 4 * b + 1), ld(g1_body_iquat + 4 * b + 2),
+                         ld(g1_body_iquat + 4 * b + 3)};
+    qmul(s.Q[b], iq, qi);
+    for (int k = 0; k < 3; k++) {
+      float e[3] = {0.f, 0.f, 0.f}, col[3];
+      e[k] = 1.f;
+      qrot(qi, e, col);
+      for (int r = 0; r < 3; r++) Rm[r][k] = col[r];
+    }
+    const float In[3] = {ld(g1_body_inertia + 3 * b), ld(g1_body_inertia + 3 * b + 1),
+                         ld(g1_body_inertia + 3 * b + 2)};
+    float I[3][3];
+    for (int r = 0; r < 3; r++)
+      for (int q = r; q < 3; q++) {
+        const float v = Rm[r][0] * In[0] * Rm[q][0] + Rm[r][1] * In[1] * Rm[q][1] + Rm[r][2] * In[2] * Rm[q][2];
+        I[r][q] = v; I[q][r] = v;
+      }
+    const float m = ld(g1_body_mass + b);
+    float cO[3];
+    for (int k = 0; k < 3; k++) cO[k] = s.X[b][k] + c[k] - O[k];
+    const float cc = dot3(cO, cO);
+    float* J = Ic[b];
+    J[0] = I[0][0] + m * (cc - cO[0] * cO[0]);
+    J[1] = I[1][1] + m * (cc - cO[1] * cO[1]);
+    J[2] = I[2][2] + m * (cc - cO[2] * cO[2]);
+    J[3] = I[0][1] - m * cO[0] * cO[1];
+    J[4] = I[0][2] - m * cO[0] * cO[2];
+    J[5] = I[1][2] - m * cO[1] * cO[2];
+    J[6] = m * cO[0]; J[7] = m * cO[1]; J[8] = m * cO[2]; J[9] = m;
+  }
+  __syncwarp();
+  const int depth = b < NB ? ldi(g1_body_depth + b) : -1, nch = b < NB ? ldi(g1_body_nchild + b) : 0;
+  for (int lv = MAXD - 1; lv >= 1; lv--) {
+    if (depth == lv && nch > 0) {
+      float J[10];
+      for (int k = 0; k < 10; k++) J[k] = Ic[b][k];
+      for (int ci = 0; ci < nch; ci++) {
+        const int ch = ldi(g1_body_child + 3 * b + ci);
+        for (int k = 0; k < 10; k++) J[k] += Ic[ch][k];
+      }
+      for (int k = 0; k < 10; k++) Ic[b][k] = J[k];
+    }
+    __syncwarp();
+  }
+  for (int e = lane; e < NTRIP / 4; e += 32) reinterpret_cast<float4*>(M)[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  // dof i's motion about O: translations (0, e_i), the pelvis's rotations (w, 0), hinges (w, w x (O - X_b))
+  auto motion = [&](int i, float* w, float* v) {
+    for (int k = 0; k < 3; k++) { w[k] = i < 3 ? 0.f : W.ax[i][k]; v[k] = i < 3 && k == i ? 1.f : 0.f; }
+    if (i >= 6) {
+      const int bb = i - 4;
+      const float r[3] = {O[0] - s.X[bb][0], O[1] - s.X[bb][1], O[2] - s.X[bb][2]};
+      cross(w, r, v);
+    }
+  };
+  for (int i = lane; i < NV; i += 32) {
+    const int bi = ldi(g1_dof_body + i);
+    float w[3], v[3], n[3], f[3];
+    motion(i, w, v);
+    apply_inertia(Ic[bi], w, v, n, f);
+    unsigned long long anc = g1_body_dofmask[bi] & ((1ull << i) - 1ull);
+    while (anc) {
+      const int j = __ffsll((long long)anc) - 1;
+      anc &= anc - 1ull;
+      float wj[3], vj[3];
+      motion(j, wj, vj);
+      M[TRI(i, j)] = dot3(wj, n) + dot3(vj, f);
+    }
+    M[TRI(i, i)] = dot3(w, n) + dot3(v, f) + ld(g1_dof_armature + i);
+  }
+  __syncwarp();
+  tb_factor(M, true, L, dinv, lane);
+}
+
+// full: rec holds L_Q (a full record), else it is rebuilt from the replayed poses (adj_replay_kin must have run)
 template <class SH, class RW>
-__device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, const float* rec, const float* LQ,
-                                              const float* dinvQ, const float* LH, const float* dinvH, int lane) {
+__device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, const float* rec, bool full, int lane) {
   const float h = G1_TIMESTEP;
   PROF_START(A);
   // A1: the integrator. v' = v + h a_adv; root rotation: q' = q exp(h w' / 2). The input tangent gets qbar' (kept in
@@ -1116,28 +1198,25 @@ __device__ __forceinline__ void adj_row_solve(AWorld& s, const SH& W, RW& A, con
     __syncwarp();
   }
   PROF(A, 0);
-  // y = (M + h kv)^-1 abar_adv with L_Q; abar* = abar_adv - h kv y
-  float* L = solve_scratch(A);  // (without the record's factors: each copied here just before its solve)
-  float* dinv = solve_scratch_dinv(A);
-  if (!LQ) {
+  // y = (M + h kv)^-1 abar_adv with L_Q; abar* = abar_adv - h kv y (each factor copied in just before its solve)
+  float* L = A.L;
+  float* dinv = A.dinv;
+  if (full) {
     copy_factor_tb(L, rec + T_LQ, lane, true);
     for (int i = lane; i < NV; i += 32) dinv[i] = rec[T_DINVQ + i];
+  } else {
+    adj_mass_factor(s, W, A.M, A.Ic, L, dinv, lane);
   }
   for (int i = lane; i < NV; i += 32) A.lam[i] = A.y[i];
   __syncwarp();
-  chol_solve<true>(LQ ? LQ : L, LQ ? dinvQ : dinv, A.y, lane);  // L_Q is in tree-block order
+  chol_solve<true>(L, dinv, A.y, lane);  // L_Q is in tree-block order
   for (int i = lane; i < NV; i += 32) A.lam[i] -= h * ld(g1_dof_kv + i) * A.y[i];
   // A2: lambda = H^-1 abar* with L_H
-  if (!LH) {
-    __syncwarp();
-    copy_factor(L, rec + T_LH, lane);
-    for (int i = lane; i < NV; i += 32) dinv[i] = rec[T_DINVH + i];
-    __syncwarp();
-    chol_solve(L, dinv, A.lam, lane);
-  } else {
-    __syncwarp();
-    chol_solve(LH, dinvH, A.lam, lane);
-  }
+  __syncwarp();
+  copy_factor(L, rec + T_LH, lane);
+  for (int i = lane; i < NV; i += 32) dinv[i] = rec[T_DINVH + i];
+  __syncwarp();
+  chol_solve(L, dinv, A.lam, lane);
   PROF(A, 1);
 }
 
@@ -1191,11 +1270,22 @@ __device__ __forceinline__ int adj_row_rest(AWorld& s, const SH& W, RW& A, const
 }
 
 // the adjoint's substep (one cotangent per world): both parts in one warp, the factors copied as they are needed
-__device__ __forceinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, int clamp_kv, float clamp_soft,
-                                           float (*cw)[30], int lane, bool block_sync = false) {
-  adj_record(s, A, rec, nullptr, nullptr, nullptr, nullptr, lane);
-  adj_row_solve(s, A, A, rec, nullptr, nullptr, nullptr, nullptr, lane);
-  adj_replay(s, A, lane);
+// full: a full record (else compact: the poses are replayed first, for the rebuilt L_Q)
+__device__ __forceinline__ int adj_substep(AWorld& s, Adj& A, const float* rec, bool full, int clamp_kv,
+                                           float clamp_soft, float (*cw)[30], int lane, bool block_sync = false) {
+  adj_record(s, A, rec, lane);
+  if (full) {
+    adj_row_solve(s, A, A, rec, true, lane);
+    adj_replay(s, A, lane);
+  } else {
+    adj_replay_kin(s, A, lane);
+    adj_row_solve(s, A, A, rec, false, lane);
+    adj_motion(s, A, s.qacc, A.VA, lane);
+    adj_motion(s, A, s.qvel, A.VV, lane);
+    adj_replay_geoms(s, A, lane);
+    adj_replay_rows(s, A, lane);
+    __syncwarp();
+  }
   return adj_row_rest(s, A, A, rec, clamp_kv, clamp_soft, cw, lane, block_sync);
 }
 

@@ -70,8 +70,9 @@ struct __align__(16) JRec {
 // space of lambda and y, which the cotangents write only after it.
 constexpr int JO_LAM = 0, JO_Y = NV, JO_Q = 2 * NV, JO_V = 3 * NV, JO_U = 4 * NV, JO_SLOT = 4 * NV + NU;
 constexpr int JSLOT = 36, JRHS_ROWS = JO_SLOT + JSLOT;
-struct JPrep { AWorld s; AdjShared W; };
+struct JPrep { AWorld s; AdjShared W; float M[NTRIP]; float Ic[NB][10]; };  // (M, Ic: a compact record's L_Q)
 static_assert(sizeof(JPrep) <= sizeof(float) * 2 * NV * JS, "the preparation's scratch fits lambda and y");
+static_assert(offsetof(JPrep, M) % 16 == 0 && offsetof(JRec, LQ) % 16 == 0, "written as float4 by adj_mass_factor");
 struct __align__(16) JBlock {
   JRec R;
   union {
@@ -85,22 +86,25 @@ struct __align__(16) JBlock {
 // (warp 2); 2: the replay (warp 0), the limit and actuator coefficients (warp 1), each body's contact list (warp 2);
 // 3: the contacts' matrices (thread = contact), then the bodies' and dofs' terms; 4: G(lambda) onto the bodies and
 // the shared subtree sums (warp 0)
-__device__ __forceinline__ void jac_prep_state(JBlock& B, const float* rec, const float* fric_w, const float* com_w,
-                                               const float* ctrl_w, int t) {
+__device__ __forceinline__ void jac_prep_state(JBlock& B, const float* rec, bool full, const float* fric_w,
+                                               const float* com_w, const float* ctrl_w, int t) {
   JRec& R = B.R;
   AWorld& s = B.prep.s;
   AdjShared& W = B.prep.W;
   const int warp = t >> 5, lane = t & 31;
   const float h = G1_TIMESTEP;
   if (warp == 0) {
-    adj_record(s, W, rec, nullptr, nullptr, nullptr, nullptr, lane);
+    adj_record(s, W, rec, lane);
     if (lane == 0) { s.fric = *fric_w; R.ncon = s.ncon; }
     if (lane < 3) s.com[lane] = com_w[lane];
     for (int i = lane; i < NU; i += 32) W.u[i] = ctrl_w ? ctrl_w[i] : 0.f;
   } else if (warp == 1) {
-    copy_factor_tb(R.LQ, rec + T_LQ, lane, false);  // (entries off L_Q's pattern: zeroed once)
+    if (full) {  // (a compact record's L_Q is rebuilt from the replayed poses in step 3)
+      copy_factor_tb(R.LQ, rec + T_LQ, lane, false);  // (entries off L_Q's pattern: zeroed once)
+      for (int i = lane; i < NV; i += 32) R.dinvQ[i] = rec[T_DINVQ + i];
+    }
     copy_factor(R.LH, rec + T_LH, lane);
-    for (int i = lane; i < NV; i += 32) { R.dinvQ[i] = rec[T_DINVQ + i]; R.dinvH[i] = rec[T_DINVH + i]; }
+    for (int i = lane; i < NV; i += 32) R.dinvH[i] = rec[T_DINVH + i];
   } else {
     for (int i = lane; i < NV; i += 32) {
       R.vd[i] = rec[T_QVEL + i];
@@ -344,13 +348,14 @@ __device__ __forceinline__ void jac_prep_sums(JRec& R, int lane) {
 }
 
 // the whole preparation of record rec (every thread of the block)
-__device__ __forceinline__ void jac_prep(JBlock& B, const float* rec, const float* fric_w, const float* com_w,
-                                         const float* ctrl_w, float clamp_soft, int clamp_kv, int normal, int t) {
+__device__ __forceinline__ void jac_prep(JBlock& B, const float* rec, bool full, const float* fric_w,
+                                         const float* com_w, const float* ctrl_w, float clamp_soft, int clamp_kv,
+                                         int normal, int t) {
   JRec& R = B.R;
   AWorld& s = B.prep.s;
   AdjShared& W = B.prep.W;
   const int warp = t >> 5, lane = t & 31;
-  jac_prep_state(B, rec, fric_w, com_w, ctrl_w, t);
+  jac_prep_state(B, rec, full, fric_w, com_w, ctrl_w, t);
   __syncthreads();
   if (warp == 0) adj_replay_kin(s, W, lane);
   else if (warp == 1) jac_prep_dofs(R, s, W, clamp_soft, clamp_kv, lane);
@@ -368,6 +373,7 @@ __device__ __forceinline__ void jac_prep(JBlock& B, const float* rec, const floa
     if (lane >= 1 && lane < NB) jac_prep_body(R, s, W, lane);
   } else {
     adj_motion(s, W, s.qvel, W.VV, lane);
+    if (!full) adj_mass_factor(s, W, B.prep.M, B.prep.Ic, R.LQ, R.dinvQ, lane);
   }
   __syncthreads();
   for (int i = t; i < 3 * R.ncon; i += JTHREADS) jac_prep_contact(R, s, W, normal, i);

@@ -46,17 +46,18 @@ constexpr int ROWS_PER_LANE = (WROWS + 31) / 32;
 enum : int { UNSUPPORTED_PAIR = 1, CONTACT_OVERFLOW = 4, ROW_OVERFLOW = 16 };
 
 // The forward tape: one record of REC_WORDS float32 words per world and substep (record w * nsub + k), what the
-// adjoint reads: the substep's input state, the Newton solution a*, a_adv = (M + h kv)^-1 M a*, the Cholesky factors
-// of the Newton Hessian at the final zones (L_H, dof order) and of M + h kv (L_Q, tree-block order: tb_factor, only
-// the entries of its pattern) with their inverse diagonals, the contact
-// table (pair | slot << 9, two 16-bit entries per word, contact order), the rows' final zone bits, the actuator
-// clamp mask (dof bits) and a header
-constexpr int T_QPOS = 0, T_QVEL = 36, T_ASTAR = 71, T_AADV = 106, T_DINVH = 141, T_DINVQ = 176, T_LH = 211;
+// adjoint reads: the substep's input state, the Newton solution a*, a_adv = (M + h kv)^-1 M a*, the Cholesky factor
+// of the Newton Hessian at the final zones (L_H, dof order) with its inverse diagonal, the contact table (pair | slot
+// << 9, two 16-bit entries per word, contact order), the rows' final zone bits, the actuator clamp mask (dof bits), a
+// header and flags, then the factor of M + h kv (L_Q, tree-block order: tb_factor, only the entries of its pattern)
+// with its inverse diagonal. The compact tape's records are the first REC_COMPACT words of these (no L_Q: its reader
+// rebuilds M + h kv from the replayed poses and factors it).
+constexpr int T_QPOS = 0, T_QVEL = 36, T_ASTAR = 71, T_AADV = 106, T_DINVH = 141, T_LH = 176;
 constexpr int NTB_TAPE = 341;  // the tree-block factor's pattern (NTB, checked below)
-constexpr int T_LQ = T_LH + NTRI, T_CON = T_LQ + NTB_TAPE, T_ZONE = T_CON + MAXCON / 2;
-constexpr int T_CLAMP = T_ZONE + NEFC / 32;
-constexpr int T_HDR = T_CLAMP + 2, T_FLAGS = T_HDR + 1, REC_WORDS = ((T_FLAGS + 1 + 3) / 4) * 4;
-static_assert(T_LQ == 841 && REC_WORDS == 1224, "tape layout");
+constexpr int T_CON = T_LH + NTRI, T_ZONE = T_CON + MAXCON / 2, T_CLAMP = T_ZONE + NEFC / 32;
+constexpr int T_HDR = T_CLAMP + 2, T_FLAGS = T_HDR + 1, REC_COMPACT = T_FLAGS + 1;
+constexpr int T_DINVQ = REC_COMPACT, T_LQ = T_DINVQ + NV, REC_WORDS = T_LQ + NTB_TAPE;
+static_assert(REC_COMPACT == 848 && REC_WORDS == 1224 && REC_COMPACT % 4 == 0 && REC_WORDS % 4 == 0, "tape layout");
 // TAPE_SINGULAR: a pivot of the recorded Hessian factor was clamped (at 1e-30: not positive definite in float32)
 enum : unsigned { TAPE_REFACT = 1u << 8, TAPE_NONCONV = 1u << 9, TAPE_SINGULAR = 1u << 12 };
 enum : unsigned char { ROW_LIMIT = 0, ROW_PYRAMID = 1, ROW_NORMAL = 2 };
@@ -1680,8 +1681,9 @@ __device__ __noinline__ void substep_pre(World& s, int lane, float* rec) {
 }
 
 // stats: null, or this world's 8 counters of the substep (contacts kept, rows, Newton iterations, line-search
-// evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count
-__device__ __noinline__ void substep_post(World& s, int lane, int* stats, float* rec) {
+// evaluations, Hessian factorisations, broad-phase candidates, contacts found, 0), the inputs of the FLOP count;
+// rec: null or the tape record, full (REC_WORDS) or compact (REC_COMPACT: no L_Q)
+__device__ __noinline__ void substep_post(World& s, int lane, int* stats, float* rec, bool full) {
   const float h = G1_TIMESTEP;
   PROF(s, 25);  // (profile builds: the wait at the block barriers after this world's last iteration)
   const int it = s.nit_cur;
@@ -1715,7 +1717,6 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
       __stcs(rec + T_HDR, __uint_as_float((unsigned)ncon | (unsigned)nefc << 8 | (unsigned)s.nlim << 16));
       __stcs(rec + T_FLAGS, __uint_as_float((unsigned)s.unsup | (refact ? TAPE_REFACT : 0u) |
                                             (s.ndone ? 0u : TAPE_NONCONV) | (sing ? TAPE_SINGULAR : 0u)));
-      for (int k = T_FLAGS + 1; k < REC_WORDS; k++) __stcs(rec + k, 0.f);
     }
     __syncwarp();
   }
@@ -1729,8 +1730,10 @@ __device__ __noinline__ void substep_post(World& s, int lane, int* stats, float*
   tb_factor(s.M, true, s.L, s.dinv, lane);
   chol_solve<true>(s.L, s.dinv, s.p, lane);
   if (rec) {
-    for (int e = lane; e < NTB; e += 32) __stcs(rec + T_LQ + e, s.L[g_tb_index.e[e]]);
-    tape_put(rec + T_DINVQ, s.dinv, NV, lane);
+    if (full) {
+      for (int e = lane; e < NTB; e += 32) __stcs(rec + T_LQ + e, s.L[g_tb_index.e[e]]);
+      tape_put(rec + T_DINVQ, s.dinv, NV, lane);
+    }
     tape_put(rec + T_AADV, s.p, NV, lane);
   }
   for (int i = lane; i < NV; i += 32) s.qvel[i] += h * s.p[i];

@@ -121,14 +121,25 @@ def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
-def _rec_words():
-    return int(capi.sizes()[6])
+def _rec_words(compact=False):
+    return capi.tape_words(compact)
 
 
-def tape_bytes(nworld, substeps=SUBSTEPS, steps=1):
+def _tape_words(tape, nsub):
+    """The record size of a tape argument (full or compact records), from its width; else the full one (for the
+    shape check's message)."""
+    import torch
+    if isinstance(tape, torch.Tensor) and tape.dim() == 2:
+        for words in (_rec_words(False), _rec_words(True)):
+            if tape.shape[1] == nsub * words:
+                return words
+    return _rec_words(False)
+
+
+def tape_bytes(nworld, substeps=SUBSTEPS, steps=1, compact=False):
     """Bytes of the tapes that `steps` differentiated control steps of nworld worlds hold until their backward
-    (reference torch_ffi.py:454)."""
-    return 4 * _rec_words() * substeps * nworld * steps
+    (reference torch_ffi.py:454); compact: the compact tape's records (no L_Q)."""
+    return 4 * _rec_words(compact) * substeps * nworld * steps
 
 
 # ---- per-device state: preparation, counters, last-forward records ------------------------------------------------
@@ -209,7 +220,7 @@ def _launch(dev, entry, *args):
 
 
 # ---- the library calls --------------------------------------------------------------------------------------------
-def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape=False):
+def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape=False, compact=False):
     import torch
     B, dev = _validate([(n, x, t) for (n, t), x in zip(STATE_ARGS, (qpos, qvel, warm, ctrl, friction, com))])
     nsub, iters = _substeps(substeps), int(iterations)
@@ -219,16 +230,17 @@ def _forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, t
     f32 = dict(dtype=torch.float32, device=qpos.device)
     outs = (torch.empty((B, NQ), **f32), torch.empty((B, NV), **f32), torch.empty((B, NV), **f32),
             torch.empty((B, 4), dtype=torch.int32, device=qpos.device))
-    tp = torch.empty((B if tape else 0, nsub * _rec_words()), **f32)
+    words = _rec_words(compact)
+    tp = torch.empty((B if tape else 0, nsub * words), **f32)
     if B == 0:
         return outs + (tp,)
     nwork = int(capi.load().nb_g1_work_bytes(B))
     work = torch.empty((nwork,), dtype=torch.uint8, device=qpos.device)
-    _launch(dev, "nb_g1_forward", B, *map(_p, (qpos, qvel, warm, ctrl, friction, com)), iters, nsub,
-            *map(_p, outs[:4]), None, _p(tp) if tape else None, _p(work))
+    _launch(dev, "nb_g1_forward_ex", B, *map(_p, (qpos, qvel, warm, ctrl, friction, com)), iters, nsub,
+            *map(_p, outs[:4]), None, _p(tp) if tape else None, _p(work), words)
     if _Settings.counters:
-        _launch(dev, "nb_g1_diag_forward", _p(state.counters), B, nsub, iters, _p(outs[3]),
-                _p(tp) if tape else None)
+        _launch(dev, "nb_g1_diag_forward_ex", _p(state.counters), B, nsub, iters, _p(outs[3]),
+                _p(tp) if tape else None, words)
         _launch(dev, "nb_g1_last_forward", B, _p(outs[3]), _p(state.last[None]), _p(state.last_slot(B)))
     return outs + (tp,)
 
@@ -240,7 +252,8 @@ def _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv
     nm = _int_option("normal", normal, {0, 1, 2, 3})
     if (kv == 2) != (ctrl is not None):
         raise _fail("the soft clamp (clamp_kv=2) needs the step's ctrl, and only it takes one", ValueError)
-    args = [("tape", tape, (nsub * _rec_words(),)), ("friction", friction, ()), ("com", com, (3,)),
+    words = _tape_words(tape, nsub)
+    args = [("tape", tape, (nsub * words,)), ("friction", friction, ()), ("com", com, (3,)),
             ("g_qpos", g_qpos, (NQ,)), ("g_qvel", g_qvel, (NV,))]
     if ctrl is not None:
         args.append(("ctrl", ctrl, (NU,)))
@@ -251,8 +264,8 @@ def _backward_impl(tape, friction, com, g_qpos, g_qvel, ctrl, substeps, clamp_kv
             torch.empty((B,), dtype=torch.int32, device=tape.device))
     if B == 0:
         return outs
-    _launch(dev, "nb_g1_adjoint", B, nsub, *map(_p, (tape, friction, com, g_qpos, g_qvel) + outs + (ctrl,)),
-            ctypes.c_float(clamp_soft), kv, nm)
+    _launch(dev, "nb_g1_adjoint_ex", B, nsub, *map(_p, (tape, friction, com, g_qpos, g_qvel) + outs + (ctrl,)),
+            ctypes.c_float(clamp_soft), kv, nm, words)
     if _Settings.counters:
         _launch(dev, "nb_g1_diag_backward", _p(state.counters), B, *map(_p, outs[:3] + (g_qpos, g_qvel, outs[3])))
     return outs
@@ -296,7 +309,8 @@ def jacobian(tape, friction, com, *, substeps=SUBSTEPS, clamp_kv=1, normal=0, ct
     width = _soft_width(kv, clamp_soft)
     if (kv == 2) != (ctrl is not None):
         raise _fail("the soft clamp (clamp_kv=2) needs the step's ctrl, and only it takes one", ValueError)
-    args = [("tape", tape, (nsub * _rec_words(),)), ("friction", friction, ()), ("com", com, (3,))]
+    words = _tape_words(tape, nsub)
+    args = [("tape", tape, (nsub * words,)), ("friction", friction, ()), ("com", com, (3,))]
     if ctrl is not None:
         args.append(("ctrl", ctrl, (NU,)))
     B, dev = _validate(args)
@@ -304,8 +318,8 @@ def jacobian(tape, friction, com, *, substeps=SUBSTEPS, clamp_kv=1, normal=0, ct
     J = torch.empty((B, NOUT, NTAN), dtype=torch.float32, device=tape.device)
     info = torch.empty((B,), dtype=torch.int32, device=tape.device)
     if B:
-        _launch(dev, "nb_g1_jacobian", B, nsub, *map(_p, (tape, friction, com, J, info, ctrl)),
-                ctypes.c_float(0.0 if width is None else width), kv, nm)
+        _launch(dev, "nb_g1_jacobian_ex", B, nsub, *map(_p, (tape, friction, com, J, info, ctrl)),
+                ctypes.c_float(0.0 if width is None else width), kv, nm, words)
     return J, info
 
 
@@ -324,14 +338,14 @@ def _register_ops():
 
     @torch.library.custom_op("nabla_b200::forward", mutates_args=())
     def forward_op(qpos: T, qvel: T, warm: T, ctrl: T, friction: T, com: T, iterations: int, substeps: int,
-                   tape: bool) -> List[T]:
-        return list(_forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape))
+                   tape: bool, compact: bool = False) -> List[T]:
+        return list(_forward_impl(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape, compact))
 
     @forward_op.register_fake
-    def _(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape):
+    def _(qpos, qvel, warm, ctrl, friction, com, iterations, substeps, tape, compact=False):
         B = qpos.shape[0]
         return empty_like_outputs(qpos, [((B, NQ), None), ((B, NV), None), ((B, NV), None), ((B, 4), torch.int32),
-                                         ((B if tape else 0, substeps * _rec_words()), None)])
+                                         ((B if tape else 0, substeps * _rec_words(compact)), None)])
 
     @torch.library.custom_op("nabla_b200::backward", mutates_args=())
     def backward_op(tape: T, friction: T, com: T, g_qpos: T, g_qvel: T, ctrl: Optional[T], substeps: int,
@@ -392,7 +406,7 @@ def _autograd_function(name):
         @staticmethod
         def forward(ctx, qpos, qvel, warm, ctrl, friction, com, opts):
             q1, v1, w1, _, tp = custom_ops()["forward"](qpos, qvel, warm, ctrl, friction, com, opts["iterations"],
-                                                        opts["substeps"], True)
+                                                        opts["substeps"], True, opts["compact_tape"])
             ctx.save_for_backward(tp, friction, com, ctrl)
             ctx.opts = opts
             ctx.mark_non_differentiable(w1)
@@ -457,8 +471,12 @@ def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, sub
     """One control step without autograd (reference torch_ffi.py:845): (qpos', qvel', warm', info (B, 4) int32
     [, tape][, the kinematics outputs of (qpos', qvel')]). info = [Newton iterations of the last substep, the
     contacts its collision found (may exceed 64), its constraint rows, bits 1 unsupported pair / 4 contacts beyond 64 /
-    16 rows beyond 192, ORed over the substeps]."""
-    r = custom_ops()["forward"](qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape))
+    16 rows beyond 192, ORed over the substeps]. tape: False, True (full records) or "compact" (records without the
+    factor of M + h kv, which backward and jacobian rebuild: 31 % less tape); backward and jacobian take either."""
+    if tape not in (False, True, "compact"):
+        raise _fail(f"tape must be False, True or 'compact', got {tape!r}", ValueError)
+    r = custom_ops()["forward"](qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape),
+                                tape == "compact")
     out = tuple(r) if tape else tuple(r[:4])
     if kinematics:
         out += tuple(custom_ops()["kinematics"](r[0], r[1], com))
@@ -499,15 +517,17 @@ def kinematics(qpos, qvel, com):
 
 
 def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, substeps=SUBSTEPS, clamp_kv=CLAMP_KV,
-         normal=NORMAL, clamp_soft=None, grad_decay=GRAD_DECAY, kinematics=False):
+         normal=NORMAL, clamp_soft=None, grad_decay=GRAD_DECAY, kinematics=False, compact_tape=False):
     """One control step (reference torch_ffi.py:817): (qpos', qvel', warm'). Differentiable in qpos, qvel and ctrl
-    when an input requires grad (the forward then also writes the tape); warm' is not differentiable. clamp_kv,
-    normal, clamp_soft and grad_decay select the backward; with kinematics=True the output state's kinematics follow,
-    and their cotangents flow back into (qpos', qvel')'s."""
+    when an input requires grad (the forward then also writes the tape; compact_tape=True: the compact records, kept
+    until the backward in 31 % less memory, the backward rebuilding the factor of M + h kv); warm' is not
+    differentiable. clamp_kv, normal, clamp_soft and grad_decay select the backward; with kinematics=True the output
+    state's kinematics follow, and their cotangents flow back into (qpos', qvel')'s."""
     kv = _int_option("clamp_kv", clamp_kv, {0, 1, 2})
     nm = _int_option("normal", normal, {0, 1, 2, 3})
     opts = {"iterations": int(iterations), "substeps": int(substeps), "clamp_kv": kv, "normal": nm,
-            "clamp_soft": _soft_width(kv, clamp_soft), "grad_decay": float(grad_decay)}
+            "clamp_soft": _soft_width(kv, clamp_soft), "grad_decay": float(grad_decay),
+            "compact_tape": bool(compact_tape)}
     if not math.isfinite(opts["grad_decay"]):
         raise _fail(f"grad_decay must be finite, got {grad_decay}", ValueError)
     state = (qpos, qvel, warm, ctrl, friction, com)

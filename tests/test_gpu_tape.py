@@ -12,10 +12,13 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 # record layout in float32 words (nablaengine_b200/csrc/nb_g1_step.cuh, T_*): substep input qpos, qvel, the Newton
-# solution a*, a_adv, the factors' inverse diagonals, then the packed lower-triangular factors L_H and L_Q
-T_QPOS, T_QVEL, T_ASTAR, T_AADV, T_DINVH, T_DINVQ, T_LH = 0, 36, 71, 106, 141, 176, 211
+# solution a*, a_adv, L_H's inverse diagonal and packed lower triangle, the contact table, zones, clamp masks, header
+# and flags (the compact record ends there), then L_Q's inverse diagonal and its pattern entries
+T_QPOS, T_QVEL, T_ASTAR, T_AADV, T_DINVH, T_LH = 0, 36, 71, 106, 141, 176
 NQ, NV, NU, NTRI = 36, 35, 29, 630
-T_LQ = T_LH + NTRI
+REC_COMPACT = 848
+T_DINVQ = REC_COMPACT
+T_LQ = T_DINVQ + NV
 # L_Q is stored in tree-block order (legs, arms, waist, root: nb_g1_step.cuh tb_dof): position p holds dof TB_DOF[p],
 # and only the entries of its pattern (p in q's chain or an ancestor chain of it), in packed-triangle order
 TB_DOF = list(range(6, 18)) + list(range(21, 35)) + [18, 19, 20] + list(range(6))
@@ -35,14 +38,14 @@ def _cuda():
     return torch
 
 
-def _forward_with_tape(s, nsub=4, iterations=10):
-    """Outputs and the (B, nsub, REC_WORDS) tape of nb_g1_forward called through the C ABI on a tape buffer
-    pre-filled with the sentinel word."""
+def _forward_with_tape(s, nsub=4, iterations=10, compact=False):
+    """Outputs and the (B, nsub, record words) tape of nb_g1_forward_ex called through the C ABI on a tape buffer
+    pre-filled with the sentinel word (full or compact records)."""
     torch = _cuda()
     from nablaengine_b200 import capi, torch_ffi
     torch_ffi.init(0)
     lib = capi.load()
-    rec = int(capi.sizes()[6])
+    rec = capi.tape_words(compact)
     t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda() for k in KEYS]
     B = t[0].shape[0]
     q1, v1, w1 = torch.empty((B, NQ), device="cuda"), torch.empty((B, NV), device="cuda"), torch.empty(
@@ -50,8 +53,8 @@ def _forward_with_tape(s, nsub=4, iterations=10):
     info = torch.empty((B, 4), dtype=torch.int32, device="cuda")
     tape = torch.full((B, nsub * rec), int(SENTINEL.view(np.int32)), dtype=torch.int32, device="cuda")
     p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
-    rc = lib.nb_g1_forward(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), B, *map(p, t), iterations, nsub,
-                           p(q1), p(v1), p(w1), p(info), None, p(tape), None)
+    rc = lib.nb_g1_forward_ex(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), B, *map(p, t), iterations,
+                              nsub, p(q1), p(v1), p(w1), p(info), None, p(tape), None, rec)
     torch.cuda.synchronize()
     assert rc == 0, rc
     raw = tape.cpu().numpy().reshape(B, nsub, rec)
@@ -133,3 +136,56 @@ def test_hessian_factor_matches_the_oracle_hessian(taped):
         e = np.linalg.norm(L @ L.transpose(0, 2, 1) - H, axis=(1, 2)) / np.linalg.norm(H, axis=(1, 2))
         assert np.median(e) < 1e-5 and np.quantile(e, 0.9) < 1e-4, (k, np.median(e), np.quantile(e, 0.9))
         assert nrow.max() > 0
+
+
+# ---- the compact tape: records without L_Q, which the adjoint and the Jacobian rebuild from the replayed poses ------
+def test_compact_records_are_the_full_records_first_words(taped):
+    """Every word of a compact record is written, the outputs are bitwise those of the full tape, and the compact
+    record is the full record's first REC_COMPACT words bit for bit."""
+    from nablaengine_b200 import capi
+    s, outs, raw, _ = taped
+    assert capi.tape_words(True) == REC_COMPACT and capi.tape_words(False) == raw.shape[2]
+    outs_c, raw_c, _ = _forward_with_tape(s, compact=True)
+    assert raw_c.shape[2] == REC_COMPACT
+    assert not np.any(raw_c.view(np.uint32) == SENTINEL)
+    for a, b in zip(outs, outs_c):
+        assert np.array_equal(a, b)
+    assert np.array_equal(raw[:, :, :REC_COMPACT], raw_c)
+
+
+def test_compact_tape_adjoint_and_jacobian_match_the_full_tape():
+    """backward and jacobian on compact records (L_Q rebuilt from the replayed poses) equal those on full records
+    within float32 rounding, in the exact and the default gradient modes; a record size other than the two is refused."""
+    torch = _cuda()
+    from nablaengine_b200 import capi, synthetic, torch_ffi
+    s = synthetic.config_states("vjp", B=96, seed_offset=3)
+    s["qpos"][:24, 2] -= 0.1
+    t = [torch.from_numpy(np.ascontiguousarray(s[k], np.float32)).cuda() for k in KEYS]
+    full = torch_ffi.forward(*t, tape=True)
+    comp = torch_ffi.forward(*t, tape="compact")
+    assert comp[4].shape[1] == 4 * REC_COMPACT and full[4].shape[1] == 4 * capi.tape_words(False)
+    for a, b in zip(full[:4], comp[:4]):
+        assert torch.equal(a, b)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    cq = torch.randn(96, NQ, device="cuda", generator=g)
+    cv = torch.randn(96, NV, device="cuda", generator=g)
+
+    def rel(a, b):
+        return float(((a.double() - b.double()).norm(dim=-1) / b.double().norm(dim=-1).clamp_min(1e-9)).max())
+
+    for kv, nm in ((1, 0), (0, 3)):
+        rf = torch_ffi.backward(full[4], t[4], t[5], cq, cv, clamp_kv=kv, normal=nm)
+        rc = torch_ffi.backward(comp[4], t[4], t[5], cq, cv, clamp_kv=kv, normal=nm)
+        errs = [rel(a, b) for a, b in zip(rc[:3], rf[:3])]
+        print("backward", kv, nm, errs)
+        assert max(errs) < 1e-3 and torch.equal(rc[3], rf[3]), errs
+    Jf = torch_ffi.jacobian(full[4], t[4], t[5])[0]
+    Jc = torch_ffi.jacobian(comp[4], t[4], t[5])[0]
+    err = (Jc.double() - Jf.double()).norm(dim=2) / Jf.double().norm(dim=2).clamp_min(1e-9)
+    print("jacobian rows: median", float(err.median()), "max", float(err.max()))
+    assert float(err.median()) < 1e-5 and float(err.max()) < 1e-2
+    lib = capi.load()
+    p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    bad = lib.nb_g1_jacobian_ex(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), 96, 4, p(full[4]), p(t[4]),
+                                p(t[5]), p(Jf), p(rc[3]), None, ctypes.c_float(0.0), 1, 0, 1000)
+    assert bad != 0

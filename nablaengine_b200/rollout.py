@@ -82,6 +82,7 @@ def main(argv=None):
     ap.add_argument("--worlds", type=int, default=WORLDS_DEFAULT, help="worlds per GPU")
     ap.add_argument("--steps", type=int, default=T_DEFAULT, help="control steps T")
     ap.add_argument("--repeats", type=int, default=5)
+    ap.add_argument("--compact-tape", action="store_true", help="keep compact tapes (no L_Q: 31 %% less memory)")
     a = ap.parse_args(argv)
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
@@ -92,8 +93,8 @@ def main(argv=None):
     torch_ffi.init(local)
     inp = rollout_inputs(a.worlds, a.steps, rank, dev)
     inp["worlds_total"] = a.worlds * world
-    bptt(inp)  # warm-up (allocator, first launches)
-    reduce_stats(*bptt(inp))
+    bptt(inp, compact_tape=a.compact_tape)  # warm-up (allocator, first launches)
+    reduce_stats(*bptt(inp, compact_tape=a.compact_tape))
     times, red, vec = [], [], None
     for _ in range(a.repeats):
         if world > 1:
@@ -101,7 +102,7 @@ def main(argv=None):
         torch.cuda.synchronize()
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        loss, g = bptt(inp)
+        loss, g = bptt(inp, compact_tape=a.compact_tape)
         e1.record()
         vec = reduce_stats(loss, g)
         e2.record()

@@ -121,8 +121,15 @@ def _p(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+_REC_WORDS = {}
+
+
 def _rec_words(compact=False):
-    return capi.tape_words(compact)
+    """Words per world and substep of a tape record (full or compact), asked of the library once."""
+    key = bool(compact)
+    if key not in _REC_WORDS:
+        _REC_WORDS[key] = capi.tape_words(key)
+    return _REC_WORDS[key]
 
 
 def _tape_words(tape, nsub):

@@ -37,6 +37,25 @@ def test_forward_rejects_bad_arguments_without_launching():
     assert lib.nb_g1_forward(nul, 0, *[nul] * 6, 10, 4, *[nul] * 7) == 0  # no worlds: a no-op
 
 
+def test_tape_record_sizes_and_the_ex_entries_reject_other_sizes():
+    """The full and the compact record sizes; the _ex entries refuse any other record size (cudaErrorInvalidValue)
+    before any launch, and the plain entries are the _ex ones with full records."""
+    lib = capi.load()
+    full, compact = capi.tape_words(False), capi.tape_words(True)
+    assert (full, compact) == (capi.sizes()[6], 848) and capi.sizes()[7] == 4
+    assert torch_ffi.tape_bytes(4096, compact=True) * full == torch_ffi.tape_bytes(4096) * compact
+    nul, f0 = ctypes.c_void_p(0), ctypes.c_float(0.0)
+    for words in (0, -1, full - 4, compact + 4, 2 * full):
+        assert lib.nb_g1_forward_ex(nul, 1, *[nul] * 6, 10, 4, *[nul] * 7, words) == 1
+        assert lib.nb_g1_adjoint_ex(nul, 1, 4, *[nul] * 10, f0, 1, 0, words) == 1
+        assert lib.nb_g1_jacobian_ex(nul, 1, 4, *[nul] * 6, f0, 1, 0, words) == 1
+        assert lib.nb_g1_diag_forward_ex(nul, nul, 1, 4, 10, nul, nul, words) == 1
+    for words in (full, compact):  # no worlds: a no-op
+        assert lib.nb_g1_forward_ex(nul, 0, *[nul] * 6, 10, 4, *[nul] * 7, words) == 0
+        assert lib.nb_g1_adjoint_ex(nul, 0, 4, *[nul] * 10, f0, 1, 0, words) == 0
+        assert lib.nb_g1_jacobian_ex(nul, 0, 4, *[nul] * 6, f0, 1, 0, words) == 0
+
+
 def test_small_entries_reject_bad_arguments_without_launching():
     lib = capi.load()
     nul = ctypes.c_void_p(0)

@@ -76,6 +76,38 @@ def test_forward_noalloc_allocates_no_device_memory():
     assert torch.cuda.memory_reserved() == reserved0
 
 
+def test_forward_noalloc_in_a_cuda_graph():
+    """After a first call on the device (the buffer's address lookup), the call captures into a CUDA graph; replays
+    on new inputs written into the captured buffers equal nb_g1_forward on those inputs bit for bit (the graph holds
+    the library's buffer, not caller memory, as the world order's home)."""
+    torch, lib, rec = _setup()
+    from nablaengine_b200 import synthetic
+    B = 1000
+    s0 = synthetic.config_states("forward", B=B)
+    t = [torch.from_numpy(np.ascontiguousarray(s0[k], np.float32)).cuda() for k in KEYS]
+    out = [torch.empty((B, 36), device="cuda"), torch.empty((B, 35), device="cuda"),
+           torch.empty((B, 35), device="cuda"), torch.empty((B, 4), dtype=torch.int32, device="cuda")]
+    p = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    call = lambda: lib.nb_g1_forward_noalloc(  # noqa: E731
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), B, *map(p, t), 10, 4, *map(p, out), None, None)
+    assert call() == 0
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        assert call() == 0
+    for seed in (4, 5):
+        s = synthetic.config_states("vjp", B=B, seed_offset=seed)
+        for dst, k in zip(t, KEYS):
+            dst.copy_(torch.from_numpy(np.ascontiguousarray(s[k], np.float32)))
+        graph.replay()
+        torch.cuda.synchronize()
+        got = [x.cpu().numpy().view(np.uint32) for x in out]
+        want = _run(torch, lib, rec, s, noalloc=False)
+        for name, a, b in zip(("qpos'", "qvel'", "warm'", "info"), got, want[:4]):
+            assert np.array_equal(a, b), (seed, name)
+    del graph
+
+
 def test_forward_noalloc_rejects_more_worlds_than_its_buffer():
     torch, lib, _ = _setup()
     nul = ctypes.c_void_p(0)

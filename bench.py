@@ -467,7 +467,9 @@ def main():
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
+    h0 = time.perf_counter()
     e2e_run(a.steps)
+    e2e_host_ms = (time.perf_counter() - h0) * 1e3 / a.steps  # the host's time to enqueue a step (not the metric)
     e1.record(st)
     torch.cuda.synchronize()
     e2e_total = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
@@ -514,7 +516,8 @@ def main():
                      "hbm_achieved_gbs": (B * (556 + 440) / (ms / 1e3)) / 1e9,
                      "hbm_peak_gbs": peaks.get("hbm_gbs")},
         "clocks": clocks,
-        "e2e": {"value": e2e_value, "unit": "world-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": e2e_value, "unit": "world-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_s * 1e3 / a.steps, "host_enqueue_ms_per_step": e2e_host_ms},
         # k_order, k_forward (+ the diagnostics counters and the last-forward record)
         "gpu_launches": a.steps * (4 if torch_ffi.diagnostics_enabled() else 2),
         "fwd_grad": {"metric": "world-steps/sec fwd+grad at B=4096/GPU (BASELINE configuration 3: loss sum(qvel'^2), "

@@ -219,9 +219,12 @@ def _launch(dev, entry, *args):
     """Call the library entry on torch's current stream of device dev; a nonzero CUDA error raises."""
     import torch
     lib = capi.load()
-    with torch.cuda.device(dev):
-        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    if torch.cuda.current_device() == dev:  # (the common case: no device switch around the call)
         rc = getattr(lib, entry)(stream, *args)
+    else:
+        with torch.cuda.device(dev):
+            rc = getattr(lib, entry)(stream, *args)
     if rc:
         raise _fail(f"{entry} failed (CUDA error {rc})", RuntimeError)
 
@@ -467,6 +470,13 @@ def _autograd_function(name):
     return _FUNCTIONS[name]
 
 
+def _tracing():
+    """True while torch.compile traces: the library calls then go through their custom ops (opaque graph nodes);
+    eager calls go straight to the implementation (the same launches, without the dispatcher's overhead)."""
+    import torch
+    return torch.compiler.is_compiling()
+
+
 def _differentiating(*xs):
     import torch
     return torch.is_grad_enabled() and any(isinstance(x, torch.Tensor) and x.requires_grad for x in xs)
@@ -482,8 +492,8 @@ def forward(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, sub
     factor of M + h kv, which backward and jacobian rebuild: 31 % less tape); backward and jacobian take either."""
     if tape not in (False, True, "compact"):
         raise _fail(f"tape must be False, True or 'compact', got {tape!r}", ValueError)
-    r = custom_ops()["forward"](qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape),
-                                tape == "compact")
+    args = (qpos, qvel, warm, ctrl, friction, com, int(iterations), int(substeps), bool(tape), tape == "compact")
+    r = custom_ops()["forward"](*args) if _tracing() else _forward_impl(*args)
     out = tuple(r) if tape else tuple(r[:4])
     if kinematics:
         out += tuple(custom_ops()["kinematics"](r[0], r[1], com))
@@ -541,7 +551,8 @@ def step(qpos, qvel, warm, ctrl, friction, com, *, iterations=ITERATIONS, subste
     if _differentiating(*state):
         q1, v1, w1 = _autograd_function("step").apply(*state, opts)
     else:
-        q1, v1, w1 = custom_ops()["forward"](*state, opts["iterations"], opts["substeps"], False)[:3]
+        args = state + (opts["iterations"], opts["substeps"], False)
+        q1, v1, w1 = (custom_ops()["forward"](*args) if _tracing() else _forward_impl(*args))[:3]
     if kinematics:
         return (q1, v1, w1) + tuple(globals()["kinematics"](q1, v1, com))
     return q1, v1, w1

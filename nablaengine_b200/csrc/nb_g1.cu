@@ -43,7 +43,8 @@ __global__ void __launch_bounds__(WPB * 32) k_forward(int nw, const float* __res
                                                       int tape_words) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int slot = blockIdx.x * WPB + warp;  // the warp's place in the world order (k_order), or its world index
+  const int slot = blockIdx.x * (int)(blockDim.x >> 5) + warp;  // the warp's place in the world order (k_order),
+                                                                   // or its world index
 #if !NB_LOCKSTEP
   if (slot >= nw) return;  // whole warps leave; the block has no block-wide barrier
 #endif
@@ -658,19 +659,29 @@ static int launch_forward(cudaStream_t stream, int nw, const float* qpos, const 
   if (nw == 0) return 0;
   if (!qpos || !qvel || !warm || !ctrl || !friction || !com || !qpos_out || !qvel_out || !warm_out || !info)
     return (int)cudaErrorInvalidValue;
-  const int blocks = (nw + WPB - 1) / WPB;
+  // worlds per block: WPB, or when every world fits one wave of WPB per SM, the fewest that put a block on every SM
+  // (a block's time is its slowest world's, so smaller blocks on all SMs beat full blocks on a few); from two waves
+  // on, full blocks (measured: blocks of 14 spread evenly over two waves ran 1 % slower than 15)
+  int wpb = WPB;
+#if !defined(NB_PROFILE) && !defined(NB_FWD_NO_SPREAD)
+  {
+    const int sms = device_sms();
+    if (nw <= sms * WPB) wpb = std::max(1, (nw + sms - 1) / sms);
+  }
+#endif
+  const int blocks = (nw + wpb - 1) / wpb;
 #ifdef NB_PROFILE
   const size_t smem = g_prof_smem > SMEM ? g_prof_smem : SMEM;
   if (smem != SMEM) cudaFuncSetAttribute(k_forward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 #else
-  const size_t smem = SMEM;
+  const size_t smem = sizeof(World) * wpb;
 #endif
   if (order) {
     k_order<<<(nw + ORD_CHUNK - 1) / ORD_CHUNK * ORD_BLOCKS_PER_CHUNK, ORD_THREADS, 0, stream>>>(nw, qpos, order);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
   }
-  k_forward<<<blocks, WPB * 32, smem, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
+  k_forward<<<blocks, wpb * 32, smem, stream>>>(nw, qpos, qvel, warm, ctrl, friction, com, iterations, nsub, qpos_out,
                                                 qvel_out, warm_out, info, ocon, stats, tape, order, tape_words);
   return (int)cudaGetLastError();
 }

@@ -433,10 +433,12 @@ __device__ __forceinline__ void jac_rhs_solves(const JRec& R, float* x) {
     int qs, ce, js;
     tb_ranges(p, qs, ce, js);
     float v = JX(JO_SLOT, p);
+    int e = TRI(p + 1, p);  // L(q, p) for q = p + 1, p + 2, ...: TRI(q + 1, p) = TRI(q, p) + q + 1
 #pragma unroll 4
-    for (int q = p + 1; q < ce; q++) v -= R.LQ[TRI(q, p)] * JX(JO_SLOT, q);
+    for (int q = p + 1; q < ce; q++) { v -= R.LQ[e] * JX(JO_SLOT, q); e += q + 1; }
+    e = TRI(js, p);
 #pragma unroll 4
-    for (int q = js; q < NV; q++) v -= R.LQ[TRI(q, p)] * JX(JO_SLOT, q);
+    for (int q = js; q < NV; q++) { v -= R.LQ[e] * JX(JO_SLOT, q); e += q + 1; }
     JX(JO_SLOT, p) = v * R.dinvQ[p];
   }
   // abar* = abar_adv - h kv y; lambda with L_H (dof order)
@@ -458,8 +460,9 @@ __device__ __forceinline__ void jac_rhs_solves(const JRec& R, float* x) {
 #pragma unroll 1
   for (int i = NV - 1; i >= 0; i--) {
     float v = JX(JO_LAM, i);
+    int e = TRI(i + 1, i);
 #pragma unroll 4
-    for (int q = i + 1; q < NV; q++) v -= R.LH[TRI(q, i)] * JX(JO_LAM, q);
+    for (int q = i + 1; q < NV; q++) { v -= R.LH[e] * JX(JO_LAM, q); e += q + 1; }
     JX(JO_LAM, i) = v * R.dinvH[i];
   }
   // the limit rows and the actuators

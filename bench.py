@@ -92,8 +92,9 @@ class Clocks:
 
 
 # DRAM bytes (read + write) per world of one forward launch: ncu `dram__bytes_read.sum + dram__bytes_write.sum` of
-# k_forward on 2220 configuration-2 worlds with the world order (one wave; the capture command is in
-# profiles/k_forward.md), divided by the worlds; the inputs and outputs of the step, nothing re-read
+# k_forward on 2220 configuration-2 worlds with the world order (one wave, captured by `ncu --set full
+# --clock-control none -k regex:k_forward -s 2 -c 1 python bench.py --profile-case forward --worlds 2220`), divided by
+# the worlds; the inputs and outputs of the step, nothing re-read
 FORWARD_DRAM_BYTES_PER_WORLD = 702
 
 

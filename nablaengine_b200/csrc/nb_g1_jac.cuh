@@ -35,17 +35,25 @@ constexpr int JS = JNR + 2;   // the per-lane arrays' stride: the 70 right-hand 
 constexpr int JTHREADS = 32 * JWARPS;
 static_assert(JTHREADS >= MAXCON, "one thread per contact in the record's preparation");
 
-// per body (1 .. NB - 1), the same for every cotangent of the record
-struct JBody {
-  float cw[3], c[3];                 // the COM (world), its offset from the body origin
-  float I[6];                       // the inertia at the COM in the world frame: xx, yy, zz, xy, xz, yz
-  float m;
-  float FA[3], Iom[3], Ial[3];       // channel A: m ac, I om, I al
-  float om[3], alA[3], alB[3];       // the replayed angular velocity and both channels' angular accelerations
-  float FB[3], NBc[3];               // channel B: m ac, I al
-  float X[3], w[3], r[3];            // body origin, hinge axis (world), origin relative to the parent's
-  float SWA[6], SWB[6], SGL[6];      // subtree sums: both channels' own wrenches and G(lambda), at the world origin
+// per body (1 .. NB - 1), the same for every cotangent of the record. Every 3-vector sits in a 16-byte slot and every
+// 6-vector in two, so that the per-cotangent pass reads each with 128-bit broadcast loads (jv3, jv6).
+struct __align__(16) JBody {
+  float cw[4], c[4];                 // the COM (world), its offset from the body origin; c[3]: the mass
+  float I[8];                        // the inertia at the COM in the world frame: xx, yy, zz, xy, xz, yz
+  float FA[4], Iom[4], Ial[4];       // channel A: m ac, I om, I al
+  float om[4], alA[4], alB[4];       // the replayed angular velocity and both channels' angular accelerations
+  float FB[4], NBc[4];               // channel B: m ac, I al
+  float X[4], w[4], r[4];            // body origin, hinge axis (world), origin relative to the parent's
+  float SWA[8], SWB[8], SGL[8];      // subtree sums: both channels' own wrenches and G(lambda), at the world origin
 };
+__device__ __forceinline__ void jv3(const float* p, float* o) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  o[0] = v.x; o[1] = v.y; o[2] = v.z;
+}
+__device__ __forceinline__ void jv6(const float* p, float* o) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y;
+}
 // per contact: the 6-column matrices of its cotangent terms in dV (row-major 6 x 6)
 struct JCon {
   float Ga[36], P2[36], P1[36];     // G(a*) (on body 2; -G on body 1), the pose wrenches of body 2 and body 1
@@ -56,7 +64,7 @@ struct JCon {
 struct __align__(16) JRec {
   float LQ[NTRIP], LH[NTRIP];       // the tape's factors: L_Q (tree-block order, zeros off its pattern), L_H
   float dinvQ[NV + 1], dinvH[NV + 1];
-  float S6[NV][6];                  // each dof's motion vector (angular, linear at the world origin)
+  float S6[NV][8];                  // each dof's motion vector (angular, linear at the world origin; 2 slots)
   float vd[NV], ad[NV], xd[NV];     // qvel, a* and a* - a_adv of the record
   float dcq[NV], dcv[NV], dcu[NV];  // limit and actuator terms: tangent, velocity and ctrl cotangents per lambda_i
   float A1[9], A2[9];               // the root rotation's integrator: J_r(h w')' and R(h w') (row-major)
@@ -73,6 +81,7 @@ constexpr int JSLOT = 36, JRHS_ROWS = JO_SLOT + JSLOT;
 struct JPrep { AWorld s; AdjShared W; float M[NTRIP]; float Ic[NB][10]; };  // (M, Ic: a compact record's L_Q)
 static_assert(sizeof(JPrep) <= sizeof(float) * 2 * NV * JS, "the preparation's scratch fits lambda and y");
 static_assert(offsetof(JPrep, M) % 16 == 0 && offsetof(JRec, LQ) % 16 == 0, "written as float4 by adj_mass_factor");
+static_assert(offsetof(JRec, S6) % 16 == 0 && offsetof(JRec, body) % 16 == 0, "read as float4 (jv3, jv6)");
 struct __align__(16) JBlock {
   JRec R;
   union {
@@ -293,7 +302,7 @@ __device__ __forceinline__ void jac_prep_body(JRec& R, const AWorld& s, const Ad
     J.alA[k] = alA[k]; J.alB[k] = alB[k]; J.FB[k] = FB[k]; J.NBc[k] = NBc[k]; J.X[k] = X[k];
   }
   J.I[0] = I[0][0]; J.I[1] = I[1][1]; J.I[2] = I[2][2]; J.I[3] = I[0][1]; J.I[4] = I[0][2]; J.I[5] = I[1][2];
-  J.m = m;
+  J.c[3] = m;
   // the own wrenches at the origin (N + cw x F, F) of both channels; G(lambda) comes in step 4
   cross(cw, FA, t);
   for (int k = 0; k < 3; k++) { J.SWA[k] = NA[k] + t[k]; J.SWA[3 + k] = FA[k]; }
@@ -535,7 +544,9 @@ __device__ __forceinline__ void jac_path_motion(const JRec& R, const float* x, i
     const int d0 = a >= 2 ? a + 4 : 0, d1 = a >= 2 ? a + 5 : 6;
     for (int d = d0; d < d1; d++) {
       const float v = JX(o, d);
-      for (int k = 0; k < 6; k++) V[k] += R.S6[d][k] * v;
+      float s6[6];
+      jv6(R.S6[d], s6);
+      for (int k = 0; k < 6; k++) V[k] += s6[k] * v;
     }
   }
 }
@@ -553,7 +564,9 @@ __device__ __forceinline__ void jac_rel_motion(const JRec& R, const float* x, in
     const int d0 = e >= 2 ? e + 4 : 0, d1 = e >= 2 ? e + 5 : 6;
     for (int d = d0; d < d1; d++) {
       const float v = sg * JX(JO_LAM, d);
-      for (int k = 0; k < 6; k++) dV[k] += R.S6[d][k] * v;
+      float s6[6];
+      jv6(R.S6[d], s6);
+      for (int k = 0; k < 6; k++) dV[k] += s6[k] * v;
     }
     if (up2) { a = ldi(g1_body_parent + a); da--; } else { c = ldi(g1_body_parent + c); dc--; }
   }
@@ -570,60 +583,66 @@ __device__ __forceinline__ void sym_mul(const float* I, const float* v, float* o
 // its COM point (P)
 __device__ __forceinline__ void jac_own(const JBody& J, const float* VL, const float* VY, float* omb, float* alAb,
                                         float* aoAb, float* alBb, float* aoBb, float* rho, float* P) {
+  float cw[3], c[3], Iw[6], FA[3], Iom[3], Ial[3], om[3], alA[3], alB[3], FB[3], NBc[3];
+  jv3(J.cw, cw); jv6(J.I, Iw); jv3(J.FA, FA); jv3(J.Iom, Iom); jv3(J.Ial, Ial); jv3(J.om, om); jv3(J.alA, alA);
+  jv3(J.alB, alB); jv3(J.FB, FB); jv3(J.NBc, NBc);
+  const float4 c4 = *reinterpret_cast<const float4*>(J.c);
+  c[0] = c4.x; c[1] = c4.y; c[2] = c4.z;
+  const float m = c4.w;
   float t[3], cwb[3];
   {  // channel A: psi_A = -<W_b, V^lambda_b>, W_b = (N + cw x F, F), F = m (ao + al x c + om x (om x c))
     float Fb[3], Nb[3], Inb[3], n2[3], In2[3], acb[3], cb[3], z[3], zb[3];
-    cross(VL, J.cw, t);
+    cross(VL, cw, t);
     for (int k = 0; k < 3; k++) { Fb[k] = -(VL[3 + k] + t[k]); Nb[k] = -VL[k]; }
-    cross(VL, J.FA, cwb);
-    sym_mul(J.I, Nb, Inb);
+    cross(VL, FA, cwb);
+    sym_mul(Iw, Nb, Inb);
     for (int k = 0; k < 3; k++) alAb[k] = Inb[k];
-    cross(Nb, J.om, n2);
-    sym_mul(J.I, n2, In2);
-    cross(J.Iom, Nb, t);
+    cross(Nb, om, n2);
+    sym_mul(Iw, n2, In2);
+    cross(Iom, Nb, t);
     for (int k = 0; k < 3; k++) omb[k] = t[k] + In2[k];
-    cross(J.Ial, Nb, rho);
-    cross(Inb, J.alA, t);
+    cross(Ial, Nb, rho);
+    cross(Inb, alA, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
-    cross(J.Iom, n2, t);
+    cross(Iom, n2, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
-    cross(In2, J.om, t);
+    cross(In2, om, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
-    for (int k = 0; k < 3; k++) { acb[k] = J.m * Fb[k]; aoAb[k] = acb[k]; }
-    cross(J.c, acb, t);
+    for (int k = 0; k < 3; k++) { acb[k] = m * Fb[k]; aoAb[k] = acb[k]; }
+    cross(c, acb, t);
     for (int k = 0; k < 3; k++) alAb[k] += t[k];
-    cross(acb, J.alA, cb);
-    cross(J.om, J.c, z);
-    cross(acb, J.om, zb);
+    cross(acb, alA, cb);
+    cross(om, c, z);
+    cross(acb, om, zb);
     cross(z, acb, t);
     for (int k = 0; k < 3; k++) omb[k] += t[k];
-    cross(J.c, zb, t);
+    cross(c, zb, t);
     for (int k = 0; k < 3; k++) omb[k] += t[k];
-    cross(zb, J.om, t);
+    cross(zb, om, t);
     for (int k = 0; k < 3; k++) cb[k] += t[k];
-    cross(J.c, cb, t);
+    cross(c, cb, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
   }
   {  // channel B: weight +1, om = 0
     float Fb[3], Inb[3], acb[3], cb[3];
-    cross(VY, J.cw, t);
+    cross(VY, cw, t);
     for (int k = 0; k < 3; k++) Fb[k] = VY[3 + k] + t[k];
-    cross(J.FB, VY, t);
+    cross(FB, VY, t);
     for (int k = 0; k < 3; k++) cwb[k] += t[k];
-    sym_mul(J.I, VY, Inb);
+    sym_mul(Iw, VY, Inb);
     for (int k = 0; k < 3; k++) alBb[k] = Inb[k];
-    cross(J.NBc, VY, t);
+    cross(NBc, VY, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
-    cross(Inb, J.alB, t);
+    cross(Inb, alB, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
-    for (int k = 0; k < 3; k++) { acb[k] = J.m * Fb[k]; aoBb[k] = acb[k]; }
-    cross(J.c, acb, t);
+    for (int k = 0; k < 3; k++) { acb[k] = m * Fb[k]; aoBb[k] = acb[k]; }
+    cross(c, acb, t);
     for (int k = 0; k < 3; k++) alBb[k] += t[k];
-    cross(acb, J.alB, cb);
-    cross(J.c, cb, t);
+    cross(acb, alB, cb);
+    cross(c, cb, t);
     for (int k = 0; k < 3; k++) rho[k] += t[k];
   }
-  cross(J.cw, cwb, t);  // the COM point's cotangent: a force at cw
+  cross(cw, cwb, t);  // the COM point's cotangent: a force at cw
   for (int k = 0; k < 3; k++) { P[k] = t[k]; P[3 + k] = cwb[k]; }
 }
 
@@ -647,11 +666,15 @@ __device__ __forceinline__ void jac_rhs_sweep(const JRec& R, float* x) {
 #pragma unroll 1
   for (int b = NB - 1; b >= 1; b--) {
     const JBody& J = R.body[b];
+    float Xb[3];
+    jv3(J.X, Xb);
     const bool carried = b + 1 < NB && ldi(g1_body_parent + b + 1) == b;  // hv is the child b + 1's hand-over
     if (carried) {
       const int dc = b + 5;  // the child's hinge
       const float xl = JX(JO_LAM, dc), xy = JX(JO_Y, dc);
-      for (int k = 0; k < 6; k++) { VL[k] -= R.S6[dc][k] * xl; VY[k] -= R.S6[dc][k] * xy; }
+      float s6[6];
+      jv6(R.S6[dc], s6);
+      for (int k = 0; k < 6; k++) { VL[k] -= s6[k] * xl; VY[k] -= s6[k] * xy; }
     } else {
       jac_path_motion(R, x, JO_LAM, b, VL);
       jac_path_motion(R, x, JO_Y, b, VY);
@@ -679,68 +702,71 @@ __device__ __forceinline__ void jac_rhs_sweep(const JRec& R, float* x) {
         P[r] += pw;
       }
     }
-    if (carried) jac_inflow(hv, J.X, omb, alAb, aoAb, alBb, aoBb, P, SGa, SGv, SP);
+    if (carried) jac_inflow(hv, Xb, omb, alAb, aoAb, alBb, aoBb, P, SGa, SGv, SP);
     if (parked == b) {
       float sv[JSLOT];
       for (int k = 0; k < JSLOT; k++) sv[k] = JX(JO_SLOT, k);
-      jac_inflow(sv, J.X, omb, alAb, aoAb, alBb, aoBb, P, SGa, SGv, SP);
+      jac_inflow(sv, Xb, omb, alAb, aoAb, alBb, aoBb, P, SGa, SGv, SP);
       parked = -1;
     }
     float t[3];
     if (b >= 2) {
       const int d = b + 4, p = ldi(g1_body_parent + b);
       const JBody& Pp = R.body[p];
+      float wj[3], rj[3], pom[3], palA[3], palB[3];
+      jv3(J.w, wj); jv3(J.r, rj); jv3(Pp.om, pom); jv3(Pp.alA, palA); jv3(Pp.alB, palB);
       const float vd = R.vd[d], ad = R.ad[d], xd = R.xd[d];
       float wb[3], z[3], zb[3], rb[3], aw[3], wv[3];
       // channel A: om_b = om_p + w vd; al_b = al_p + om_p x (w vd) + w ad; ao_b = ao_p + al_p x r + om_p x (om_p x r)
       for (int k = 0; k < 3; k++) {
         hv[k] = omb[k]; hv[3 + k] = alAb[k]; hv[6 + k] = aoAb[k];
         wb[k] = vd * omb[k] + ad * alAb[k];
-        wv[k] = J.w[k] * vd;
+        wv[k] = wj[k] * vd;
       }
-      float vbar = dot3(J.w, omb);
+      float vbar = dot3(wj, omb);
       cross(wv, alAb, t);
       for (int k = 0; k < 3; k++) hv[k] += t[k];
-      cross(alAb, Pp.om, aw);
+      cross(alAb, pom, aw);
       for (int k = 0; k < 3; k++) wb[k] += vd * aw[k];
-      vbar += dot3(J.w, aw);
-      cross(J.r, aoAb, t);
+      vbar += dot3(wj, aw);
+      cross(rj, aoAb, t);
       for (int k = 0; k < 3; k++) hv[3 + k] += t[k];
-      cross(Pp.om, J.r, z);
-      cross(aoAb, Pp.om, zb);
+      cross(pom, rj, z);
+      cross(aoAb, pom, zb);
       cross(z, aoAb, t);
       for (int k = 0; k < 3; k++) hv[k] += t[k];
-      cross(J.r, zb, t);
+      cross(rj, zb, t);
       for (int k = 0; k < 3; k++) hv[k] += t[k];
-      cross(aoAb, Pp.alA, rb);
-      cross(zb, Pp.om, t);
+      cross(aoAb, palA, rb);
+      cross(zb, pom, t);
       for (int k = 0; k < 3; k++) rb[k] += t[k];
       // channel B: al_b = al_p + w xd; ao_b = ao_p + al_p x r
       for (int k = 0; k < 3; k++) { hv[9 + k] = alBb[k]; hv[12 + k] = aoBb[k]; wb[k] += xd * alBb[k]; }
-      cross(J.r, aoBb, t);
+      cross(rj, aoBb, t);
       for (int k = 0; k < 3; k++) hv[9 + k] += t[k];
-      cross(aoBb, Pp.alB, t);
+      cross(aoBb, palB, t);
       for (int k = 0; k < 3; k++) rb[k] += t[k];
       // r = X - Xp: force rbar at X (this body), -rbar at Xp (the parent)
-      cross(J.X, rb, t);
+      cross(Xb, rb, t);
       for (int k = 0; k < 3; k++) { P[k] += t[k]; P[3 + k] += rb[k]; hv[15 + k] = rb[k]; }
       // the dof's motion vector s = (w, X x w): sbar = -lam W_A + y W_B + lam G_l + a G_a + v G_v (subtree sums)
       const float lam = JX(JO_LAM, d), yd = JX(JO_Y, d);
-      float sb[6];
+      float sb[6], swa[6], swb[6], sgl[6];
+      jv6(J.SWA, swa); jv6(J.SWB, swb); jv6(J.SGL, sgl);
       for (int k = 0; k < 6; k++)
-        sb[k] = -lam * J.SWA[k] + yd * J.SWB[k] + lam * J.SGL[k] + ad * SGa[k] + vd * SGv[k];
-      JX(JO_V, d) += vbar + wrench_dot(SGv, J.w, J.X);
-      cross(sb + 3, J.X, t);
+        sb[k] = -lam * swa[k] + yd * swb[k] + lam * sgl[k] + ad * SGa[k] + vd * SGv[k];
+      JX(JO_V, d) += vbar + wrench_dot(SGv, wj, Xb);
+      cross(sb + 3, Xb, t);
       for (int k = 0; k < 3; k++) wb[k] += sb[k] + t[k];
       float xf[3];
-      cross(J.w, sb + 3, xf);
-      cross(J.X, xf, t);
+      cross(wj, sb + 3, xf);
+      cross(Xb, xf, t);
       for (int k = 0; k < 3; k++) { P[k] += t[k]; P[3 + k] += xf[k]; }
-      cross(J.w, wb, t);  // the axis rotates with the body
+      cross(wj, wb, t);  // the axis rotates with the body
       for (int k = 0; k < 3; k++) rho[k] += t[k];
       for (int k = 0; k < 3; k++) P[k] += rho[k];
       for (int k = 0; k < 6; k++) SP[k] += P[k];
-      JX(JO_Q, d) += wrench_dot(SP, J.w, J.X);
+      JX(JO_Q, d) += wrench_dot(SP, wj, Xb);
       for (int k = 0; k < 6; k++) { hv[18 + k] = SGa[k]; hv[24 + k] = SGv[k]; hv[30 + k] = SP[k]; }
       if (p != b - 1) {  // the parent is not visited next: park the hand-over (added to one parked for p)
         const bool add = parked == p;
@@ -755,21 +781,23 @@ __device__ __forceinline__ void jac_rhs_sweep(const JRec& R, float* x) {
         for (int k = 0; k < 3; k++)
           wbr[i][k] = R.vd[3 + i] * omb[k] + R.ad[3 + i] * alAb[k] + R.xd[3 + i] * alBb[k];
       }
+      float swa[6], swb[6], sgl[6];
+      jv6(J.SWA, swa); jv6(J.SWB, swb); jv6(J.SGL, sgl);
       for (int i = 0; i < 6; i++) {
         const float lam = JX(JO_LAM, i), yd = JX(JO_Y, i);
         float sb[6];
         for (int k = 0; k < 6; k++)
-          sb[k] = -lam * J.SWA[k] + yd * J.SWB[k] + lam * J.SGL[k] + R.ad[i] * SGa[k] + R.vd[i] * SGv[k];
+          sb[k] = -lam * swa[k] + yd * swb[k] + lam * sgl[k] + R.ad[i] * SGa[k] + R.vd[i] * SGv[k];
         if (i < 3) {
           JX(JO_V, i) += SGv[3 + i];  // s = (0, e_i)
         } else {
           const float* w = R.S6[i];
-          JX(JO_V, i) += wrench_dot(SGv, w, J.X);
-          cross(sb + 3, J.X, t);
+          JX(JO_V, i) += wrench_dot(SGv, w, Xb);
+          cross(sb + 3, Xb, t);
           for (int k = 0; k < 3; k++) wbr[i - 3][k] += sb[k] + t[k];
           float xf[3];
           cross(w, sb + 3, xf);
-          cross(J.X, xf, t);
+          cross(Xb, xf, t);
           for (int k = 0; k < 3; k++) { P[k] += t[k]; P[3 + k] += xf[k]; }
         }
       }
@@ -780,7 +808,7 @@ __device__ __forceinline__ void jac_rhs_sweep(const JRec& R, float* x) {
       for (int k = 0; k < 3; k++) P[k] += rho[k];
       for (int k = 0; k < 6; k++) SP[k] += P[k];
       for (int i = 0; i < 3; i++) JX(JO_Q, i) += SP[3 + i];
-      for (int i = 3; i < 6; i++) JX(JO_Q, i) += wrench_dot(SP, R.S6[i], J.X);
+      for (int i = 3; i < 6; i++) JX(JO_Q, i) += wrench_dot(SP, R.S6[i], Xb);
     }
   }
 }
